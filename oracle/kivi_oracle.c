@@ -1,0 +1,462 @@
+/*
+ * kivi_oracle.c -- CPU restatement of the reference's 4-bit KV-cache path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker the CUDA kernels are
+ * compared against; it is never linked into, loaded by, or called from the
+ * product library.  Only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline / reference arm use it.
+ *
+ * Every function names the reference code it restates (paths are relative to
+ * the a1exxd0/poolside-hackathon tree).  Parity of this restatement with the
+ * reference itself is pinned by tests/golden/ (fixtures produced by running the
+ * reference's own kv_quant.py / scripts on CPU; see tests/golden/make_golden.py).
+ *
+ * Floating-point contract (compile with -O2 -ffp-contract=off, never
+ * -ffast-math): every operation below is one IEEE fp32 operation in the same
+ * order torch's CPU kernels perform it, so results are bit-identical.
+ *   - kv_quant.py:247-266 `_calibrate`:  scale = absmax/qmax, or for 'mse'
+ *     scale_a = (alpha_a*absmax)/qmax, err_a = mean((x - q(x/s)*s)**2),
+ *     first argmin over a.
+ *   - the 16-element `mean` is reduced by torch's CPU vector kernel as
+ *     v[j] = e[j] + e[j+8] (j < 8), then ((v0+v1)+v2)+...+v7, then /16
+ *     (measured against torch 2.11 CPU; pinned by the golden fixtures).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+#include <stdlib.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define BLK 16
+#define PACKB 8
+
+enum { FMT_INT4 = 0, FMT_INT3 = 1, FMT_NVFP4 = 2 };
+enum { CAL_ABSMAX = 0, CAL_MSE = 1 };
+enum { LAYOUT_HEADDIM = 0, LAYOUT_CHANNEL = 1 };
+
+/* kv_quant.py:207-208 `_E2M1_LEVELS`, `_E2M1_BOUNDS` */
+static const float E2M1_LEVELS[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+static const float E2M1_BOUNDS[7] = {0.25f, 0.75f, 1.25f, 1.75f, 2.5f, 3.5f, 5.0f};
+
+/* kv_quant.py:228 `_FORMATS` qmax column */
+static float qmax_of(int fmt) {
+    return fmt == FMT_INT4 ? 7.0f : (fmt == FMT_INT3 ? 3.0f : 6.0f);
+}
+
+/* kv_quant.py:220-225 `_q_e2m1`: bucketize(|y|, bounds, right=False) gives the
+ * number of bounds strictly below |y| (ties go to the lower level); result is
+ * sign(y) * level.  Returns the magnitude index; *neg = (y < 0). */
+static int e2m1_index(float y, int *neg) {
+    float a = fabsf(y);
+    int idx = 0;
+    for (int i = 0; i < 7; ++i) idx += (E2M1_BOUNDS[i] < a);
+    *neg = (y < 0.0f);
+    return idx;
+}
+
+/* kv_quant.py:211-225: round a scale-normalised value onto the format grid. */
+static float q_grid(float y, int fmt) {
+    if (fmt == FMT_NVFP4) {
+        int neg, idx = e2m1_index(y, &neg);
+        float l = E2M1_LEVELS[idx];
+        if (y > 0.0f) return l;
+        if (y < 0.0f) return -l;
+        return 0.0f;           /* torch.sign(+-0) * level == +0 */
+    }
+    float r = rintf(y), qm = qmax_of(fmt);      /* .round().clamp(-qmax, qmax) */
+    if (r > qm) return qm;
+    if (r < -qm) return -qm;
+    return r;
+}
+
+/* torch CPU order for mean over a contiguous 16-element row (see header). */
+static float mean16(const float e[BLK]) {
+    float v[8];
+    for (int j = 0; j < 8; ++j) v[j] = e[j] + e[j + 8];
+    float s = v[0];
+    for (int j = 1; j < 8; ++j) s = s + v[j];
+    return s / 16.0f;
+}
+
+static float absmax16(const float x[BLK]) {
+    float m = 0.0f;
+    for (int i = 0; i < BLK; ++i) {
+        float a = fabsf(x[i]);
+        if (a > m) m = a;
+    }
+    return m < 1e-9f ? 1e-9f : m;   /* .clamp_min(1e-9) */
+}
+
+/* kv_quant.py:247-266 `_calibrate` for one 16-element block. */
+float orc_calibrate_block(const float *x, int fmt, int calib,
+                          const float *alphas, int n_alphas) {
+    float qmax = qmax_of(fmt);
+    float amax = absmax16(x);
+    if (calib == CAL_ABSMAX) return amax / qmax;
+    float best = INFINITY, bs = 0.0f;
+    for (int a = 0; a < n_alphas; ++a) {
+        float s = (alphas[a] * amax) / qmax;
+        float e[BLK];
+        for (int i = 0; i < BLK; ++i) {
+            float q = q_grid(x[i] / s, fmt);
+            float d = x[i] - q * s;
+            e[i] = d * d;
+        }
+        float err = mean16(e);
+        if (err < best) { best = err; bs = s; }
+    }
+    return bs;
+}
+
+/* Gather one block of [H, S, D] x under a layout (kv_quant.py:232-244). */
+static void gather_block(const float *x, int S, int D, int layout, int h,
+                         int i0, int i1, float out[BLK]) {
+    /* headdim: (token i0, dblock i1); channel: (channel i0, page i1) */
+    if (layout == LAYOUT_HEADDIM) {
+        const float *row = x + ((size_t)h * S + i0) * D + (size_t)i1 * BLK;
+        for (int c = 0; c < BLK; ++c) out[c] = row[c];
+    } else {
+        for (int j = 0; j < BLK; ++j)
+            out[j] = x[((size_t)h * S + (size_t)i1 * BLK + j) * D + i0];
+    }
+}
+
+static void scatter_block(float *y, int S, int D, int layout, int h,
+                          int i0, int i1, const float v[BLK]) {
+    if (layout == LAYOUT_HEADDIM) {
+        float *row = y + ((size_t)h * S + i0) * D + (size_t)i1 * BLK;
+        for (int c = 0; c < BLK; ++c) row[c] = v[c];
+    } else {
+        for (int j = 0; j < BLK; ++j)
+            y[((size_t)h * S + (size_t)i1 * BLK + j) * D + i0] = v[j];
+    }
+}
+
+/* kv_quant.py:299-321 `roundtrip` (fp32 result before the final dtype cast).
+ * x, y: fp32 [H, S, D].  For 'channel' the trailing S % 16 tokens are copied. */
+void orc_roundtrip(const float *x, float *y, int H, int S, int D, int fmt,
+                   int layout, int calib, const float *alphas, int n_alphas) {
+    int n_full = (S / BLK) * BLK;
+    int nA = (layout == LAYOUT_HEADDIM) ? S : D;           /* i0 range */
+    int nB = (layout == LAYOUT_HEADDIM) ? D / BLK : n_full / BLK;
+    if (layout == LAYOUT_CHANNEL) {
+        for (int h = 0; h < H; ++h)
+            for (int t = n_full; t < S; ++t)
+                memcpy(y + ((size_t)h * S + t) * D, x + ((size_t)h * S + t) * D,
+                       sizeof(float) * D);
+    }
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int h = 0; h < H; ++h)
+        for (int a = 0; a < nA; ++a)
+            for (int b = 0; b < nB; ++b) {
+                float blk[BLK], out[BLK];
+                gather_block(x, S, D, layout, h, a, b, blk);
+                float s = orc_calibrate_block(blk, fmt, calib, alphas, n_alphas);
+                for (int i = 0; i < BLK; ++i) out[i] = q_grid(blk[i] / s, fmt) * s;
+                scatter_block(y, S, D, layout, h, a, b, out);
+            }
+}
+
+/* kv_quant.py:247-266 over n contiguous blocks: scales[n]. */
+void orc_calibrate(const float *blocks, long n, int fmt, int calib,
+                   const float *alphas, int n_alphas, float *scales) {
+    #pragma omp parallel for schedule(static)
+    for (long i = 0; i < n; ++i)
+        scales[i] = orc_calibrate_block(blocks + i * BLK, fmt, calib, alphas, n_alphas);
+}
+
+/* ------------------------------------------------------------------------- */
+/* small-float encoders: round-to-nearest-even onto a binary format with      */
+/* `mbits` mantissa bits, minimum normal exponent `emin` and bias `bias`.     */
+/* ------------------------------------------------------------------------- */
+static double round_fmt(double a, int mbits, int emin) {
+    if (a == 0.0) return 0.0;
+    int ex;
+    frexp(a, &ex);                 /* a = m * 2^ex, m in [0.5, 1) */
+    int E = ex - 1;
+    if (E < emin) E = emin;
+    double q = ldexp(1.0, E - mbits);
+    return nearbyint(a / q) * q;   /* exact scaling, RNE in default mode */
+}
+
+static uint32_t encode_fmt(double r, int mbits, int emin, int bias) {
+    if (r == 0.0) return 0;
+    int ex;
+    frexp(r, &ex);
+    int E = ex - 1;
+    if (E < emin) return (uint32_t)(r / ldexp(1.0, emin - mbits));   /* subnormal */
+    uint32_t mant = (uint32_t)((r / ldexp(1.0, E) - 1.0) * (double)(1 << mbits));
+    return ((uint32_t)(E + bias) << mbits) | mant;
+}
+
+/* fp32 -> IEEE binary16 bits, RNE, overflow to inf (torch .to(float16)). */
+uint16_t orc_f32_to_f16(float f) {
+    uint32_t sign = signbit(f) ? 0x8000u : 0u;
+    if (isnan(f)) return (uint16_t)(sign | 0x7e00u);
+    double a = fabs((double)f);
+    if (isinf(f)) return (uint16_t)(sign | 0x7c00u);
+    double r = round_fmt(a, 10, -14);
+    if (r > 65504.0) return (uint16_t)(sign | 0x7c00u);
+    return (uint16_t)(sign | encode_fmt(r, 10, -14, 15));
+}
+
+float orc_f16_to_f32(uint16_t h) {
+    int s = h >> 15, e = (h >> 10) & 0x1f, m = h & 0x3ff;
+    double v;
+    if (e == 0) v = ldexp((double)m, -24);
+    else if (e == 31) v = m ? NAN : INFINITY;
+    else v = ldexp(1.0 + m / 1024.0, e - 15);
+    return (float)(s ? -v : v);
+}
+
+/* fp32 -> float8 e4m3fn bits, RNE, saturating to +-448 (cvt.rn.satfinite). */
+uint8_t orc_f32_to_e4m3(float f) {
+    uint32_t sign = (f < 0.0f) ? 0x80u : 0u;
+    if (isnan(f)) return 0x7f;
+    double a = fabs((double)f);
+    double r = round_fmt(a, 3, -6);
+    if (r > 448.0) r = 448.0;
+    return (uint8_t)(sign | encode_fmt(r, 3, -6, 7));
+}
+
+float orc_e4m3_to_f32(uint8_t b) {
+    int s = b >> 7, e = (b >> 3) & 0xf, m = b & 7;
+    double v;
+    if (e == 0) v = ldexp((double)m, -9);
+    else if (e == 15 && m == 7) v = NAN;
+    else v = ldexp(1.0 + m / 8.0, e - 7);
+    return (float)(s ? -v : v);
+}
+
+/* ------------------------------------------------------------------------- */
+/* INT4-KIVI store (int4_kivi/triton_kernels.py:137-178, 216-254 and          */
+/* int4_kivi/cache.py:90-141): codes against the fp32 scale, scale stored     */
+/* as fp16, two's-complement nibbles, element 2j -> low nibble of byte j.     */
+/* ------------------------------------------------------------------------- */
+static void pack16(const int c[BLK], uint8_t out[PACKB]) {
+    for (int j = 0; j < PACKB; ++j)
+        out[j] = (uint8_t)((c[2 * j] & 0xf) | ((c[2 * j + 1] & 0xf) << 4));
+}
+
+/* k, v: fp32 [H, S, D].  Outputs follow int4_kivi/cache.py:52-63:
+ * k_packed [H, D, NP, 8], k_scale f16 [H, D, NP], v_packed [H, S, ND, 8],
+ * v_scale f16 [H, S, ND].  (The bf16 hot tail is a verbatim copy.) */
+void orc_store_int4(const float *k, const float *v, int H, int S, int D,
+                    int calib_k, int calib_v, const float *alphas, int n_alphas,
+                    uint8_t *k_packed, uint16_t *k_scale,
+                    uint8_t *v_packed, uint16_t *v_scale) {
+    int NP = S / BLK, ND = D / BLK;
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int h = 0; h < H; ++h)
+        for (int d = 0; d < D; ++d)
+            for (int p = 0; p < NP; ++p) {
+                float x[BLK]; int c[BLK];
+                gather_block(k, S, D, LAYOUT_CHANNEL, h, d, p, x);
+                float s = orc_calibrate_block(x, FMT_INT4, calib_k, alphas, n_alphas);
+                for (int j = 0; j < BLK; ++j) c[j] = (int)q_grid(x[j] / s, FMT_INT4);
+                size_t r = ((size_t)h * D + d) * NP + p;
+                pack16(c, k_packed + r * PACKB);
+                k_scale[r] = orc_f32_to_f16(s);
+            }
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int h = 0; h < H; ++h)
+        for (int t = 0; t < S; ++t)
+            for (int db = 0; db < ND; ++db) {
+                float x[BLK]; int c[BLK];
+                gather_block(v, S, D, LAYOUT_HEADDIM, h, t, db, x);
+                float s = orc_calibrate_block(x, FMT_INT4, calib_v, alphas, n_alphas);
+                for (int j = 0; j < BLK; ++j) c[j] = (int)q_grid(x[j] / s, FMT_INT4);
+                size_t r = ((size_t)h * S + t) * ND + db;
+                pack16(c, v_packed + r * PACKB);
+                v_scale[r] = orc_f32_to_f16(s);
+            }
+}
+
+static inline int sx4(int n) { return n >= 8 ? n - 16 : n; }
+
+/* int4_kivi/triton_kernels.py:181-210,257-286: value = code * fp32(f16 scale),
+ * written as fp32 (the caller rounds to bf16).  kout [H, S, D] covers the first
+ * NP*16 tokens; vout [H, S, D] covers every token. */
+void orc_dequant_int4(const uint8_t *k_packed, const uint16_t *k_scale,
+                      const uint8_t *v_packed, const uint16_t *v_scale,
+                      int H, int S, int D, float *kout, float *vout) {
+    int NP = S / BLK, ND = D / BLK;
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int h = 0; h < H; ++h)
+        for (int d = 0; d < D; ++d)
+            for (int p = 0; p < NP; ++p) {
+                size_t r = ((size_t)h * D + d) * NP + p;
+                float s = orc_f16_to_f32(k_scale[r]);
+                for (int j = 0; j < BLK; ++j) {
+                    int b = k_packed[r * PACKB + j / 2];
+                    int n = (j & 1) ? (b >> 4) : (b & 0xf);
+                    kout[((size_t)h * S + p * BLK + j) * D + d] = (float)sx4(n) * s;
+                }
+            }
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int h = 0; h < H; ++h)
+        for (int t = 0; t < S; ++t)
+            for (int db = 0; db < ND; ++db) {
+                size_t r = ((size_t)h * S + t) * ND + db;
+                float s = orc_f16_to_f32(v_scale[r]);
+                for (int c = 0; c < BLK; ++c) {
+                    int b = v_packed[r * PACKB + c / 2];
+                    int n = (c & 1) ? (b >> 4) : (b & 0xf);
+                    vout[((size_t)h * S + t) * D + db * BLK + c] = (float)sx4(n) * s;
+                }
+            }
+}
+
+/* ------------------------------------------------------------------------- */
+/* NVFP4-KIVI store.  Reference semantics: kv_quant.py:220-229 (`nvfp4`:     */
+/* e2m1 grid, qmax 6, bucketize ties toward the smaller magnitude) with the   */
+/* fp8-e4m3 block scale of the paged fork (scripts/diag_kernel_perchannel.py: */
+/* 30-48, WRITEUP.md:97-107: scales rounded to e4m3 inside the search).       */
+/* Block scale byte sc = e4m3(s / g); the dequantisable scale is              */
+/* sd = fp32(sc) * g; codes are e2m1(x / sd) (all +0 when sd == 0).  Nibble = */
+/* sign << 3 | level index, i.e. the hardware e2m1 bit pattern.               */
+/* ------------------------------------------------------------------------- */
+static float nvfp4_block(const float x[BLK], int calib, const float *alphas,
+                         int n_alphas, float g, uint8_t *sc_out, uint8_t nib[BLK]) {
+    float amax = absmax16(x);
+    int nA = (calib == CAL_ABSMAX) ? 1 : n_alphas;
+    float best = INFINITY;
+    uint8_t best_sc = 0;
+    for (int a = 0; a < nA; ++a) {
+        float s = (calib == CAL_ABSMAX) ? amax / 6.0f : (alphas[a] * amax) / 6.0f;
+        uint8_t sc = orc_f32_to_e4m3(s / g);
+        float sd = orc_e4m3_to_f32(sc) * g;
+        float e[BLK];
+        for (int i = 0; i < BLK; ++i) {
+            float q = (sd == 0.0f) ? 0.0f : q_grid(x[i] / sd, FMT_NVFP4);
+            float d = x[i] - q * sd;
+            e[i] = d * d;
+        }
+        float err = mean16(e);
+        if (err < best) { best = err; best_sc = sc; }
+    }
+    float sd = orc_e4m3_to_f32(best_sc) * g;
+    for (int i = 0; i < BLK; ++i) {
+        if (sd == 0.0f) { nib[i] = 0; continue; }
+        int neg, idx = e2m1_index(x[i] / sd, &neg);
+        nib[i] = (uint8_t)((neg ? 8 : 0) | idx);
+    }
+    *sc_out = best_sc;
+    return sd;
+}
+
+/* Same tensor geometry as orc_store_int4, with 1-byte e4m3 scales. */
+void orc_store_nvfp4(const float *k, const float *v, int H, int S, int D,
+                     int calib_k, int calib_v, const float *alphas, int n_alphas,
+                     float g_k, float g_v,
+                     uint8_t *k_packed, uint8_t *k_scale,
+                     uint8_t *v_packed, uint8_t *v_scale) {
+    int NP = S / BLK, ND = D / BLK;
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int h = 0; h < H; ++h)
+        for (int d = 0; d < D; ++d)
+            for (int p = 0; p < NP; ++p) {
+                float x[BLK]; uint8_t nib[BLK]; int c[BLK];
+                gather_block(k, S, D, LAYOUT_CHANNEL, h, d, p, x);
+                size_t r = ((size_t)h * D + d) * NP + p;
+                nvfp4_block(x, calib_k, alphas, n_alphas, g_k, &k_scale[r], nib);
+                for (int j = 0; j < BLK; ++j) c[j] = nib[j];
+                pack16(c, k_packed + r * PACKB);
+            }
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int h = 0; h < H; ++h)
+        for (int t = 0; t < S; ++t)
+            for (int db = 0; db < ND; ++db) {
+                float x[BLK]; uint8_t nib[BLK]; int c[BLK];
+                gather_block(v, S, D, LAYOUT_HEADDIM, h, t, db, x);
+                size_t r = ((size_t)h * S + t) * ND + db;
+                nvfp4_block(x, calib_v, alphas, n_alphas, g_v, &v_scale[r], nib);
+                for (int j = 0; j < BLK; ++j) c[j] = nib[j];
+                pack16(c, v_packed + r * PACKB);
+            }
+}
+
+static inline float e2m1_val(int n) {
+    float l = E2M1_LEVELS[n & 7];
+    return (n & 8) ? -l : l;
+}
+
+/* value = e2m1(code) * (fp32(e4m3 scale) * g), fp32. */
+void orc_dequant_nvfp4(const uint8_t *k_packed, const uint8_t *k_scale,
+                       const uint8_t *v_packed, const uint8_t *v_scale,
+                       int H, int S, int D, float g_k, float g_v,
+                       float *kout, float *vout) {
+    int NP = S / BLK, ND = D / BLK;
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int h = 0; h < H; ++h)
+        for (int d = 0; d < D; ++d)
+            for (int p = 0; p < NP; ++p) {
+                size_t r = ((size_t)h * D + d) * NP + p;
+                float s = orc_e4m3_to_f32(k_scale[r]) * g_k;
+                for (int j = 0; j < BLK; ++j) {
+                    int b = k_packed[r * PACKB + j / 2];
+                    int n = (j & 1) ? (b >> 4) : (b & 0xf);
+                    kout[((size_t)h * S + p * BLK + j) * D + d] = e2m1_val(n) * s;
+                }
+            }
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int h = 0; h < H; ++h)
+        for (int t = 0; t < S; ++t)
+            for (int db = 0; db < ND; ++db) {
+                size_t r = ((size_t)h * S + t) * ND + db;
+                float s = orc_e4m3_to_f32(v_scale[r]) * g_v;
+                for (int c = 0; c < BLK; ++c) {
+                    int b = v_packed[r * PACKB + c / 2];
+                    int n = (c & 1) ? (b >> 4) : (b & 0xf);
+                    vout[((size_t)h * S + t) * D + db * BLK + c] = e2m1_val(n) * s;
+                }
+            }
+}
+
+/* ------------------------------------------------------------------------- */
+/* Decode attention over dequantised K/V (scripts/validate_int4_kivi_decode.py*/
+/* :73-84 `ref_decode_fp32`: GQA by repeat_interleave, softmax(q.k*sm) @ v),  */
+/* evaluated in double.  k, v: fp32 [B, Hkv, S, D]; q: [B, Hq, D];            */
+/* out: fp32 [B, Hq, D].  Optional per-batch lengths (NULL = all S).          */
+/* ------------------------------------------------------------------------- */
+void orc_decode_attention(const float *q, const float *k, const float *v,
+                          const int *seq_lens, int B, int Hq, int Hkv, int S,
+                          int D, float sm_scale, float *out) {
+    int G = Hq / Hkv;
+    #pragma omp parallel for collapse(2) schedule(dynamic)
+    for (int b = 0; b < B; ++b)
+        for (int hq = 0; hq < Hq; ++hq) {
+            int L = seq_lens ? seq_lens[b] : S;
+            int hk = hq / G;
+            const float *qq = q + ((size_t)b * Hq + hq) * D;
+            const float *kk = k + ((size_t)b * Hkv + hk) * (size_t)S * D;
+            const float *vv = v + ((size_t)b * Hkv + hk) * (size_t)S * D;
+            double *sc = (double *)malloc(sizeof(double) * (L > 0 ? L : 1));
+            double m = -INFINITY;
+            for (int t = 0; t < L; ++t) {
+                double acc = 0.0;
+                for (int d = 0; d < D; ++d) acc += (double)qq[d] * kk[(size_t)t * D + d];
+                sc[t] = acc * sm_scale;
+                if (sc[t] > m) m = sc[t];
+            }
+            double l = 0.0;
+            for (int t = 0; t < L; ++t) { sc[t] = exp(sc[t] - m); l += sc[t]; }
+            float *o = out + ((size_t)b * Hq + hq) * D;
+            for (int d = 0; d < D; ++d) {
+                double acc = 0.0;
+                for (int t = 0; t < L; ++t) acc += sc[t] * vv[(size_t)t * D + d];
+                o[d] = (float)(L > 0 ? acc / l : 0.0);
+            }
+            free(sc);
+        }
+}
+
+int orc_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
