@@ -1,0 +1,160 @@
+/*
+ * kivi_sm100.h -- C ABI of libkivi_sm100.so, the B200 (sm_100a) 4-bit
+ * KV-cache library: INT4-KIVI / NVFP4-KIVI quantize-and-store, dequant, the
+ * kv_quant roundtrip primitive, and fused split-K flash-decode with an LSE
+ * merge.
+ *
+ * Conventions
+ *   - Every pointer is device memory owned by the caller; nothing here
+ *     allocates, frees or synchronises.  Work is enqueued on `stream`
+ *     (a cudaStream_t; NULL = legacy default stream).
+ *   - Element strides are in elements of the pointed-to type.
+ *   - bf16 / fp16 tensors are passed as `const void*` (raw 16-bit words).
+ *   - Return value: KIVI_OK (0) or a kivi_status code; kivi_status_string()
+ *     names it.  Argument errors are detected before any launch.
+ *   - Device-side timeouts (a pipeline wait that never completes) do not trap:
+ *     the kernel writes a nonzero code into `err` (if non-NULL) and returns.
+ *
+ * Reference interfaces replaced (paths inside a1exxd0/poolside-hackathon):
+ * each entry point cites the Triton kernel + host wrapper it stands in for.
+ */
+#ifndef KIVI_SM100_H
+#define KIVI_SM100_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *kivi_stream_t;   /* == cudaStream_t */
+
+enum kivi_status {
+    KIVI_OK = 0,
+    KIVI_ERR_ARG = 1,          /* bad shape / null pointer / bad enum       */
+    KIVI_ERR_ALIGN = 2,        /* pointer or stride violates alignment rule */
+    KIVI_ERR_UNSUPPORTED = 3,  /* valid but not implemented (e.g. head_dim) */
+    KIVI_ERR_CUDA = 4,         /* a CUDA runtime/driver call failed         */
+    KIVI_ERR_TIMEOUT = 5       /* device-side bounded wait expired          */
+};
+
+enum kivi_fmt { KIVI_FMT_INT4 = 0, KIVI_FMT_INT3 = 1, KIVI_FMT_NVFP4 = 2 };
+enum kivi_calib { KIVI_CALIB_ABSMAX = 0, KIVI_CALIB_MSE = 1 };
+enum kivi_layout { KIVI_LAYOUT_HEADDIM = 0, KIVI_LAYOUT_CHANNEL = 1 };
+enum kivi_dtype { KIVI_DT_BF16 = 0, KIVI_DT_F16 = 1, KIVI_DT_F32 = 2 };
+
+const char *kivi_status_string(int status);
+int kivi_version(void);                 /* 100 * major + minor */
+int kivi_last_cuda_error(void);         /* cudaError_t of the last KIVI_ERR_CUDA */
+
+/* ------------------------------------------------------------------------ */
+/* Quantize-and-store.                                                       */
+/*                                                                           */
+/* Replaces int4_kivi/triton_kernels.py:162-203 (k_store_kernel),            */
+/* :241-279 (v_store_kernel) and their launches in int4_kivi/cache.py:90-141.*/
+/*                                                                           */
+/* Input K: 16-bit [H, S_k, D], V: [H, S_v, D] (dtype `in_dtype`), strided.  */
+/* (S_k and S_v differ on append: K pages vs new V tokens, one launch.)      */
+/* K: the first (S_k/16)*16 tokens, per channel over 16-token pages, are     */
+/*    written to k_packed[h, d, kpage0 + p, 0:8] (row stride k_np_stride     */
+/*    pages) and k_scale[h, d, kpage0 + p].  Input token 0 must start a page. */
+/* V: every token, per 16-channel block, to v_packed[h, vtok0 + t, db, 0:8]  */
+/*    (head stride v_s_stride tokens) and v_scale[h, vtok0 + t, db].          */
+/* fmt INT4: scale = fp16 (2 bytes), codes two's-complement nibbles.         */
+/* fmt NVFP4: scale = e4m3 byte of (s / g), codes e2m1 nibbles (g_k, g_v).   */
+/* alphas: device fp32 [n_alphas], the MSE clip grid linspace(0.5, 1, n).    */
+/* D must be a multiple of 16.                                               */
+/* ------------------------------------------------------------------------ */
+int kivi_store(const void *k, const void *v, int in_dtype,
+               int64_t sk_h, int64_t sk_s, int64_t sk_d,
+               int64_t sv_h, int64_t sv_s, int64_t sv_d,
+               int H, int S_k, int S_v, int D, int fmt, int calib_k, int calib_v,
+               const float *alphas, int n_alphas, float g_k, float g_v,
+               uint8_t *k_packed, void *k_scale, int kpage0, int k_np_stride,
+               uint8_t *v_packed, void *v_scale, int vtok0, int v_s_stride,
+               kivi_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Dequantize to bf16 [H, S, D] (out strides in elements).                   */
+/* Replaces int4_kivi/triton_kernels.py:206-235 (k_dequant_kernel),          */
+/* :282-311 (v_dequant_kernel) and int4_kivi/cache.py:165-201.               */
+/* K writes tokens [0, (S/16)*16) only (the bf16 hot tail is the caller's);  */
+/* V writes every token.  value = code * fp32(scale) (NVFP4: * g).           */
+/* ------------------------------------------------------------------------ */
+int kivi_dequant(const uint8_t *k_packed, const void *k_scale, int k_np_stride,
+                 const uint8_t *v_packed, const void *v_scale, int v_s_stride,
+                 int H, int S, int D, int fmt, float g_k, float g_v,
+                 void *k_out, void *v_out, int64_t so_h, int64_t so_s, int64_t so_d,
+                 kivi_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* kv_quant.roundtrip on the GPU.  Replaces kv_quant.py:299-321 (and         */
+/* _calibrate/_to_blocks :232-266) for x [H, S, D] contiguous of `dtype`.    */
+/* 'channel' copies the trailing S % 16 tokens unchanged.                    */
+/* ------------------------------------------------------------------------ */
+int kivi_roundtrip(const void *x, void *y, int dtype, int H, int S, int D,
+                   int fmt, int layout, int calib, const float *alphas, int n_alphas,
+                   kivi_stream_t stream);
+
+/* kv_quant.py:247-266 `_calibrate` over n contiguous fp32 blocks [n, 16]. */
+int kivi_calibrate(const float *blocks, int64_t n, int fmt, int calib,
+                   const float *alphas, int n_alphas, float *scales,
+                   kivi_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Fused split-K flash-decode over a packed cache.                           */
+/*                                                                           */
+/* Replaces int4_kivi/decode.py:53-219 (_kivi_decode_kernel +                */
+/* kivi_decode_attention), :234-317,494-533 (split-K batched) and            */
+/* :351-477 (GQA split-K) plus :320-340 (_combine_kernel).                   */
+/*                                                                           */
+/* q       : bf16 [B, Hq, D] (strides q_sb, q_sh; last dim contiguous)       */
+/* cache   : B*Hkv stacked heads, kv-head index b*Hkv + h.                    */
+/*           k_packed [BH, D, k_np_stride, 8], k_scale [BH, D, k_np_stride]  */
+/*           k_hot bf16 [BH, hot_stride, D] (tokens n_full..S-1)             */
+/*           v_packed [BH, v_s_stride, D/16, 8], v_scale [BH, v_s_stride, D/16]*/
+/*           fmt INT4: fp16 scales; NVFP4: e4m3 scales with g_k, g_v.        */
+/* S       : tokens attended (n_full = (S/16)*16 from pages, rest from k_hot)*/
+/* out     : bf16 [B, Hq, D] contiguous.                                     */
+/* work    : fp32 scratch of kivi_decode_workspace_floats(...) floats.       */
+/* err     : optional int32 device flag, set nonzero on a device timeout.    */
+/* Fast path requirements: D == 128, Hq/Hkv <= 8, k_np_stride % 16 == 0,     */
+/* v_s_stride % 16 == 0, 16-byte aligned pointers; otherwise a generic       */
+/* CUDA-core path with identical results semantics runs.                     */
+/* ------------------------------------------------------------------------ */
+int64_t kivi_decode_workspace_floats(int B, int Hq, int Hkv, int S, int D);
+
+int kivi_decode(const void *q, int64_t q_sb, int64_t q_sh,
+                const uint8_t *k_packed, const void *k_scale, int k_np_stride,
+                const void *k_hot, int hot_stride,
+                const uint8_t *v_packed, const void *v_scale, int v_s_stride,
+                int B, int Hq, int Hkv, int S, int D, int fmt,
+                float sm_scale, float g_k, float g_v,
+                void *out, float *work, int64_t work_floats, int *err,
+                kivi_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Partial-state variant for sequence-parallel decode across GPUs: instead   */
+/* of bf16 output, writes this rank's merged (m, l, acc) per (b, q-head):     */
+/* m_out/l_out fp32 [B*Hq] (m in log2 units of the scaled score), acc_out    */
+/* fp32 [B*Hq, D] unnormalised.  kivi_lse_merge() combines R such records.   */
+/* ------------------------------------------------------------------------ */
+int kivi_decode_partial(const void *q, int64_t q_sb, int64_t q_sh,
+                        const uint8_t *k_packed, const void *k_scale, int k_np_stride,
+                        const void *k_hot, int hot_stride,
+                        const uint8_t *v_packed, const void *v_scale, int v_s_stride,
+                        int B, int Hq, int Hkv, int S, int D, int fmt,
+                        float sm_scale, float g_k, float g_v,
+                        float *m_out, float *l_out, float *acc_out,
+                        float *work, int64_t work_floats, int *err,
+                        kivi_stream_t stream);
+
+/* Log-sum-exp merge of R partial records laid out [R, rows] / [R, rows, D]  */
+/* (int4_kivi/decode.py:320-340 semantics) -> bf16 out [rows, D].            */
+int kivi_lse_merge(const float *m, const float *l, const float *acc, int R, int rows,
+                   int D, void *out, kivi_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KIVI_SM100_H */

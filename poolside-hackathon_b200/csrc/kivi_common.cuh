@@ -1,0 +1,247 @@
+// kivi_common.cuh -- shared device helpers for the sm_100a 4-bit KV-cache kernels.
+//
+// Quantiser arithmetic restates kv_quant.py:16-42, 206-266 (the reference's
+// calibration) with every fp32 operation written as an explicitly rounded
+// intrinsic (__fdiv_rn, __fmul_rn, __fadd_rn, __fsub_rn) so the compiler can
+// neither contract nor reorder it: codes and scales are bit-identical to the
+// reference on CPU.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+namespace kivi {
+
+constexpr int BLK = 16;   // elements per quant block; tokens per K page
+constexpr int PACKB = 8;  // bytes per packed block
+
+enum Fmt { FMT_INT4 = 0, FMT_INT3 = 1, FMT_NVFP4 = 2 };
+enum Calib { CAL_ABSMAX = 0, CAL_MSE = 1 };
+
+__device__ __forceinline__ float qmax_of(int fmt) {
+    return fmt == FMT_INT4 ? 7.0f : (fmt == FMT_INT3 ? 3.0f : 6.0f);
+}
+
+// kv_quant.py:220-225: bucketize(|y|, bounds, right=False) -> count of bounds
+// strictly below |y|; ties resolve to the smaller magnitude.
+__device__ __forceinline__ int e2m1_index(float a) {
+    return (a > 0.25f) + (a > 0.75f) + (a > 1.25f) + (a > 1.75f) +
+           (a > 2.5f) + (a > 3.5f) + (a > 5.0f);
+}
+
+__device__ __forceinline__ float e2m1_level(int idx) {
+    // 0, .5, 1, 1.5, 2, 3, 4, 6
+    return idx < 4 ? 0.5f * idx : (idx == 4 ? 2.0f : (idx == 5 ? 3.0f : (idx == 6 ? 4.0f : 6.0f)));
+}
+
+// kv_quant.py:211-225: scale-normalised value onto the format grid.
+__device__ __forceinline__ float q_grid(float y, int fmt) {
+    if (fmt == FMT_NVFP4) {
+        float l = e2m1_level(e2m1_index(fabsf(y)));
+        return y > 0.0f ? l : (y < 0.0f ? -l : 0.0f);
+    }
+    float r = rintf(y), qm = qmax_of(fmt);
+    return r > qm ? qm : (r < -qm ? -qm : r);
+}
+
+// torch CPU order for the mean of a contiguous 16-element row:
+// v[j] = e[j] + e[j+8], then ((v0+v1)+v2)+...+v7, then / 16.
+__device__ __forceinline__ float mean16(const float e[BLK]) {
+    float s = __fadd_rn(e[0], e[8]);
+#pragma unroll
+    for (int j = 1; j < 8; ++j) s = __fadd_rn(s, __fadd_rn(e[j], e[j + 8]));
+    return __fdiv_rn(s, 16.0f);
+}
+
+__device__ __forceinline__ float absmax16(const float x[BLK]) {
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < BLK; ++i) m = fmaxf(m, fabsf(x[i]));
+    return fmaxf(m, 1e-9f);   // .clamp_min(1e-9)
+}
+
+// Reconstruction error of one block under scale s (the kv_quant MSE term).
+__device__ __forceinline__ float block_err(const float x[BLK], float s, int fmt) {
+    float e[BLK];
+#pragma unroll
+    for (int i = 0; i < BLK; ++i) {
+        float q = (s == 0.0f) ? 0.0f : q_grid(__fdiv_rn(x[i], s), fmt);
+        float d = __fsub_rn(x[i], __fmul_rn(q, s));
+        e[i] = __fmul_rn(d, d);
+    }
+    return mean16(e);
+}
+
+// kv_quant.py:247-266 `_calibrate` for one block (fp32 scale).
+__device__ __forceinline__ float calibrate16(const float x[BLK], int fmt, int calib,
+                                             const float* __restrict__ alphas, int n_alphas) {
+    const float qmax = qmax_of(fmt);
+    const float amax = absmax16(x);
+    if (calib == CAL_ABSMAX) return __fdiv_rn(amax, qmax);
+    float best = __int_as_float(0x7f800000), bs = 0.0f;
+    for (int a = 0; a < n_alphas; ++a) {
+        float s = __fdiv_rn(__fmul_rn(alphas[a], amax), qmax);
+        float err = block_err(x, s, fmt);
+        if (err < best) { best = err; bs = s; }   // strict '<' == torch.argmin
+    }
+    return bs;
+}
+
+// fp32 -> e4m3 (RNE, saturating) and back; used for NVFP4 block scales.
+__device__ __forceinline__ uint8_t f32_to_e4m3(float f) {
+    return (uint8_t)__nv_cvt_float_to_fp8(f, __NV_SATFINITE, __NV_E4M3);
+}
+__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
+    __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
+    return __half2float(__half(h));
+}
+
+// NVFP4-KIVI block: pick the e4m3 scale byte (scale rounded inside the search),
+// return the dequantisable scale sd = fp32(e4m3(s/g)) * g.
+__device__ __forceinline__ float nvfp4_calibrate16(const float x[BLK], int calib,
+                                                   const float* __restrict__ alphas, int n_alphas,
+                                                   float g, uint8_t* sc_out) {
+    const float amax = absmax16(x);
+    const int nA = (calib == CAL_ABSMAX) ? 1 : n_alphas;
+    float best = __int_as_float(0x7f800000);
+    uint8_t best_sc = 0;
+    for (int a = 0; a < nA; ++a) {
+        float s = (calib == CAL_ABSMAX) ? __fdiv_rn(amax, 6.0f)
+                                        : __fdiv_rn(__fmul_rn(alphas[a], amax), 6.0f);
+        uint8_t sc = f32_to_e4m3(__fdiv_rn(s, g));
+        float sd = __fmul_rn(e4m3_to_f32(sc), g);
+        float err = block_err(x, sd, FMT_NVFP4);
+        if (err < best) { best = err; best_sc = sc; }
+    }
+    *sc_out = best_sc;
+    return __fmul_rn(e4m3_to_f32(best_sc), g);
+}
+
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+
+__device__ __forceinline__ int sx4(int n) { return n >= 8 ? n - 16 : n; }
+
+// ---------------------------------------------------------------------------
+// PTX wrappers: mbarrier, TMA, ldmatrix, mma.sync
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: returns false after ~timeout_ns without the phase completing.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint64_t timeout_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > timeout_ns) return false;
+    }
+}
+
+// TMA tiled loads (no multicast), completion counted on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];"
+        :: "r"(smem_u32(dst)), "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_t* bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];"
+        :: "r"(smem_u32(dst)), "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z) : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+
+// D = A(16x16 f16, row) * B(16x8 f16, col) + D, fp32 accumulate.
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t m, uint32_t x) {
+    // (a & m) ^ x
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0x78;" : "=r"(d) : "r"(a), "r"(m), "r"(x));
+    return d;
+}
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// Signed INT4 nibbles at bit offsets {0,16} (lo) or {4,20} (hi) of a word ->
+// exact fp16x2 codes (fp16 magic-number method: nibble^8 placed in the
+// mantissa of 1024, then the bias 1032 removed).
+__device__ __forceinline__ __half2 int4_lo_to_h2(uint32_t w) {
+    uint32_t v = lop3_and_xor(w, 0x000F000Fu, 0x64086408u);      // 1024 + (n ^ 8)
+    return __hsub2(u32_as_h2(v), u32_as_h2(0x64086408u));         // - 1032
+}
+__device__ __forceinline__ __half2 int4_hi_to_h2(uint32_t w) {
+    uint32_t v = lop3_and_xor(w, 0x00F000F0u, 0x64806480u);      // 1024 + 16 (n ^ 8)
+    return __hfma2(u32_as_h2(v), __float2half2_rn(0.0625f), __float2half2_rn(-72.0f));
+}
+
+// Two e2m1 nibbles of one byte -> fp16x2 (exact), hardware conversion.
+__device__ __forceinline__ uint32_t e2m1x2_to_h2(uint32_t byte_in_low8) {
+    uint32_t d;
+    asm("{ .reg .b8 t; cvt.u8.u32 t, %1; cvt.rn.f16x2.e2m1x2 %0, t; }" : "=r"(d) : "r"(byte_in_low8));
+    return d;
+}
+__device__ __forceinline__ uint32_t e4m3x2_to_h2(uint16_t two) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(two));
+    return d;
+}
+
+}  // namespace kivi

@@ -1,0 +1,761 @@
+// kivi_decode.cu -- fused split-K flash-decode over a packed INT4/NVFP4 KIVI cache.
+//
+// Replaces the reference's Triton decode path (int4_kivi/decode.py:53-477):
+// per (sequence, kv-head) the full 16-token pages are streamed once, every
+// query head of the GQA group is served from the same bytes, and a second
+// launch merges the per-warp partial softmax states with log-sum-exp (the
+// reference's _combine_kernel, decode.py:320-340) and adds the bf16 hot tail.
+//
+// Fast path (D = 128, GQA group <= 8, 16-aligned strides):
+//   * work = flattened (head, 128-token tile) list split evenly over a
+//     persistent grid (stream-K style), so every SM gets the same bytes;
+//   * warp 4 issues TMA tile loads (K codes/scales, V codes/scales) into a
+//     4-stage ring guarded by mbarriers; warps 0-3 each own 32 tokens of a
+//     tile;
+//   * packed nibbles go smem -> registers with ldmatrix.trans, which pairs
+//     two channels (K) or two tokens (V) per 32-bit word; a LOP3 fp16 magic
+//     (INT4) or the hardware e2m1 -> f16x2 cvt (NVFP4) yields exact codes,
+//     which are scaled by per-page / per-token scale pairs;
+//   * QK^T and PV run on mma.sync m16n8k16 (f16 in, f32 accumulate) with the
+//     query heads as the N=8 side; for INT4 the fp16 scale is split into an
+//     8-bit head and a 3-bit tail so every product is exact (two MMAs);
+//   * online softmax in base 2 with warp-shuffle row maxima.
+#include "kivi_common.cuh"
+#include "kivi_internal.h"
+#include <cuda.h>
+
+namespace kivi {
+
+constexpr int TILE = 128;        // tokens per pipeline stage (8 pages)
+constexpr int NWARP_C = 4;       // consumer warps, 32 tokens each
+constexpr int NTHREADS = (NWARP_C + 1) * 32;
+constexpr int NST = 4;           // pipeline depth
+constexpr int DH = 128;          // head_dim of the fast path
+constexpr int PB_PITCH = 40;     // halves per head row in the P staging buffer
+
+struct DecodeParams {
+    const __nv_bfloat16* q; int64_t q_sb, q_sh;
+    const uint8_t* k_packed; const void* k_scale; int k_np_stride;
+    const __nv_bfloat16* k_hot; int hot_stride;
+    const uint8_t* v_packed; const void* v_scale; int v_s_stride;
+    int B, Hq, Hkv, G, S, D, n_full, hot;
+    float scale2;        // sm_scale * log2(e) (* g_k for NVFP4)
+    float g_v;
+    float sm_scale, g_k;
+    int T;               // tiles per head
+    int64_t W;           // total tiles
+    int N;               // CTAs of the main kernel
+    float* part_m; float* part_l; float* part_acc;
+    int* err;
+};
+
+__host__ __device__ inline int64_t tile_start(int64_t c, int64_t W, int N) { return c * W / N; }
+
+template <int FMT>
+struct StageLayout {
+    static constexpr int KC = 0;                        // 128 ch x 64 B, 64B-swizzled
+    static constexpr int KS = 8192;                     // INT4: 128 x 16 B ; NVFP4: 128 x 16 B raw e4m3
+    static constexpr int VC = 8192 + 2048;              // 128 tok x 64 B, 64B-swizzled
+    static constexpr int VS = VC + 8192;                // INT4: 128 x 16 B ; NVFP4: 128 x 8 B
+    static constexpr int BYTES = VS + 2048;
+    static constexpr uint32_t TX = (FMT == FMT_NVFP4) ? (8192 + 2048 + 8192 + 1024) : 20480;
+};
+
+struct __align__(8) SmemCtl {
+    uint64_t full[NST];
+    uint64_t empty[NST];
+    int abort;
+};
+
+__device__ __forceinline__ void set_err(int* err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+// Dequantise two ldmatrix words (k-halves A and B of one MMA) into the A
+// fragments of tile 0 (nibble bytes 0/2) and tile 1 (bytes 1/3), unscaled.
+template <int FMT>
+__device__ __forceinline__ void codes4(uint32_t w, uint32_t& t0_lo, uint32_t& t0_hi,
+                                       uint32_t& t1_lo, uint32_t& t1_hi) {
+    if (FMT == FMT_NVFP4) {
+        uint32_t h0 = e2m1x2_to_h2(w & 0xFF), h1 = e2m1x2_to_h2((w >> 8) & 0xFF);
+        uint32_t h2 = e2m1x2_to_h2((w >> 16) & 0xFF), h3 = e2m1x2_to_h2(w >> 24);
+        t0_lo = __byte_perm(h0, h2, 0x5410);
+        t0_hi = __byte_perm(h0, h2, 0x7632);
+        t1_lo = __byte_perm(h1, h3, 0x5410);
+        t1_hi = __byte_perm(h1, h3, 0x7632);
+    } else {
+        t0_lo = h2_as_u32(int4_lo_to_h2(w));
+        t0_hi = h2_as_u32(int4_hi_to_h2(w));
+        const uint32_t w8 = w >> 8;
+        t1_lo = h2_as_u32(int4_lo_to_h2(w8));
+        t1_hi = h2_as_u32(int4_hi_to_h2(w8));
+    }
+}
+
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+    return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
+}
+
+// One m16n8k16 step for two M-tiles given the k-half words wA, wB and their
+// scale pairs.  INT4 splits each scale into head/tail parts (two exact MMAs).
+template <int FMT>
+__device__ __forceinline__ void mma_pair(float (&c0)[4], float (&c1)[4], uint32_t wA, uint32_t wB,
+                                         uint32_t sA, uint32_t sB, uint32_t b0, uint32_t b1) {
+    uint32_t a0l, a0h, a1l, a1h, c0l, c0h, c1l, c1h;
+    codes4<FMT>(wA, a0l, a0h, a1l, a1h);     // k-half A: tile0 rows(lo,hi), tile1 rows
+    codes4<FMT>(wB, c0l, c0h, c1l, c1h);     // k-half B
+    if (FMT == FMT_NVFP4) {
+        mma_f16(c0, hmul2u(a0l, sA), hmul2u(a0h, sA), hmul2u(c0l, sB), hmul2u(c0h, sB), b0, b1);
+        mma_f16(c1, hmul2u(a1l, sA), hmul2u(a1h, sA), hmul2u(c1l, sB), hmul2u(c1h, sB), b0, b1);
+    } else {
+        const uint32_t sAh = sA & 0xFFF8FFF8u, sBh = sB & 0xFFF8FFF8u;
+        const uint32_t sAl = h2_as_u32(__hsub2(u32_as_h2(sA), u32_as_h2(sAh)));
+        const uint32_t sBl = h2_as_u32(__hsub2(u32_as_h2(sB), u32_as_h2(sBh)));
+        mma_f16(c0, hmul2u(a0l, sAh), hmul2u(a0h, sAh), hmul2u(c0l, sBh), hmul2u(c0h, sBh), b0, b1);
+        mma_f16(c0, hmul2u(a0l, sAl), hmul2u(a0h, sAl), hmul2u(c0l, sBl), hmul2u(c0h, sBl), b0, b1);
+        mma_f16(c1, hmul2u(a1l, sAh), hmul2u(a1h, sAh), hmul2u(c1l, sBh), hmul2u(c1h, sBh), b0, b1);
+        mma_f16(c1, hmul2u(a1l, sAl), hmul2u(a1h, sAl), hmul2u(c1l, sBl), hmul2u(c1h, sBl), b0, b1);
+    }
+}
+
+__device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
+    return row * 64u + 16u * (chunk ^ ((row >> 1) & 3u));
+}
+
+// ---------------------------------------------------------------------------
+// Fast path kernel.
+// ---------------------------------------------------------------------------
+template <int FMT>
+__global__ void __launch_bounds__(NTHREADS, 2)
+decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_constant__ CUtensorMap tm_ks,
+                   const __grid_constant__ CUtensorMap tm_vc, const __grid_constant__ CUtensorMap tm_vs,
+                   const DecodeParams p) {
+    using L = StageLayout<FMT>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stages = smem;                                            // NST * L::BYTES
+    __half* pbuf = reinterpret_cast<__half*>(stages + NST * L::BYTES); // [4][8][PB_PITCH]
+    __half* scv = pbuf + NWARP_C * 8 * PB_PITCH;                       // NVFP4: [4 warps][32][8] fp16
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(scv + (FMT == FMT_NVFP4 ? NWARP_C * 32 * 8 : 0));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x;
+    const int64_t i0 = tile_start(c, p.W, p.N), i1 = tile_start(c + 1, p.W, p.N);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NST; ++s) { mbar_init(&ctl->full[s], 1); mbar_init(&ctl->empty[s], NWARP_C); }
+        ctl->abort = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == NWARP_C) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            prefetch_tmap(&tm_kc); prefetch_tmap(&tm_ks); prefetch_tmap(&tm_vc); prefetch_tmap(&tm_vs);
+            int it = 0;
+            for (int64_t i = i0; i < i1; ++i, ++it) {
+                const int s = it % NST;
+                if (!mbar_wait_bounded(&ctl->empty[s], ((it / NST) & 1) ^ 1)) {
+                    set_err(p.err, KIVI_ERR_TIMEOUT);
+                    ctl->abort = 1;
+                    break;
+                }
+                if (ctl->abort) break;
+                const int bh = (int)(i / p.T), tl = (int)(i % p.T);
+                uint8_t* st = stages + s * L::BYTES;
+                mbar_arrive_expect_tx(&ctl->full[s], L::TX);
+                tma_load_2d(st + L::KC, &tm_kc, &ctl->full[s], tl * 64, bh * DH);
+                if (FMT == FMT_NVFP4) tma_load_2d(st + L::KS, &tm_ks, &ctl->full[s], (tl >> 1) * 16, bh * DH);
+                else tma_load_2d(st + L::KS, &tm_ks, &ctl->full[s], tl * 8, bh * DH);
+                const int vrow = bh * p.v_s_stride + tl * TILE;
+                tma_load_2d(st + L::VC, &tm_vc, &ctl->full[s], 0, vrow);
+                if (FMT == FMT_NVFP4) tma_load_2d(st + L::VS, &tm_vs, &ctl->full[s], 0, vrow >> 1);
+                else tma_load_2d(st + L::VS, &tm_vs, &ctl->full[s], 0, vrow);
+            }
+            // Drain: every issued tile's bytes must land before the CTA retires.
+            for (int j = (it > NST ? it - NST : 0); j < it; ++j)
+                if (!mbar_wait_bounded(&ctl->full[j % NST], (j / NST) & 1)) set_err(p.err, KIVI_ERR_TIMEOUT);
+        }
+        return;
+    }
+
+    // ------------------------------- consumers --------------------------------
+    const int g = lane >> 2, tq = lane & 3;
+    const int G = p.G;
+    const int src_k = ((2 * warp + (g >> 2)) << 2) | tq;   // lane holding my page's K scales
+    __half* pb = pbuf + warp * 8 * PB_PITCH;
+
+    uint32_t qB[8][2];
+    float acc[8][4];     // [tile: 2*seg + (0:X,1:Y)][c]
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    int cur = -1;
+
+    auto flush = [&](int bh) {
+        // per-warp partial record: slot = (c + bh) * 4 + warp
+        float L0 = l0, L1 = l1;
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            L0 += __shfl_xor_sync(0xffffffffu, L0, o);
+            L1 += __shfl_xor_sync(0xffffffffu, L1, o);
+        }
+        const int64_t slot = ((int64_t)(c + bh) * NWARP_C + warp) * G;
+        const float gv = (FMT == FMT_NVFP4) ? p.g_v : 1.0f;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int h = 2 * tq + hh;
+            if (h < G) {
+                if (g == 0) {
+                    p.part_m[slot + h] = hh ? m1 : m0;
+                    p.part_l[slot + h] = hh ? L1 : L0;
+                }
+                float* a = p.part_acc + (slot + h) * DH;
+#pragma unroll
+                for (int sg = 0; sg < 4; ++sg) {
+                    float4 v = make_float4(acc[2 * sg][hh] * gv, acc[2 * sg][2 + hh] * gv,
+                                           acc[2 * sg + 1][hh] * gv, acc[2 * sg + 1][2 + hh] * gv);
+                    *reinterpret_cast<float4*>(a + 32 * sg + 4 * g) = v;
+                }
+            }
+        }
+    };
+
+    int it = 0;
+    for (int64_t i = i0; i < i1; ++i, ++it) {
+        const int bh = (int)(i / p.T), tl = (int)(i % p.T);
+        if (bh != cur) {
+            if (cur >= 0) flush(cur);
+            cur = bh;
+            m0 = m1 = -INFINITY; l0 = l1 = 0.f;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+            const int b = bh / p.Hkv, kvh = bh % p.Hkv;
+            const __nv_bfloat16* qp = p.q + b * p.q_sb + (int64_t)(kvh * G + g) * p.q_sh;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    uint32_t v = 0;
+                    if (g < G) {
+                        const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(qp + 16 * k + 8 * hf + 2 * tq);
+                        v = h2_as_u32(__float22half2_rn(__bfloat1622float2(b2)));
+                    }
+                    qB[k][hf] = v;
+                }
+            }
+        }
+        const int s = it % NST;
+        if (!mbar_wait_bounded(&ctl->full[s], (it / NST) & 1)) {
+            set_err(p.err, KIVI_ERR_TIMEOUT);
+            ctl->abort = 1;
+        }
+        if (ctl->abort) break;
+        uint8_t* st = stages + s * L::BYTES;
+        const uint8_t* vs_base = st + L::VS;
+        if (FMT == FMT_NVFP4) {
+            // my 32 tokens' e4m3 V scales -> fp16 rows [token][8] (per-warp buffer)
+            __half* vw = scv + warp * 32 * 8;
+            const uint2 raw = *reinterpret_cast<const uint2*>(st + L::VS + (32 * warp + lane) * 8);
+            __syncwarp();
+            *reinterpret_cast<uint4*>(vw + lane * 8) =
+                make_uint4(e4m3x2_to_h2((uint16_t)raw.x), e4m3x2_to_h2((uint16_t)(raw.x >> 16)),
+                           e4m3x2_to_h2((uint16_t)raw.y), e4m3x2_to_h2((uint16_t)(raw.y >> 16)));
+            __syncwarp();
+            vs_base = reinterpret_cast<const uint8_t*>(vw) - 32 * warp * 16;
+        }
+
+        const int t_span = tl * TILE + 32 * warp;      // first token of my span
+        const int limit = p.n_full - t_span;           // valid tokens in my span
+        if (limit > 0) {
+            // ------------------------------ QK^T ------------------------------
+            float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t kc_s = smem_u32(st + L::KC), ks_s = smem_u32(st + L::KS);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t row = 32 * j + lane;
+                uint32_t r0, r1, r2, r3, s0, s1, s2, s3;
+                ldsm_x4_t(kc_s + swz64(row, warp), r0, r1, r2, r3);
+                ldsm_x4_t(ks_s + row * 16, s0, s1, s2, s3);
+                if (FMT == FMT_NVFP4) {
+                    // raw e4m3 rows of 16 pages: u16 column = page pair; pick my page
+                    const int srcn = ((((tl & 1) * 4) + warp) << 2) | tq;
+                    const uint32_t sel = (uint32_t)(g >> 2);
+                    const uint32_t pm = ((2u + sel) << 4) | sel;
+                    s0 = e4m3x2_to_h2((uint16_t)__byte_perm(__shfl_sync(0xffffffffu, s0, srcn), 0, pm));
+                    s1 = e4m3x2_to_h2((uint16_t)__byte_perm(__shfl_sync(0xffffffffu, s1, srcn), 0, pm));
+                    s2 = e4m3x2_to_h2((uint16_t)__byte_perm(__shfl_sync(0xffffffffu, s2, srcn), 0, pm));
+                    s3 = e4m3x2_to_h2((uint16_t)__byte_perm(__shfl_sync(0xffffffffu, s3, srcn), 0, pm));
+                } else {
+                    s0 = __shfl_sync(0xffffffffu, s0, src_k);
+                    s1 = __shfl_sync(0xffffffffu, s1, src_k);
+                    s2 = __shfl_sync(0xffffffffu, s2, src_k);
+                    s3 = __shfl_sync(0xffffffffu, s3, src_k);
+                }
+                mma_pair<FMT>(ca, cb, r0, r1, s0, s1, qB[2 * j][0], qB[2 * j][1]);
+                mma_pair<FMT>(ca, cb, r2, r3, s2, s3, qB[2 * j + 1][0], qB[2 * j + 1][1]);
+            }
+            // ----------------------------- softmax ----------------------------
+            // ca: tokens 4g (c0,c1), 4g+1 (c2,c3); cb: 4g+2, 4g+3; heads 2tq(+1)
+            float x[8] = {ca[0], ca[2], cb[0], cb[2], ca[1], ca[3], cb[1], cb[3]};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[e] *= p.scale2;
+            if (limit < 32) {
+                const int tk[4] = {4 * g, 4 * g + 1, 4 * g + 2, 4 * g + 3};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) if (tk[e & 3] >= limit) x[e] = -INFINITY;
+            }
+            float mx0 = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+            float mx1 = fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7]));
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+            }
+            const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+            // mn == -inf only if every token so far is masked (cannot happen
+            // for limit > 0, kept for safety): use 0 as the reference point.
+            const float r0 = (mn0 == -INFINITY) ? 0.f : mn0, r1 = (mn1 == -INFINITY) ? 0.f : mn1;
+            const float al0 = exp2f(m0 - r0), al1 = exp2f(m1 - r1);
+            m0 = mn0; m1 = mn1;
+            float pr[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) { pr[e] = exp2f(x[e] - r0); pr[4 + e] = exp2f(x[4 + e] - r1); }
+            l0 = l0 * al0 + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
+            l1 = l1 * al1 + ((pr[4] + pr[5]) + (pr[6] + pr[7]));
+            if (!__all_sync(0xffffffffu, al0 == 1.f && al1 == 1.f)) {
+#pragma unroll
+                for (int t = 0; t < 8; ++t) { acc[t][0] *= al0; acc[t][2] *= al0; acc[t][1] *= al1; acc[t][3] *= al1; }
+            }
+            // stage P as fp16 [head][token] for the PV B-fragments
+            __syncwarp();
+            *reinterpret_cast<uint2*>(pb + (2 * tq) * PB_PITCH + 4 * g) =
+                make_uint2(h2_as_u32(__floats2half2_rn(pr[0], pr[1])), h2_as_u32(__floats2half2_rn(pr[2], pr[3])));
+            *reinterpret_cast<uint2*>(pb + (2 * tq + 1) * PB_PITCH + 4 * g) =
+                make_uint2(h2_as_u32(__floats2half2_rn(pr[4], pr[5])), h2_as_u32(__floats2half2_rn(pr[6], pr[7])));
+            __syncwarp();
+            // ------------------------------- PV -------------------------------
+            const uint32_t vc_s = smem_u32(st + L::VC), vs_s = smem_u32(vs_base);
+            uint32_t vr[4];
+            ldsm_x4_t(vs_s + (32 * warp + lane) * 16, vr[0], vr[1], vr[2], vr[3]);
+            const bool mask_v = limit < 32;
+#pragma unroll
+            for (int lam = 0; lam < 2; ++lam) {
+                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pb + g * PB_PITCH + 16 * lam + 2 * tq);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(pb + g * PB_PITCH + 16 * lam + 8 + 2 * tq);
+#pragma unroll
+                for (int sp = 0; sp < 2; ++sp) {          // segment pairs (2sp, 2sp+1)
+                    const uint32_t trow = 32 * warp + 16 * lam + 8 * ((lane >> 3) & 1) + (lane & 7);
+                    const uint32_t chunk = 2 * sp + (lane >> 4);
+                    uint32_t w0, w1, w2, w3;
+                    ldsm_x4_t(vc_s + swz64(trow, chunk), w0, w1, w2, w3);
+#pragma unroll
+                    for (int hs = 0; hs < 2; ++hs) {
+                        const int sg = 2 * sp + hs;
+                        const int src_v = ((2 * sg + (g >> 2)) << 2) | tq;
+                        uint32_t sa = __shfl_sync(0xffffffffu, vr[2 * lam], src_v);
+                        uint32_t sb = __shfl_sync(0xffffffffu, vr[2 * lam + 1], src_v);
+                        if (mask_v) {
+                            const int t0 = 16 * lam + 2 * tq;     // tokens of sa: t0, t0+1; sb: t0+8, t0+9
+                            sa = (t0 + 1 < limit) ? sa : (t0 < limit ? (sa & 0x0000FFFFu) : 0u);
+                            sb = (t0 + 9 < limit) ? sb : (t0 + 8 < limit ? (sb & 0x0000FFFFu) : 0u);
+                        }
+                        mma_pair<FMT>(acc[2 * sg], acc[2 * sg + 1], hs ? w2 : w0, hs ? w3 : w1, sa, sb, b0, b1);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->empty[s]);
+    }
+    if (cur >= 0 && !ctl->abort) flush(cur);
+}
+
+// ---------------------------------------------------------------------------
+// Generic path (any D multiple of 16 up to 256, any group <= 16, any strides):
+// same work partition and partial-record format as the fast path, CUDA-core
+// arithmetic, one warp streams its 32-token span of each tile token by token.
+// ---------------------------------------------------------------------------
+constexpr int GEN_MAXG = 16, GEN_MAXC = 8;
+
+template <int FMT>
+__device__ __forceinline__ float gen_scale(const void* s, int64_t idx, float g) {
+    if (FMT == FMT_NVFP4) return e4m3_to_f32(reinterpret_cast<const uint8_t*>(s)[idx]) * g;
+    return __half2float(__ushort_as_half(reinterpret_cast<const uint16_t*>(s)[idx]));
+}
+template <int FMT>
+__device__ __forceinline__ float gen_code(uint32_t nib) {
+    if (FMT == FMT_NVFP4) { float l = e2m1_level(nib & 7); return (nib & 8) ? -l : l; }
+    return (float)sx4((int)nib);
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeParams p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x, G = p.G, D = p.D, ND = D / BLK;
+    const int64_t i0 = tile_start(c, p.W, p.N), i1 = tile_start(c + 1, p.W, p.N);
+    const float sc2 = p.sm_scale * 1.4426950408889634f;
+    float q[GEN_MAXG][GEN_MAXC], acc[GEN_MAXG][GEN_MAXC], m[GEN_MAXG], l[GEN_MAXG];
+    int cur = -1;
+    auto flush = [&](int bh) {
+        const int64_t slot = ((int64_t)(c + bh) * NWARP_C + warp) * G;
+        for (int h = 0; h < G; ++h) {
+            if (lane == 0) { p.part_m[slot + h] = m[h]; p.part_l[slot + h] = l[h]; }
+            for (int e = 0; e < GEN_MAXC; ++e) {
+                const int d = lane + 32 * e;
+                if (d < D) p.part_acc[(slot + h) * D + d] = acc[h][e];
+            }
+        }
+    };
+    for (int64_t i = i0; i < i1; ++i) {
+        const int bh = (int)(i / p.T), tl = (int)(i % p.T);
+        if (bh != cur) {
+            if (cur >= 0) flush(cur);
+            cur = bh;
+            const int b = bh / p.Hkv, kvh = bh % p.Hkv;
+            for (int h = 0; h < G; ++h) {
+                m[h] = -INFINITY; l[h] = 0.f;
+                const __nv_bfloat16* qp = p.q + b * p.q_sb + (int64_t)(kvh * G + h) * p.q_sh;
+                for (int e = 0; e < GEN_MAXC; ++e) {
+                    const int d = lane + 32 * e;
+                    q[h][e] = d < D ? __bfloat162float(qp[d]) : 0.f;
+                    acc[h][e] = 0.f;
+                }
+            }
+        }
+        const int t_end = min(p.n_full, tl * TILE + 32 * warp + 32);
+        for (int t = tl * TILE + 32 * warp; t < t_end; ++t) {
+            float kv[GEN_MAXC], vv[GEN_MAXC];
+            const int pg = t / BLK, j = t % BLK;
+            for (int e = 0; e < GEN_MAXC; ++e) {
+                const int d = lane + 32 * e;
+                kv[e] = vv[e] = 0.f;
+                if (d < D) {
+                    const int64_t kr = ((int64_t)bh * D + d) * p.k_np_stride + pg;
+                    const uint32_t kb = p.k_packed[kr * PACKB + j / 2];
+                    kv[e] = gen_code<FMT>((kb >> (4 * (j & 1))) & 0xF) * gen_scale<FMT>(p.k_scale, kr, p.g_k);
+                    const int64_t vr = ((int64_t)bh * p.v_s_stride + t) * ND + d / BLK;
+                    const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
+                    vv[e] = gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
+                }
+            }
+            for (int h = 0; h < G; ++h) {
+                float s = 0.f;
+                for (int e = 0; e < GEN_MAXC; ++e) s += q[h][e] * kv[e];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                s *= sc2;
+                const float mn = fmaxf(m[h], s);
+                const float al = exp2f(m[h] - mn), pr = exp2f(s - mn);
+                m[h] = mn;
+                l[h] = l[h] * al + pr;
+                for (int e = 0; e < GEN_MAXC; ++e) acc[h][e] = acc[h][e] * al + pr * vv[e];
+            }
+        }
+    }
+    if (cur >= 0) flush(cur);
+}
+
+// ---------------------------------------------------------------------------
+// Combine: bf16 hot tail + LSE merge of all partial slots of one kv-head.
+// mode 0 -> normalised bf16 out; mode 1 -> merged (m, l, acc) records.
+// ---------------------------------------------------------------------------
+template <int FMT>
+__global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int mode, __nv_bfloat16* out,
+                                                      float* m_out, float* l_out, float* acc_out) {
+    extern __shared__ float csm[];
+    const int bh = blockIdx.x, b = bh / p.Hkv, kvh = bh % p.Hkv;
+    const int G = p.G, D = p.D, ND = D / BLK, hot = p.hot;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* sc = csm;                  // [G][16] hot scores (log2 units)
+    const float sc2 = p.sm_scale * 1.4426950408889634f;
+    // hot-tail scores: one warp per (head, token) pair
+    for (int pr = warp; pr < G * hot; pr += 4) {
+        const int h = pr / hot, j = pr % hot;
+        const __nv_bfloat16* qp = p.q + b * p.q_sb + (int64_t)(kvh * G + h) * p.q_sh;
+        const __nv_bfloat16* kp = p.k_hot + ((int64_t)bh * p.hot_stride + j) * D;
+        float s = 0.f;
+        for (int d = lane; d < D; d += 32) s += __bfloat162float(qp[d]) * __bfloat162float(kp[d]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) sc[h * 16 + j] = s * sc2;
+    }
+    __syncthreads();
+    // partial slots of this head
+    int c_lo = 0, c_hi = -1;
+    if (p.W > 0) {
+        const int64_t a0 = (int64_t)bh * p.T, a1 = a0 + p.T;
+        int64_t cc = (a0 * p.N) / p.W;
+        while (cc + 1 < p.N && tile_start(cc + 1, p.W, p.N) <= a0) ++cc;
+        while (cc > 0 && tile_start(cc, p.W, p.N) > a0) --cc;
+        c_lo = (int)cc;
+        int64_t ch = cc;
+        while (ch + 1 < p.N && tile_start(ch + 1, p.W, p.N) < a1) ++ch;
+        c_hi = (int)ch;
+    }
+    for (int h = 0; h < G; ++h) {
+        float mh = -INFINITY;
+        for (int j = 0; j < hot; ++j) mh = fmaxf(mh, sc[h * 16 + j]);
+        float M = mh;
+        for (int cc = c_lo; cc <= c_hi; ++cc)
+            for (int w = 0; w < NWARP_C; ++w)
+                M = fmaxf(M, p.part_m[((int64_t)(cc + bh) * NWARP_C + w) * G + h]);
+        const float Mr = (M == -INFINITY) ? 0.f : M;
+        float Lsum = 0.f;
+        for (int cc = c_lo; cc <= c_hi; ++cc)
+            for (int w = 0; w < NWARP_C; ++w) {
+                const int64_t sl = ((int64_t)(cc + bh) * NWARP_C + w) * G + h;
+                Lsum += p.part_l[sl] * exp2f(p.part_m[sl] - Mr);
+            }
+        for (int j = 0; j < hot; ++j) Lsum += exp2f(sc[h * 16 + j] - Mr);
+        const int64_t row = (int64_t)b * p.Hq + kvh * G + h;
+        for (int d = threadIdx.x; d < D; d += blockDim.x) {
+            float a = 0.f;
+            for (int cc = c_lo; cc <= c_hi; ++cc)
+                for (int w = 0; w < NWARP_C; ++w) {
+                    const int64_t sl = ((int64_t)(cc + bh) * NWARP_C + w) * G + h;
+                    a += p.part_acc[sl * D + d] * exp2f(p.part_m[sl] - Mr);
+                }
+            for (int j = 0; j < hot; ++j) {
+                const int64_t vr = ((int64_t)bh * p.v_s_stride + p.n_full + j) * ND + d / BLK;
+                const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
+                const float v = gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
+                a += exp2f(sc[h * 16 + j] - Mr) * v;
+            }
+            if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Lsum);
+            else acc_out[row * D + d] = a;
+        }
+        if (mode == 1 && threadIdx.x == 0) { m_out[row] = M; l_out[row] = Lsum; }
+    }
+}
+
+// Merge R records [R, rows], [R, rows, D] -> bf16 [rows, D].
+__global__ void __launch_bounds__(128) lse_merge_kernel(const float* m, const float* l, const float* acc,
+                                                        int R, int rows, int D, __nv_bfloat16* out) {
+    const int row = blockIdx.x;
+    float M = -INFINITY;
+    for (int r = 0; r < R; ++r) M = fmaxf(M, m[(int64_t)r * rows + row]);
+    const float Mr = (M == -INFINITY) ? 0.f : M;
+    float Ls = 0.f;
+    for (int r = 0; r < R; ++r) Ls += l[(int64_t)r * rows + row] * exp2f(m[(int64_t)r * rows + row] - Mr);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float a = 0.f;
+        for (int r = 0; r < R; ++r)
+            a += acc[((int64_t)r * rows + row) * D + d] * exp2f(m[(int64_t)r * rows + row] - Mr);
+        out[(int64_t)row * D + d] = __float2bfloat16_rn(a / Ls);
+    }
+}
+
+}  // namespace kivi
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+using namespace kivi;
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D map over [rows, cols] of `elem` bytes each, row pitch `pitch_bytes`.
+bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t cols, uint64_t rows,
+              uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {pitch_bytes};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t es[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct DevInfo { int sms = 0; int occ[2] = {0, 0}; };
+DevInfo& dev_info(int dev) {
+    static DevInfo info[64];
+    return info[dev & 63];
+}
+
+template <int FMT>
+size_t fast_smem_bytes() {
+    return 1024 + NST * StageLayout<FMT>::BYTES + NWARP_C * 8 * PB_PITCH * 2 +
+           (FMT == FMT_NVFP4 ? NWARP_C * 32 * 8 * 2 : 0) + sizeof(SmemCtl) + 16;
+}
+
+int num_sms(int* dev_out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    DevInfo& di = dev_info(dev);
+    if (!di.sms) cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (dev_out) *dev_out = dev;
+    return di.sms;
+}
+
+template <int FMT>
+int fast_occupancy(int dev) {
+    DevInfo& di = dev_info(dev);
+    const int k = (FMT == FMT_NVFP4) ? 1 : 0;
+    if (!di.occ[k]) {
+        const size_t smem = fast_smem_bytes<FMT>();
+        if (cudaFuncSetAttribute(decode_fast_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem) != cudaSuccess)
+            return 0;
+        int occ = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_fast_kernel<FMT>, NTHREADS, smem) !=
+            cudaSuccess)
+            return 0;
+        di.occ[k] = occ > 0 ? occ : 1;
+    }
+    return di.occ[k];
+}
+
+constexpr int MAX_CTAS_PER_SM = 4;
+
+struct Plan { int T; int64_t W; int N; int64_t slots; };
+
+Plan make_plan(int BH, int n_full, int sms, int ctas_per_sm) {
+    Plan pl;
+    pl.T = (n_full + TILE - 1) / TILE;
+    pl.W = (int64_t)BH * pl.T;
+    int64_t cap = (int64_t)sms * (ctas_per_sm < MAX_CTAS_PER_SM ? ctas_per_sm : MAX_CTAS_PER_SM);
+    pl.N = (int)(pl.W < cap ? pl.W : cap);
+    pl.slots = pl.W > 0 ? (int64_t)(pl.N + BH) * NWARP_C : 0;
+    return pl;
+}
+
+int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,
+                const void* k_scale, int k_np_stride, const void* k_hot, int hot_stride,
+                const uint8_t* v_packed, const void* v_scale, int v_s_stride, int B, int Hq, int Hkv,
+                int S, int D, int fmt, float sm_scale, float g_k, float g_v, void* out, float* m_out,
+                float* l_out, float* acc_out, float* work, int64_t work_floats, int* err,
+                kivi_stream_t stream) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || S < 0 || D <= 0 || D % BLK) return KIVI_ERR_ARG;
+    if (fmt != FMT_INT4 && fmt != FMT_NVFP4) return KIVI_ERR_ARG;
+    const int G = Hq / Hkv, BH = B * Hkv;
+    const int n_full = (S / BLK) * BLK, hot = S - n_full;
+    if (k_np_stride < n_full / BLK || v_s_stride < S || (hot > 0 && hot_stride < hot)) return KIVI_ERR_ARG;
+    if (!q || (!out && mode == 0) || (mode == 1 && (!m_out || !l_out || !acc_out))) return KIVI_ERR_ARG;
+    if (n_full > 0 && (!k_packed || !k_scale)) return KIVI_ERR_ARG;
+    if (S > 0 && (!v_packed || !v_scale)) return KIVI_ERR_ARG;
+    if (hot > 0 && !k_hot) return KIVI_ERR_ARG;
+    int dev = 0;
+    const int sms = num_sms(&dev);
+    if (!sms) return record_cuda_error(cudaGetLastError());
+
+    const bool fast = D == DH && G <= 8 && k_np_stride % 16 == 0 && v_s_stride % 16 == 0 &&
+                      (uintptr_t)k_packed % 16 == 0 && (uintptr_t)k_scale % 16 == 0 &&
+                      (uintptr_t)v_packed % 16 == 0 && (uintptr_t)v_scale % 16 == 0 &&
+                      q_sh % 2 == 0 && (uintptr_t)q % 4 == 0 && n_full > 0 &&
+                      (int64_t)BH * v_s_stride < (1LL << 31) && (int64_t)BH * D < (1LL << 31);
+    if (!fast && (G > GEN_MAXG || D > 32 * GEN_MAXC)) return KIVI_ERR_UNSUPPORTED;
+    const int occ = fast ? (fmt == FMT_NVFP4 ? fast_occupancy<FMT_NVFP4>(dev) : fast_occupancy<FMT_INT4>(dev)) : 4;
+    if (!occ) return record_cuda_error(cudaGetLastError());
+    const Plan pl = make_plan(BH, n_full, sms, occ);
+    const int64_t need = pl.slots * G * (2 + (int64_t)D);
+    if (need > 0 && (!work || work_floats < need)) return KIVI_ERR_ARG;
+
+    DecodeParams p{};
+    p.q = reinterpret_cast<const __nv_bfloat16*>(q); p.q_sb = q_sb; p.q_sh = q_sh;
+    p.k_packed = k_packed; p.k_scale = k_scale; p.k_np_stride = k_np_stride;
+    p.k_hot = reinterpret_cast<const __nv_bfloat16*>(k_hot); p.hot_stride = hot_stride;
+    p.v_packed = v_packed; p.v_scale = v_scale; p.v_s_stride = v_s_stride;
+    p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.S = S; p.D = D; p.n_full = n_full; p.hot = hot;
+    p.sm_scale = sm_scale; p.g_k = g_k; p.g_v = g_v;
+    p.scale2 = sm_scale * 1.4426950408889634f * (fmt == FMT_NVFP4 ? g_k : 1.0f);
+    p.T = pl.T; p.W = pl.W; p.N = pl.N;
+    p.part_m = work; p.part_l = work + pl.slots * G; p.part_acc = work + 2 * pl.slots * G;
+    p.err = err;
+    cudaStream_t st = (cudaStream_t)stream;
+
+    if (pl.W > 0) {
+        if (fast) {
+            CUtensorMap tkc, tks, tvc, tvs;
+            const uint64_t rows_k = (uint64_t)BH * DH, rows_v = (uint64_t)BH * v_s_stride;
+            bool ok = make_map(&tkc, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_packed, (uint64_t)k_np_stride * 8, rows_k,
+                               (uint64_t)k_np_stride * 8, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B) &&
+                      make_map(&tvc, CU_TENSOR_MAP_DATA_TYPE_UINT8, v_packed, 64, rows_v, 64, 64, 128,
+                               CU_TENSOR_MAP_SWIZZLE_64B);
+            if (fmt == FMT_NVFP4) {
+                ok = ok && make_map(&tks, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_scale, (uint64_t)k_np_stride, rows_k,
+                                    (uint64_t)k_np_stride, 16, 128, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                     make_map(&tvs, CU_TENSOR_MAP_DATA_TYPE_UINT8, v_scale, 16, rows_v / 2, 16, 16, 64,
+                              CU_TENSOR_MAP_SWIZZLE_NONE);
+            } else {
+                ok = ok && make_map(&tks, CU_TENSOR_MAP_DATA_TYPE_UINT16, k_scale, (uint64_t)k_np_stride, rows_k,
+                                    (uint64_t)k_np_stride * 2, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                     make_map(&tvs, CU_TENSOR_MAP_DATA_TYPE_UINT16, v_scale, 8, rows_v, 16, 8, 128,
+                              CU_TENSOR_MAP_SWIZZLE_NONE);
+            }
+            if (!ok) return KIVI_ERR_CUDA;
+            if (fmt == FMT_NVFP4)
+                decode_fast_kernel<FMT_NVFP4><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>(), st>>>(tkc, tks, tvc, tvs, p);
+            else
+                decode_fast_kernel<FMT_INT4><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>(), st>>>(tkc, tks, tvc, tvs, p);
+        } else {
+            if (fmt == FMT_NVFP4) decode_generic_kernel<FMT_NVFP4><<<pl.N, 128, 0, st>>>(p);
+            else decode_generic_kernel<FMT_INT4><<<pl.N, 128, 0, st>>>(p);
+        }
+        int e = check_launch();
+        if (e) return e;
+    }
+    const size_t csm = (size_t)G * 16 * sizeof(float);
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
+    if (fmt == FMT_NVFP4) combine_kernel<FMT_NVFP4><<<BH, 128, csm, st>>>(p, mode, o, m_out, l_out, acc_out);
+    else combine_kernel<FMT_INT4><<<BH, 128, csm, st>>>(p, mode, o, m_out, l_out, acc_out);
+    return check_launch();
+}
+
+}  // namespace
+
+extern "C" int64_t kivi_decode_workspace_floats(int B, int Hq, int Hkv, int S, int D) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || S < 0 || D <= 0) return 0;
+    int sms = num_sms(nullptr);
+    if (!sms) sms = 148;
+    const Plan pl = make_plan(B * Hkv, (S / BLK) * BLK, sms, MAX_CTAS_PER_SM);
+    return pl.slots * (Hq / Hkv) * (2 + (int64_t)D);
+}
+
+extern "C" int kivi_decode(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,
+                           const void* k_scale, int k_np_stride, const void* k_hot, int hot_stride,
+                           const uint8_t* v_packed, const void* v_scale, int v_s_stride, int B, int Hq,
+                           int Hkv, int S, int D, int fmt, float sm_scale, float g_k, float g_v, void* out,
+                           float* work, int64_t work_floats, int* err, kivi_stream_t stream) {
+    return decode_impl(0, q, q_sb, q_sh, k_packed, k_scale, k_np_stride, k_hot, hot_stride, v_packed, v_scale,
+                       v_s_stride, B, Hq, Hkv, S, D, fmt, sm_scale, g_k, g_v, out, nullptr, nullptr, nullptr,
+                       work, work_floats, err, stream);
+}
+
+extern "C" int kivi_decode_partial(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,
+                                   const void* k_scale, int k_np_stride, const void* k_hot, int hot_stride,
+                                   const uint8_t* v_packed, const void* v_scale, int v_s_stride, int B,
+                                   int Hq, int Hkv, int S, int D, int fmt, float sm_scale, float g_k,
+                                   float g_v, float* m_out, float* l_out, float* acc_out, float* work,
+                                   int64_t work_floats, int* err, kivi_stream_t stream) {
+    return decode_impl(1, q, q_sb, q_sh, k_packed, k_scale, k_np_stride, k_hot, hot_stride, v_packed, v_scale,
+                       v_s_stride, B, Hq, Hkv, S, D, fmt, sm_scale, g_k, g_v, nullptr, m_out, l_out, acc_out,
+                       work, work_floats, err, stream);
+}
+
+extern "C" int kivi_lse_merge(const float* m, const float* l, const float* acc, int R, int rows, int D,
+                              void* out, kivi_stream_t stream) {
+    if (R <= 0 || rows < 0 || D <= 0 || !m || !l || !acc || !out) return KIVI_ERR_ARG;
+    if (rows == 0) return KIVI_OK;
+    lse_merge_kernel<<<rows, 128, 0, (cudaStream_t)stream>>>(m, l, acc, R, rows, D,
+                                                             reinterpret_cast<__nv_bfloat16*>(out));
+    return check_launch();
+}

@@ -1,0 +1,128 @@
+"""ctypes binding of libkivi_sm100.so (the C ABI in include/kivi_sm100.h).
+
+PyTorch is used only for device memory and the current CUDA stream; every
+kernel comes from the library.  There is no CPU or Triton fallback: if the
+library cannot be loaded, or the tensors are not on a CUDA device, the call
+raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(_HERE), "libkivi_sm100.so")
+
+FMT = {"int4": 0, "int3": 1, "nvfp4": 2}
+CALIB = {"absmax": 0, "mse": 1}
+LAYOUT = {"headdim": 0, "channel": 1}
+DTYPE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class KiviError(RuntimeError):
+    """A nonzero status returned by libkivi_sm100."""
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise ImportError(
+                    f"{LIB_PATH} is missing: build it with `python poolside-hackathon_b200/build.py` "
+                    "(this package has no CPU fallback)")
+            L = ctypes.CDLL(LIB_PATH)
+            P, I, F, I64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int64
+            L.kivi_status_string.restype = ctypes.c_char_p
+            L.kivi_status_string.argtypes = [I]
+            L.kivi_version.restype = I
+            L.kivi_last_cuda_error.restype = I
+            L.kivi_store.argtypes = [P, P, I, I64, I64, I64, I64, I64, I64, I, I, I, I, I, I, I, P, I, F, F,
+                                     P, P, I, I, P, P, I, I, P]
+            L.kivi_dequant.argtypes = [P, P, I, P, P, I, I, I, I, I, F, F, P, P, I64, I64, I64, P]
+            L.kivi_roundtrip.argtypes = [P, P, I, I, I, I, I, I, I, P, I, P]
+            L.kivi_calibrate.argtypes = [P, I64, I, I, P, I, P, P]
+            L.kivi_decode_workspace_floats.restype = I64
+            L.kivi_decode_workspace_floats.argtypes = [I, I, I, I, I]
+            L.kivi_decode.argtypes = [P, I64, I64, P, P, I, P, I, P, P, I, I, I, I, I, I, I, F, F, F,
+                                      P, P, I64, P, P]
+            L.kivi_decode_partial.argtypes = [P, I64, I64, P, P, I, P, I, P, P, I, I, I, I, I, I, I, F, F,
+                                              F, P, P, P, P, I64, P, P]
+            L.kivi_lse_merge.argtypes = [P, P, P, I, I, I, P, P]
+            _lib = L
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        L = lib()
+        msg = L.kivi_status_string(status).decode()
+        extra = f" (cudaError {L.kivi_last_cuda_error()})" if status == 4 else ""
+        raise KiviError(f"{what}: {msg}{extra}")
+
+
+def ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def stream_of(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def require_cuda(*ts) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("int4_kivi kernels run on CUDA tensors only (no CPU fallback)")
+
+
+# -------- per-device cached helpers (alpha grid, error flag, workspace) --------
+_alpha_cache: dict = {}
+_err_cache: dict = {}
+_work_cache: dict = {}
+
+
+def alphas(device, n_alphas: int) -> torch.Tensor:
+    """linspace(0.5, 1.0, n) built on the CPU (bit-identical to kv_quant's grid),
+    copied once per device."""
+    key = (str(device), n_alphas)
+    a = _alpha_cache.get(key)
+    if a is None:
+        a = torch.linspace(0.5, 1.0, n_alphas, dtype=torch.float32).to(device)
+        _alpha_cache[key] = a
+    return a
+
+
+def err_flag(device) -> torch.Tensor:
+    key = str(device)
+    e = _err_cache.get(key)
+    if e is None:
+        e = torch.zeros(1, dtype=torch.int32, device=device)
+        _err_cache[key] = e
+    return e
+
+
+def device_status(device) -> int:
+    """Read (and clear) the device-side timeout flag; synchronises."""
+    e = err_flag(device)
+    v = int(e.item())
+    if v:
+        e.zero_()
+    return v
+
+
+def workspace(device, n_floats: int) -> torch.Tensor:
+    """Grow-only scratch buffer for decode partials, one per (device, stream)."""
+    key = (str(device), torch.cuda.current_stream(device).cuda_stream)
+    w = _work_cache.get(key)
+    if w is None or w.numel() < n_floats:
+        w = torch.empty(max(n_floats, 1), dtype=torch.float32, device=device)
+        _work_cache[key] = w
+    return w

@@ -1,0 +1,166 @@
+"""Fused INT4-KIVI flash-decode attention (the reference's int4_kivi/decode.py
+API, decode.py:177-533), running on libkivi_sm100's split-K decode kernels.
+
+Single-query decode attention that reads the packed cache directly and
+dequantises K and V in registers, with a log-sum-exp merge of the splits and
+the bf16 hot-page tail folded into the merge.  The `split` / `block_n`
+arguments of the reference are accepted for API compatibility; the B200
+kernel sizes its own persistent grid from the SM count.
+
+Public (unchanged signatures):
+  kivi_decode_attention(q [Hq,1,D], cache, sm_scale=None, block_n=64) -> [Hq,1,D]
+  kivi_decode_attention_batched(q [B,Hq,D], stacked, n_qh, sm_scale=None, split=8, block_n=64)
+  kivi_decode_attention_gqa(q [B,Hq,D], stacked, n_qh, sm_scale=None, split=16, block_n=64)
+  stack_caches([KIVICache, ...]) -> dict
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from . import _native as N
+from .cache import BLOCK, PACK, KIVICache, alloc_packed, cache_geometry
+
+
+def _stacked_geometry(st: dict) -> tuple[int, int, dict]:
+    """(page stride, token stride, tensors) for a stacked dict, re-laid out into
+    aligned buffers if needed (slow path for externally built dicts)."""
+    class _V:  # attribute view for cache_geometry
+        pass
+    v = _V()
+    for f in ("k_packed", "k_scale", "v_packed", "v_scale"):
+        setattr(v, f, st[f])
+    try:
+        nps, ss = cache_geometry(v)
+        return nps, ss, st
+    except ValueError:
+        BH, D, NP, _ = st["k_packed"].shape
+        S = st["v_packed"].shape[1]
+        kp, ks, vp, vs = alloc_packed(BH, S, D, st["k_packed"].device, st["k_scale"].dtype)
+        kp[:, :, :NP].copy_(st["k_packed"]); ks[:, :, :NP].copy_(st["k_scale"])
+        vp[:, :S].copy_(st["v_packed"]); vs[:, :S].copy_(st["v_scale"])
+        out = dict(st, k_packed=kp[:, :, :NP], k_scale=ks[:, :, :NP], v_packed=vp[:, :S], v_scale=vs[:, :S])
+        return kp.shape[2], vp.shape[1], out
+
+
+def decode_packed(q: Tensor, st: dict, n_qh: int, sm_scale: Optional[float] = None,
+                  fmt: str = "int4", g_k: float = 1.0, g_v: float = 1.0,
+                  out: Optional[Tensor] = None, partial: bool = False):
+    """Core entry: q [B, n_qh, D] bf16 over a stacked packed cache (B*H heads).
+
+    Returns bf16 [B, n_qh, D], or with partial=True the merged per-row state
+    (m [B*n_qh] in log2 units, l [B*n_qh], acc [B*n_qh, D]) for a cross-GPU
+    log-sum-exp merge."""
+    B, H, S, D = st["B"], st["H"], st["S"], st["D"]
+    N.require_cuda(q, st["v_packed"])
+    assert q.shape == (B, n_qh, D), f"q must be [B={B}, n_qh={n_qh}, D={D}]"
+    assert n_qh % H == 0, "n_q_heads must be a multiple of n_kv_heads"
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    q = q.to(torch.bfloat16)
+    if q.stride(2) != 1:
+        q = q.contiguous()
+    nps, ss, st = _stacked_geometry(st)
+    khot = st["k_hot"]
+    if khot.shape[1] and khot.stride(2) != 1 or khot.shape[1] and khot.stride(1) != D:
+        khot = khot.contiguous()
+    hot_stride = khot.shape[1]
+    dev = q.device
+    need = N.lib().kivi_decode_workspace_floats(B, n_qh, H, S, D)
+    work = N.workspace(dev, need)
+    err = N.err_flag(dev)
+    L = N.lib()
+    if partial:
+        m = torch.empty(B * n_qh, dtype=torch.float32, device=dev)
+        l = torch.empty(B * n_qh, dtype=torch.float32, device=dev)
+        acc = torch.empty(B * n_qh, D, dtype=torch.float32, device=dev)
+        rc = L.kivi_decode_partial(
+            N.ptr(q), q.stride(0), q.stride(1), N.ptr(st["k_packed"]), N.ptr(st["k_scale"]), nps,
+            N.ptr(khot) if hot_stride else None, hot_stride, N.ptr(st["v_packed"]), N.ptr(st["v_scale"]), ss,
+            B, n_qh, H, S, D, N.FMT[fmt], sm_scale, g_k, g_v, N.ptr(m), N.ptr(l), N.ptr(acc),
+            N.ptr(work), work.numel(), N.ptr(err), N.stream_of(q))
+        N.check(rc, "kivi_decode_partial")
+        return m, l, acc
+    if out is None:
+        out = torch.empty((B, n_qh, D), dtype=torch.bfloat16, device=dev)
+    rc = L.kivi_decode(
+        N.ptr(q), q.stride(0), q.stride(1), N.ptr(st["k_packed"]), N.ptr(st["k_scale"]), nps,
+        N.ptr(khot) if hot_stride else None, hot_stride, N.ptr(st["v_packed"]), N.ptr(st["v_scale"]), ss,
+        B, n_qh, H, S, D, N.FMT[fmt], sm_scale, g_k, g_v, N.ptr(out), N.ptr(work), work.numel(),
+        N.ptr(err), N.stream_of(q))
+    N.check(rc, "kivi_decode")
+    return out
+
+
+def _single(cache) -> dict:
+    return dict(k_packed=cache.k_packed, k_scale=cache.k_scale, k_hot=cache.k_hot,
+                v_packed=cache.v_packed, v_scale=cache.v_scale, H=cache.H, S=cache.S, D=cache.D,
+                NP=cache.k_packed.shape[2], ND=cache.v_packed.shape[2], B=1)
+
+
+def kivi_decode_attention(q: Tensor, cache: KIVICache, sm_scale: float | None = None,
+                          block_n: int = 64) -> Tensor:
+    """Fused decode attention over a packed INT4-KIVI cache.
+
+    q: bf16 [n_q_heads, 1, D]; cache: KIVICache of one sequence.
+    Returns bf16 [n_q_heads, 1, D]."""
+    assert q.is_cuda and cache.k_packed.is_cuda
+    n_qh, D = q.shape[0], cache.D
+    assert q.shape[-1] == D
+    assert n_qh % cache.H == 0, "n_q_heads must be a multiple of n_kv_heads"
+    out = decode_packed(q.reshape(1, n_qh, D), _single(cache), n_qh, sm_scale,
+                        fmt=cache.fmt, g_k=getattr(cache, "g_k", 1.0), g_v=getattr(cache, "g_v", 1.0))
+    return out.reshape(n_qh, 1, D)
+
+
+def kivi_decode_attention_batched(q: Tensor, stacked: dict, n_qh: int, sm_scale: float | None = None,
+                                  split: int = 8, block_n: int = 64) -> Tensor:
+    """Split-K batched fused decode. q [B, n_qh, D] bf16, stacked from stack_caches."""
+    return decode_packed(q.reshape(stacked["B"], n_qh, stacked["D"]), stacked, n_qh, sm_scale,
+                         fmt=stacked.get("fmt", "int4"), g_k=stacked.get("g_k", 1.0), g_v=stacked.get("g_v", 1.0))
+
+
+def kivi_decode_attention_gqa(q: Tensor, stacked: dict, n_qh: int, sm_scale: float | None = None,
+                              split: int = 16, block_n: int = 64) -> Tensor:
+    """GQA-grouped split-K fused decode (fast path). q [B, n_qh, D] bf16."""
+    return kivi_decode_attention_batched(q, stacked, n_qh, sm_scale, split, block_n)
+
+
+def stack_caches(caches: list) -> dict:
+    """Stack per-sequence caches into batched packed tensors (B*H front dim).
+
+    Same keys and shapes as the reference (decode.py:480-491); the storage is
+    16-aligned so the TMA fast path applies.  All caches must share S."""
+    c0 = caches[0]
+    H, S, D = c0.H, c0.S, c0.D
+    assert all(c.S == S and c.H == H and c.D == D for c in caches), "stack_caches needs equal S"
+    B = len(caches)
+    NP = c0.k_packed.shape[2]
+    kp, ks, vp, vs = alloc_packed(B * H, S, D, c0.k_packed.device, c0.k_scale.dtype)
+    for b, c in enumerate(caches):
+        kp[b * H:(b + 1) * H, :, :NP].copy_(c.k_packed)
+        ks[b * H:(b + 1) * H, :, :NP].copy_(c.k_scale)
+        vp[b * H:(b + 1) * H, :S].copy_(c.v_packed)
+        vs[b * H:(b + 1) * H, :S].copy_(c.v_scale)
+    d = dict(k_packed=kp[:, :, :NP], k_scale=ks[:, :, :NP],
+             k_hot=torch.cat([c.k_hot for c in caches], dim=0),
+             v_packed=vp[:, :S], v_scale=vs[:, :S],
+             H=H, S=S, D=D, NP=NP, ND=c0.v_packed.shape[2], B=B)
+    if getattr(c0, "fmt", "int4") != "int4":
+        d.update(fmt=c0.fmt, g_k=c0.g_k, g_v=c0.g_v)
+    return d
+
+
+def lse_merge(m: Tensor, l: Tensor, acc: Tensor) -> Tensor:
+    """Merge R partial states m/l [R, rows], acc [R, rows, D] -> bf16 [rows, D]
+    (the reference's _combine_kernel semantics, decode.py:320-340)."""
+    R, rows = m.shape
+    D = acc.shape[-1]
+    m, l, acc = m.float().contiguous(), l.float().contiguous(), acc.float().contiguous()
+    out = torch.empty(rows, D, dtype=torch.bfloat16, device=m.device)
+    N.check(N.lib().kivi_lse_merge(N.ptr(m), N.ptr(l), N.ptr(acc), R, rows, D, N.ptr(out), N.stream_of(m)),
+            "kivi_lse_merge")
+    return out

@@ -1,0 +1,195 @@
+"""HuggingFace `Cache` backed by the INT4-KIVI store (the reference's
+int4_kivi/hf_cache.py:41-267 contract, on libkivi_sm100 kernels).
+
+Per layer: completed 16-token pages are frozen into INT4 with `store_kivi`
+semantics (K per-channel, V per-token); the partial page stays bf16.  `update`
+returns the full dequantised bf16 K/V `[1, H, S, D]` so the model's own
+attention runs unchanged.  Sliding-window layers keep only the trailing
+window, exactly as DynamicSlidingWindowLayer does.
+
+B200 differences (values returned are identical):
+  * frozen pages live in ONE capacity-backed packed cache per layer and new
+    pages are appended in place (`append_kivi`), instead of a list of chunks;
+  * the dequantised prefix is kept in a grow-only bf16 buffer and only newly
+    frozen pages are dequantised per step, instead of every chunk on every
+    step (hf_cache.py:137-154 re-dequantised O(S) bytes per token).
+"""
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from transformers.cache_utils import Cache, CacheLayerMixin
+
+from .cache import BLOCK, KIVICache, append_kivi, dequant_kivi, store_kivi
+
+
+class _Int4KiviLayer(CacheLayerMixin):
+    def __init__(self, k_calib: str = "mse", v_calib: str = "mse", is_sliding: bool = False,
+                 sliding_window: int | None = None):
+        super().__init__()
+        self.k_calib, self.v_calib = k_calib, v_calib
+        self.is_sliding, self.sliding_window = is_sliding, sliding_window
+        self.store: KIVICache | None = None     # frozen pages (S multiple of 16)
+        self.hot_k: Tensor | None = None        # [H, t < 16, D] bf16
+        self.hot_v: Tensor | None = None
+        self.cumulative_length = 0
+        self._offset = 0                        # frozen tokens dropped by sliding eviction
+        self._deq_k: Tensor | None = None       # [H, cap, D] bf16 dequantised frozen prefix
+        self._deq_v: Tensor | None = None
+        self._deq_len = 0
+
+    # -- transformers Cache layer interface ---------------------------------
+    def lazy_initialization(self, key_states: Tensor, value_states: Tensor) -> None:
+        self.dtype, self.device = key_states.dtype, key_states.device
+        self.is_initialized = True
+
+    def get_max_cache_shape(self) -> int:
+        return self.sliding_window if self.is_sliding else -1
+
+    def get_seq_length(self) -> int:
+        return self.cumulative_length if self.is_sliding else self._stored_len()
+
+    def get_mask_sizes(self, query_length: int) -> tuple[int, int]:
+        if not self.is_sliding:
+            return self.get_seq_length() + query_length, 0
+        is_full = self.cumulative_length >= self.sliding_window
+        kv_offset = max(self.cumulative_length - self.sliding_window + 1, 0)
+        kv_length = self.sliding_window - 1 + query_length if is_full else self.cumulative_length + query_length
+        return kv_length, kv_offset
+
+    # -- internals -----------------------------------------------------------
+    def _hot_len(self) -> int:
+        return 0 if self.hot_k is None else self.hot_k.shape[1]
+
+    def _frozen_len(self) -> int:
+        return (0 if self.store is None else self.store.S) - self._offset
+
+    def _stored_len(self) -> int:
+        return self._frozen_len() + self._hot_len()
+
+    def _freeze_pages(self) -> None:
+        n_full = (self._hot_len() // BLOCK) * BLOCK
+        if n_full == 0:
+            return
+        kp, vp = self.hot_k[:, :n_full], self.hot_v[:, :n_full]
+        if self.store is None:
+            self.store = store_kivi(kp.contiguous(), vp.contiguous(), self.k_calib, self.v_calib,
+                                    capacity=max(4 * n_full, 1024))
+        else:
+            append_kivi(self.store, kp, vp, self.k_calib, self.v_calib)
+        self.hot_k = self.hot_k[:, n_full:].contiguous()
+        self.hot_v = self.hot_v[:, n_full:].contiguous()
+
+    def _evict_sliding(self) -> None:
+        if not self.is_sliding or self.store is None:
+            return
+        keep = self.sliding_window - 1 + BLOCK
+        while self._frozen_len() - BLOCK >= keep:
+            self._offset += BLOCK       # drop whole pages from the front (view offset)
+
+    def _dequant_frozen(self) -> tuple[Tensor, Tensor]:
+        S = 0 if self.store is None else self.store.S
+        if S > self._deq_len:
+            k_all, v_all = dequant_kivi(self.store)   # newly frozen pages only are kept below
+            H, _, D = k_all.shape
+            if self._deq_k is None or self._deq_k.shape[1] < S:
+                cap = max(2 * S, 1024)
+                nk = torch.empty((H, cap, D), dtype=torch.bfloat16, device=k_all.device)
+                nv = torch.empty_like(nk)
+                if self._deq_len:
+                    nk[:, :self._deq_len] = self._deq_k[:, :self._deq_len]
+                    nv[:, :self._deq_len] = self._deq_v[:, :self._deq_len]
+                self._deq_k, self._deq_v = nk, nv
+            self._deq_k[:, self._deq_len:S] = k_all[:, self._deq_len:S]
+            self._deq_v[:, self._deq_len:S] = v_all[:, self._deq_len:S]
+            self._deq_len = S
+        return self._deq_k[:, self._offset:S], self._deq_v[:, self._offset:S]
+
+    # -- the contract the model calls ----------------------------------------
+    def update(self, key_states: Tensor, value_states: Tensor, *args, **kwargs) -> tuple[Tensor, Tensor]:
+        if not self.is_initialized:
+            self.lazy_initialization(key_states, value_states)
+        assert key_states.shape[0] == 1, "Int4KiviCache supports batch size 1"
+        k_new = key_states[0].to(torch.bfloat16)
+        v_new = value_states[0].to(torch.bfloat16)
+        self._H, self._D = k_new.shape[0], k_new.shape[2]
+        n_new = k_new.shape[1]
+        self.cumulative_length += n_new
+        if self.hot_k is None:
+            self.hot_k, self.hot_v = k_new, v_new
+        else:
+            self.hot_k = torch.cat([self.hot_k, k_new], dim=1)
+            self.hot_v = torch.cat([self.hot_v, v_new], dim=1)
+        self._freeze_pages()
+        self._evict_sliding()
+        ks, vs = [], []
+        if self._frozen_len() > 0:
+            fk, fv = self._dequant_frozen()
+            ks.append(fk); vs.append(fv)
+        if self._hot_len() > 0:
+            ks.append(self.hot_k); vs.append(self.hot_v)
+        k_full = torch.cat(ks, dim=1) if len(ks) > 1 else ks[0]
+        v_full = torch.cat(vs, dim=1) if len(vs) > 1 else vs[0]
+        if self.is_sliding and self.cumulative_length >= self.sliding_window:
+            want = self.sliding_window - 1 + n_new
+            if k_full.shape[1] > want:
+                k_full, v_full = k_full[:, -want:], v_full[:, -want:]
+        return k_full.unsqueeze(0), v_full.unsqueeze(0)
+
+    # -- memory accounting ----------------------------------------------------
+    def nbytes(self) -> int:
+        total = 0
+        if self.store is not None and self._frozen_len() > 0:
+            per_tok = self.store.nbytes / max(self.store.S, 1)
+            total += int(per_tok * self._frozen_len())
+        if self.hot_k is not None:
+            total += self.hot_k.numel() * self.hot_k.element_size() * 2
+        return total
+
+    def bf16_nbytes(self) -> int:
+        return 2 * (self._stored_len() * getattr(self, "_H", 0) * getattr(self, "_D", 0)) * 2
+
+    def reset(self) -> None:
+        self.__init__(self.k_calib, self.v_calib, self.is_sliding, self.sliding_window)
+
+    def reorder_cache(self, beam_idx) -> None:
+        pass
+
+    def crop(self, max_length: int) -> None:
+        raise NotImplementedError("crop is not supported by Int4KiviCache")
+
+    def batch_repeat_interleave(self, repeats: int) -> None:
+        raise NotImplementedError("batch expansion is not supported by Int4KiviCache")
+
+    def batch_select_indices(self, indices) -> None:
+        raise NotImplementedError("batch selection is not supported by Int4KiviCache")
+
+
+class Int4KiviCache(Cache):
+    """Drop-in ``past_key_values`` for ``model.generate``:
+
+        cache = Int4KiviCache(config=model.config)
+        model.generate(..., past_key_values=cache)
+    """
+
+    def __init__(self, config, k_calib: str = "mse", v_calib: str = "mse"):
+        decoder = config.get_text_config(decoder=True)
+        sliding_window = getattr(decoder, "sliding_window", None) or getattr(decoder, "attention_chunk_size", None)
+        layer_types = getattr(decoder, "layer_types", None)
+        if layer_types is None:
+            kind = "sliding_attention" if sliding_window is not None else "full_attention"
+            layer_types = [kind] * decoder.num_hidden_layers
+        layers = [_Int4KiviLayer(k_calib=k_calib, v_calib=v_calib, is_sliding=(lt == "sliding_attention"),
+                                 sliding_window=sliding_window if lt == "sliding_attention" else None)
+                  for lt in layer_types]
+        super().__init__(layers=layers)
+
+    def nbytes(self) -> int:
+        return sum(l.nbytes() for l in self.layers)
+
+    def bf16_nbytes(self) -> int:
+        return sum(l.bf16_nbytes() for l in self.layers)
+
+    def compression_ratio_vs_bf16(self) -> float:
+        return self.bf16_nbytes() / max(self.nbytes(), 1)

@@ -1,0 +1,67 @@
+"""CPU-only checks of the boundary: the C-ABI library loads, exports every
+symbol include/kivi_sm100.h declares, and rejects bad arguments before any
+device work (no compute calls here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+
+def _declared():
+    names = []
+    for h in os.listdir(os.path.join(ROOT, "include")):
+        if h.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", h)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names += re.findall(r"\b(kivi_\w+)\s*\(", src)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    from int4_kivi import _native
+    L = _native.lib()
+    decl = _declared()
+    assert "kivi_decode" in decl and "kivi_store" in decl
+    for n in decl:
+        assert hasattr(L, n), f"{n} not exported"
+
+
+def test_status_and_version():
+    from int4_kivi import _native
+    L = _native.lib()
+    assert L.kivi_version() >= 100
+    assert L.kivi_status_string(0) == b"ok"
+    assert b"argument" in L.kivi_status_string(1)
+
+
+def test_argument_errors_without_device_work():
+    from int4_kivi import _native
+    L = _native.lib()
+    # D not a multiple of 16
+    rc = L.kivi_store(None, None, 0, 0, 0, 0, 0, 0, 0, 1, 16, 16, 15, 0, 0, 0, None, 0, 1.0, 1.0,
+                      None, None, 0, 1, None, None, 0, 16, None)
+    assert rc == 1
+    # bad format
+    rc = L.kivi_roundtrip(None, None, 0, 1, 16, 16, 9, 0, 0, None, 0, None)
+    assert rc == 1
+    # Hq not a multiple of Hkv
+    rc = L.kivi_decode(None, 0, 0, None, None, 16, None, 0, None, None, 16, 1, 6, 4, 32, 128, 0, 0.1,
+                       1.0, 1.0, None, None, 0, None, None)
+    assert rc == 1
+    assert L.kivi_decode_workspace_floats(1, 6, 4, 32, 128) == 0
+
+
+def test_no_cpu_fallback():
+    """The product path raises on CPU tensors instead of computing on the host."""
+    import torch
+    from int4_kivi import store_kivi
+    k = torch.zeros(2, 32, 128, dtype=torch.bfloat16)
+    with pytest.raises(AssertionError):
+        store_kivi(k, k)
+    if not torch.cuda.is_available():
+        import kv_quant
+        with pytest.raises(RuntimeError):
+            kv_quant.roundtrip(k, "int4", "channel", "mse")
