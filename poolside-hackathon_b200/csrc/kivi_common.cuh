@@ -214,7 +214,7 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
 __device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t m, uint32_t x) {
     // (a & m) ^ x
     uint32_t d;
-    asm("lop3.b32 %0, %1, %2, %3, 0x78;" : "=r"(d) : "r"(a), "r"(m), "r"(x));
+    asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(m), "r"(x));
     return d;
 }
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
@@ -229,7 +229,7 @@ __device__ __forceinline__ __half2 int4_lo_to_h2(uint32_t w) {
 }
 __device__ __forceinline__ __half2 int4_hi_to_h2(uint32_t w) {
     uint32_t v = lop3_and_xor(w, 0x00F000F0u, 0x64806480u);      // 1024 + 16 (n ^ 8)
-    return __hfma2(u32_as_h2(v), __float2half2_rn(0.0625f), __float2half2_rn(-72.0f));
+    return __hfma2(u32_as_h2(v), u32_as_h2(0x2C002C00u), u32_as_h2(0xD480D480u));   // * 1/16 - 72
 }
 
 // Two e2m1 nibbles of one byte -> fp16x2 (exact), hardware conversion.

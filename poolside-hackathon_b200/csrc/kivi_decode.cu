@@ -29,7 +29,7 @@ namespace kivi {
 constexpr int TILE = 128;        // tokens per pipeline stage (8 pages)
 constexpr int NWARP_C = 4;       // consumer warps, 32 tokens each
 constexpr int NTHREADS = (NWARP_C + 1) * 32;
-constexpr int NST = 4;           // pipeline depth
+constexpr int NST = 3;           // pipeline depth
 constexpr int DH = 128;          // head_dim of the fast path
 constexpr int PB_PITCH = 40;     // halves per head row in the P staging buffer
 
@@ -98,13 +98,13 @@ __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
 
 // One m16n8k16 step for two M-tiles given the k-half words wA, wB and their
 // scale pairs.  INT4 splits each scale into head/tail parts (two exact MMAs).
-template <int FMT>
+template <int FMT, bool SPLIT>
 __device__ __forceinline__ void mma_pair(float (&c0)[4], float (&c1)[4], uint32_t wA, uint32_t wB,
                                          uint32_t sA, uint32_t sB, uint32_t b0, uint32_t b1) {
     uint32_t a0l, a0h, a1l, a1h, c0l, c0h, c1l, c1h;
     codes4<FMT>(wA, a0l, a0h, a1l, a1h);     // k-half A: tile0 rows(lo,hi), tile1 rows
     codes4<FMT>(wB, c0l, c0h, c1l, c1h);     // k-half B
-    if (FMT == FMT_NVFP4) {
+    if (FMT == FMT_NVFP4 || !SPLIT) {
         mma_f16(c0, hmul2u(a0l, sA), hmul2u(a0h, sA), hmul2u(c0l, sB), hmul2u(c0h, sB), b0, b1);
         mma_f16(c1, hmul2u(a1l, sA), hmul2u(a1h, sA), hmul2u(c1l, sB), hmul2u(c1h, sB), b0, b1);
     } else {
@@ -126,7 +126,7 @@ __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
 // Fast path kernel.
 // ---------------------------------------------------------------------------
 template <int FMT>
-__global__ void __launch_bounds__(NTHREADS, 2)
+__global__ void __launch_bounds__(NTHREADS, 3)
 decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_constant__ CUtensorMap tm_ks,
                    const __grid_constant__ CUtensorMap tm_vc, const __grid_constant__ CUtensorMap tm_vs,
                    const DecodeParams p) {
@@ -154,7 +154,8 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
         if (lane == 0) {
             prefetch_tmap(&tm_kc); prefetch_tmap(&tm_ks); prefetch_tmap(&tm_vc); prefetch_tmap(&tm_vs);
             int it = 0;
-            for (int64_t i = i0; i < i1; ++i, ++it) {
+            int bh = (int)(i0 / p.T), tl = (int)(i0 % p.T);
+            for (int64_t i = i0; i < i1; ++i, ++it, (++tl == p.T ? (tl = 0, ++bh) : 0)) {
                 const int s = it % NST;
                 if (!mbar_wait_bounded(&ctl->empty[s], ((it / NST) & 1) ^ 1)) {
                     set_err(p.err, KIVI_ERR_TIMEOUT);
@@ -162,7 +163,6 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                     break;
                 }
                 if (ctl->abort) break;
-                const int bh = (int)(i / p.T), tl = (int)(i % p.T);
                 uint8_t* st = stages + s * L::BYTES;
                 mbar_arrive_expect_tx(&ctl->full[s], L::TX);
                 tma_load_2d(st + L::KC, &tm_kc, &ctl->full[s], tl * 64, bh * DH);
@@ -221,8 +221,8 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
     };
 
     int it = 0;
-    for (int64_t i = i0; i < i1; ++i, ++it) {
-        const int bh = (int)(i / p.T), tl = (int)(i % p.T);
+    int bh = (int)(i0 / p.T), tl = (int)(i0 % p.T);
+    for (int64_t i = i0; i < i1; ++i, ++it, (++tl == p.T ? (tl = 0, ++bh) : 0)) {
         if (bh != cur) {
             if (cur >= 0) flush(cur);
             cur = bh;
@@ -268,7 +268,11 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
         const int limit = p.n_full - t_span;           // valid tokens in my span
         if (limit > 0) {
             // ------------------------------ QK^T ------------------------------
-            float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
+            float qa[2][4], qb[2][4];      // two accumulator pairs: shorter MMA chains
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) qa[j][e] = qb[j][e] = 0.f;
             const uint32_t kc_s = smem_u32(st + L::KC), ks_s = smem_u32(st + L::KS);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -291,8 +295,14 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                     s2 = __shfl_sync(0xffffffffu, s2, src_k);
                     s3 = __shfl_sync(0xffffffffu, s3, src_k);
                 }
-                mma_pair<FMT>(ca, cb, r0, r1, s0, s1, qB[2 * j][0], qB[2 * j][1]);
-                mma_pair<FMT>(ca, cb, r2, r3, s2, s3, qB[2 * j + 1][0], qB[2 * j + 1][1]);
+                mma_pair<FMT, true>(qa[j & 1], qb[j & 1], r0, r1, s0, s1, qB[2 * j][0], qB[2 * j][1]);
+                mma_pair<FMT, true>(qa[j & 1], qb[j & 1], r2, r3, s2, s3, qB[2 * j + 1][0], qB[2 * j + 1][1]);
+            }
+            float ca[4], cb[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                ca[e] = qa[0][e] + qa[1][e];
+                cb[e] = qb[0][e] + qb[1][e];
             }
             // ----------------------------- softmax ----------------------------
             // ca: tokens 4g (c0,c1), 4g+1 (c2,c3); cb: 4g+2, 4g+3; heads 2tq(+1)
@@ -311,21 +321,26 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                 mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
                 mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
             }
-            const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-            // mn == -inf only if every token so far is masked (cannot happen
-            // for limit > 0, kept for safety): use 0 as the reference point.
-            const float r0 = (mn0 == -INFINITY) ? 0.f : mn0, r1 = (mn1 == -INFINITY) ? 0.f : mn1;
-            const float al0 = exp2f(m0 - r0), al1 = exp2f(m1 - r1);
-            m0 = mn0; m1 = mn1;
-            float pr[8];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) { pr[e] = exp2f(x[e] - r0); pr[4 + e] = exp2f(x[4 + e] - r1); }
-            l0 = l0 * al0 + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
-            l1 = l1 * al1 + ((pr[4] + pr[5]) + (pr[6] + pr[7]));
-            if (!__all_sync(0xffffffffu, al0 == 1.f && al1 == 1.f)) {
+            // Lazy rescaling: the running reference max only moves when a new
+            // score exceeds it by more than 2^8 (p stays <= 256, exact in the
+            // final normalisation since l uses the same reference).
+            const bool need = (mx0 > m0 + 8.f) || (mx1 > m1 + 8.f);
+            if (__any_sync(0xffffffffu, need)) {
+                const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+                const float al0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - mn0);
+                const float al1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - mn1);
+                m0 = mn0; m1 = mn1;
+                l0 *= al0; l1 *= al1;
 #pragma unroll
                 for (int t = 0; t < 8; ++t) { acc[t][0] *= al0; acc[t][2] *= al0; acc[t][1] *= al1; acc[t][3] *= al1; }
             }
+            // m == -inf only while every token so far is masked: use 0 as reference
+            const float r0 = (m0 == -INFINITY) ? 0.f : m0, r1 = (m1 == -INFINITY) ? 0.f : m1;
+            float pr[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) { pr[e] = exp2f(x[e] - r0); pr[4 + e] = exp2f(x[4 + e] - r1); }
+            l0 += (pr[0] + pr[1]) + (pr[2] + pr[3]);
+            l1 += (pr[4] + pr[5]) + (pr[6] + pr[7]);
             // stage P as fp16 [head][token] for the PV B-fragments
             __syncwarp();
             *reinterpret_cast<uint2*>(pb + (2 * tq) * PB_PITCH + 4 * g) =
@@ -359,7 +374,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                             sa = (t0 + 1 < limit) ? sa : (t0 < limit ? (sa & 0x0000FFFFu) : 0u);
                             sb = (t0 + 9 < limit) ? sb : (t0 + 8 < limit ? (sb & 0x0000FFFFu) : 0u);
                         }
-                        mma_pair<FMT>(acc[2 * sg], acc[2 * sg + 1], hs ? w2 : w0, hs ? w3 : w1, sa, sb, b0, b1);
+                        mma_pair<FMT, false>(acc[2 * sg], acc[2 * sg + 1], hs ? w2 : w0, hs ? w3 : w1, sa, sb, b0, b1);
                     }
                 }
             }

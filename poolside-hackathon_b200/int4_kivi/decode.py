@@ -47,7 +47,7 @@ def _stacked_geometry(st: dict) -> tuple[int, int, dict]:
 
 
 def decode_packed(q: Tensor, st: dict, n_qh: int, sm_scale: Optional[float] = None,
-                  fmt: str = "int4", g_k: float = 1.0, g_v: float = 1.0,
+                  fmt: Optional[str] = None, g_k: Optional[float] = None, g_v: Optional[float] = None,
                   out: Optional[Tensor] = None, partial: bool = False):
     """Core entry: q [B, n_qh, D] bf16 over a stacked packed cache (B*H heads).
 
@@ -55,6 +55,9 @@ def decode_packed(q: Tensor, st: dict, n_qh: int, sm_scale: Optional[float] = No
     (m [B*n_qh] in log2 units, l [B*n_qh], acc [B*n_qh, D]) for a cross-GPU
     log-sum-exp merge."""
     B, H, S, D = st["B"], st["H"], st["S"], st["D"]
+    fmt = st.get("fmt", "int4") if fmt is None else fmt
+    g_k = st.get("g_k", 1.0) if g_k is None else g_k
+    g_v = st.get("g_v", 1.0) if g_v is None else g_v
     N.require_cuda(q, st["v_packed"])
     assert q.shape == (B, n_qh, D), f"q must be [B={B}, n_qh={n_qh}, D={D}]"
     assert n_qh % H == 0, "n_q_heads must be a multiple of n_kv_heads"
