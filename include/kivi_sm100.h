@@ -35,7 +35,8 @@ enum kivi_status {
     KIVI_ERR_ALIGN = 2,        /* pointer or stride violates alignment rule */
     KIVI_ERR_UNSUPPORTED = 3,  /* valid but not implemented (e.g. head_dim) */
     KIVI_ERR_CUDA = 4,         /* a CUDA runtime/driver call failed         */
-    KIVI_ERR_TIMEOUT = 5       /* device-side bounded wait expired          */
+    KIVI_ERR_TIMEOUT = 5,      /* device-side bounded wait expired          */
+    KIVI_ERR_SCRATCH = 6       /* problem exceeds the fixed no-alloc scratch */
 };
 
 enum kivi_fmt { KIVI_FMT_INT4 = 0, KIVI_FMT_INT3 = 1, KIVI_FMT_NVFP4 = 2 };
@@ -148,6 +149,31 @@ int kivi_decode_partial(const void *q, int64_t q_sb, int64_t q_sh,
                         float *m_out, float *l_out, float *acc_out,
                         float *work, int64_t work_floats, int *err,
                         kivi_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* kivi_decode without a caller workspace: no counterpart in the reference.  */
+/* For callers that cannot allocate device memory at decode time (a serving  */
+/* engine with its own fixed memory pool, a stream capture, an FFI host      */
+/* without a CUDA allocator).  Same arguments and result as kivi_decode,     */
+/* minus `work`; the split-K partials go to a library-owned device array of  */
+/* KIVI_NOALLOC_SCRATCH_FLOATS floats (8 MiB, held on every GPU that loads   */
+/* the library until exit).  Problems whose kivi_decode_workspace_floats()   */
+/* exceeds that return KIVI_ERR_SCRATCH before any launch.  The first call   */
+/* on a device looks up the array's device address (cudaGetSymbolAddress);   */
+/* make that first call before any stream capture.  All calls share the one  */
+/* array: calls that overlap on the GPU (different streams, or different     */
+/* host threads on the same device) race and must be serialised by the      */
+/* caller.  Nothing is allocated or freed.                                   */
+/* ------------------------------------------------------------------------ */
+#define KIVI_NOALLOC_SCRATCH_FLOATS (1 << 21)
+
+int kivi_decode_noalloc(const void *q, int64_t q_sb, int64_t q_sh,
+                        const uint8_t *k_packed, const void *k_scale, int k_np_stride,
+                        const void *k_hot, int hot_stride,
+                        const uint8_t *v_packed, const void *v_scale, int v_s_stride,
+                        int B, int Hq, int Hkv, int S, int D, int fmt,
+                        float sm_scale, float g_k, float g_v,
+                        void *out, int *err, kivi_stream_t stream);
 
 /* Log-sum-exp merge of R partial records laid out [R, rows] / [R, rows, D]  */
 /* (int4_kivi/decode.py:320-340 semantics) -> bf16 out [rows, D].            */

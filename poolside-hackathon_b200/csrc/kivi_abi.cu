@@ -17,6 +17,7 @@ extern "C" const char* kivi_status_string(int status) {
         case KIVI_ERR_UNSUPPORTED: return "unsupported configuration";
         case KIVI_ERR_CUDA: return "CUDA runtime/driver error (see kivi_last_cuda_error)";
         case KIVI_ERR_TIMEOUT: return "device-side bounded wait expired";
+        case KIVI_ERR_SCRATCH: return "problem needs more scratch than the fixed no-alloc buffer (use kivi_decode with a workspace)";
         default: return "unknown status";
     }
 }

@@ -23,6 +23,7 @@
 #include "kivi_common.cuh"
 #include "kivi_internal.h"
 #include <cuda.h>
+#include <mutex>
 
 namespace kivi {
 
@@ -773,4 +774,61 @@ extern "C" int kivi_lse_merge(const float* m, const float* l, const float* acc, 
     lse_merge_kernel<<<rows, 128, 0, (cudaStream_t)stream>>>(m, l, acc, R, rows, D,
                                                              reinterpret_cast<__nv_bfloat16*>(out));
     return check_launch();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode.
+//
+// Some callers cannot call cudaMalloc at decode time: a serving engine that
+// hands out all device memory from its own pre-sized pool, code running
+// under a CUDA stream capture, or an FFI host (Go, Java) that owns no CUDA
+// allocator.  For them the split-K partials live in one fixed, library-owned
+// device array instead of a caller-supplied workspace.  Its size is fixed at
+// KIVI_NOALLOC_SCRATCH_FLOATS fp32 values (8 MiB) and every GPU that loads the
+// library keeps it until the process exits.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float g_noalloc_scratch[KIVI_NOALLOC_SCRATCH_FLOATS];
+
+namespace {
+struct NoallocSlot { float* ptr = nullptr; bool ready = false; };
+std::mutex g_noalloc_mu;
+NoallocSlot g_noalloc_slots[64];
+
+// Device address of the scratch array for the current device.  In host code
+// `g_noalloc_scratch` is only a host-side stand-in for the symbol, so the
+// address must be looked up once per device with that device current.
+int noalloc_scratch_ptr(float** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    if (dev < 0 || dev >= 64) return KIVI_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoallocSlot& s = g_noalloc_slots[dev];
+    if (!s.ready) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        s.ptr = static_cast<float*>(p);
+        s.ready = true;
+    }
+    *out = s.ptr;
+    return KIVI_OK;
+}
+}  // namespace
+
+extern "C" int kivi_decode_noalloc(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,
+                                   const void* k_scale, int k_np_stride, const void* k_hot, int hot_stride,
+                                   const uint8_t* v_packed, const void* v_scale, int v_s_stride, int B,
+                                   int Hq, int Hkv, int S, int D, int fmt, float sm_scale, float g_k,
+                                   float g_v, void* out, int* err, kivi_stream_t stream) {
+    const int64_t need = kivi_decode_workspace_floats(B, Hq, Hkv, S, D);
+    if (need > KIVI_NOALLOC_SCRATCH_FLOATS) return KIVI_ERR_SCRATCH;
+    float* scratch = nullptr;
+    const int rc = noalloc_scratch_ptr(&scratch);
+    if (rc != KIVI_OK) return rc;
+    // Every slot the merge reads is written by the split kernel of the same
+    // call, so nothing in the scratch has to start at zero.
+    return decode_impl(0, q, q_sb, q_sh, k_packed, k_scale, k_np_stride, k_hot, hot_stride, v_packed,
+                       v_scale, v_s_stride, B, Hq, Hkv, S, D, fmt, sm_scale, g_k, g_v, out, nullptr, nullptr,
+                       nullptr, scratch, KIVI_NOALLOC_SCRATCH_FLOATS, err, stream);
 }
