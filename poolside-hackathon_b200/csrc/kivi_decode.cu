@@ -24,6 +24,8 @@
 #include "kivi_internal.h"
 #include <cuda.h>
 #include <mutex>
+#include <algorithm>
+#include <type_traits>
 
 namespace kivi {
 
@@ -267,7 +269,9 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
 
         const int t_span = tl * TILE + 32 * warp;      // first token of my span
         const int limit = p.n_full - t_span;           // valid tokens in my span
-        if (limit > 0) {
+        // Full spans take the branch-free body; only a sequence's last tile is masked.
+        auto span = [&](auto masked_tag) {
+            constexpr bool MASKED = decltype(masked_tag)::value;
             // ------------------------------ QK^T ------------------------------
             float qa[2][4], qb[2][4];      // two accumulator pairs: shorter MMA chains
 #pragma unroll
@@ -310,7 +314,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
             float x[8] = {ca[0], ca[2], cb[0], cb[2], ca[1], ca[3], cb[1], cb[3]};
 #pragma unroll
             for (int e = 0; e < 8; ++e) x[e] *= p.scale2;
-            if (limit < 32) {
+            if (MASKED) {
                 const int tk[4] = {4 * g, 4 * g + 1, 4 * g + 2, 4 * g + 3};
 #pragma unroll
                 for (int e = 0; e < 8; ++e) if (tk[e & 3] >= limit) x[e] = -INFINITY;
@@ -353,7 +357,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
             const uint32_t vc_s = smem_u32(st + L::VC), vs_s = smem_u32(vs_base);
             uint32_t vr[4];
             ldsm_x4_t(vs_s + (32 * warp + lane) * 16, vr[0], vr[1], vr[2], vr[3]);
-            const bool mask_v = limit < 32;
+            
 #pragma unroll
             for (int lam = 0; lam < 2; ++lam) {
                 const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pb + g * PB_PITCH + 16 * lam + 2 * tq);
@@ -370,7 +374,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                         const int src_v = ((2 * sg + (g >> 2)) << 2) | tq;
                         uint32_t sa = __shfl_sync(0xffffffffu, vr[2 * lam], src_v);
                         uint32_t sb = __shfl_sync(0xffffffffu, vr[2 * lam + 1], src_v);
-                        if (mask_v) {
+                        if (MASKED) {
                             const int t0 = 16 * lam + 2 * tq;     // tokens of sa: t0, t0+1; sb: t0+8, t0+9
                             sa = (t0 + 1 < limit) ? sa : (t0 < limit ? (sa & 0x0000FFFFu) : 0u);
                             sb = (t0 + 9 < limit) ? sb : (t0 + 8 < limit ? (sb & 0x0000FFFFu) : 0u);
@@ -379,7 +383,9 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                     }
                 }
             }
-        }
+        };
+        if (limit >= 32) span(std::false_type{});
+        else if (limit > 0) span(std::true_type{});
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->empty[s]);
     }
@@ -472,76 +478,88 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeParams 
 }
 
 // ---------------------------------------------------------------------------
-// Combine: bf16 hot tail + LSE merge of all partial slots of one kv-head.
+// Combine: bf16 hot tail + LSE merge of all partial slots of one (kv-head,
+// q-head) pair; one 128-thread block per pair.  The slot weights
+// exp2(m_s - M) are computed once into shared memory, then every thread
+// reduces its channels over the slots with coalesced loads.
 // mode 0 -> normalised bf16 out; mode 1 -> merged (m, l, acc) records.
 // ---------------------------------------------------------------------------
+__host__ __device__ inline void head_cta_range(int bh, int T, int64_t W, int N, int& c_lo, int& c_hi) {
+    c_lo = 0; c_hi = -1;
+    if (W <= 0) return;
+    const int64_t a0 = (int64_t)bh * T, a1 = a0 + T;
+    int64_t cc = (a0 * N) / W;
+    while (cc + 1 < N && tile_start(cc + 1, W, N) <= a0) ++cc;
+    while (cc > 0 && tile_start(cc, W, N) > a0) --cc;
+    c_lo = (int)cc;
+    int64_t ch = cc;
+    while (ch + 1 < N && tile_start(ch + 1, W, N) < a1) ++ch;
+    c_hi = (int)ch;
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int mode, __nv_bfloat16* out,
                                                       float* m_out, float* l_out, float* acc_out) {
     extern __shared__ float csm[];
-    const int bh = blockIdx.x, b = bh / p.Hkv, kvh = bh % p.Hkv;
+    const int bh = blockIdx.x, h = blockIdx.y, b = bh / p.Hkv, kvh = bh % p.Hkv;
     const int G = p.G, D = p.D, ND = D / BLK, hot = p.hot;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* sc = csm;                  // [G][16] hot scores (log2 units)
+    int c_lo, c_hi;
+    head_cta_range(bh, p.T, p.W, p.N, c_lo, c_hi);
+    const int ns = (c_hi - c_lo + 1) * NWARP_C;          // partial slots of this head
+    float* w = csm;                                      // [ns + 16] weights (slots, then hot tokens)
+    float* red = csm + ns + 16;                          // [8] block reduction scratch
     const float sc2 = p.sm_scale * 1.4426950408889634f;
-    // hot-tail scores: one warp per (head, token) pair
-    for (int pr = warp; pr < G * hot; pr += 4) {
-        const int h = pr / hot, j = pr % hot;
-        const __nv_bfloat16* qp = p.q + b * p.q_sb + (int64_t)(kvh * G + h) * p.q_sh;
+    const __nv_bfloat16* qp = p.q + b * p.q_sb + (int64_t)(kvh * G + h) * p.q_sh;
+    // hot-tail scores (log2 units), one warp per token
+    for (int j = warp; j < hot; j += 4) {
         const __nv_bfloat16* kp = p.k_hot + ((int64_t)bh * p.hot_stride + j) * D;
-        float s = 0.f;
-        for (int d = lane; d < D; d += 32) s += __bfloat162float(qp[d]) * __bfloat162float(kp[d]);
+        float sdot = 0.f;
+        for (int d = lane; d < D; d += 32) sdot += __bfloat162float(qp[d]) * __bfloat162float(kp[d]);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) sc[h * 16 + j] = s * sc2;
+        for (int o = 16; o > 0; o >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, o);
+        if (lane == 0) w[ns + j] = sdot * sc2;
     }
+    auto slot = [&](int i) -> int64_t {
+        return ((int64_t)(c_lo + i / NWARP_C + bh) * NWARP_C + (i % NWARP_C)) * G + h;
+    };
+    for (int i = threadIdx.x; i < ns; i += blockDim.x) w[i] = p.part_m[slot(i)];
     __syncthreads();
-    // partial slots of this head
-    int c_lo = 0, c_hi = -1;
-    if (p.W > 0) {
-        const int64_t a0 = (int64_t)bh * p.T, a1 = a0 + p.T;
-        int64_t cc = (a0 * p.N) / p.W;
-        while (cc + 1 < p.N && tile_start(cc + 1, p.W, p.N) <= a0) ++cc;
-        while (cc > 0 && tile_start(cc, p.W, p.N) > a0) --cc;
-        c_lo = (int)cc;
-        int64_t ch = cc;
-        while (ch + 1 < p.N && tile_start(ch + 1, p.W, p.N) < a1) ++ch;
-        c_hi = (int)ch;
+    // M = max over slots and hot tokens
+    float M = -INFINITY;
+    for (int i = threadIdx.x; i < ns + hot; i += blockDim.x) M = fmaxf(M, w[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if (lane == 0) red[warp] = M;
+    __syncthreads();
+    M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const float Mr = (M == -INFINITY) ? 0.f : M;
+    __syncthreads();
+    // weights and L
+    float Ls = 0.f;
+    for (int i = threadIdx.x; i < ns + hot; i += blockDim.x) {
+        const float e = exp2f(w[i] - Mr);
+        Ls += (i < ns) ? p.part_l[slot(i)] * e : e;
+        w[i] = e;
     }
-    for (int h = 0; h < G; ++h) {
-        float mh = -INFINITY;
-        for (int j = 0; j < hot; ++j) mh = fmaxf(mh, sc[h * 16 + j]);
-        float M = mh;
-        for (int cc = c_lo; cc <= c_hi; ++cc)
-            for (int w = 0; w < NWARP_C; ++w)
-                M = fmaxf(M, p.part_m[((int64_t)(cc + bh) * NWARP_C + w) * G + h]);
-        const float Mr = (M == -INFINITY) ? 0.f : M;
-        float Lsum = 0.f;
-        for (int cc = c_lo; cc <= c_hi; ++cc)
-            for (int w = 0; w < NWARP_C; ++w) {
-                const int64_t sl = ((int64_t)(cc + bh) * NWARP_C + w) * G + h;
-                Lsum += p.part_l[sl] * exp2f(p.part_m[sl] - Mr);
-            }
-        for (int j = 0; j < hot; ++j) Lsum += exp2f(sc[h * 16 + j] - Mr);
-        const int64_t row = (int64_t)b * p.Hq + kvh * G + h;
-        for (int d = threadIdx.x; d < D; d += blockDim.x) {
-            float a = 0.f;
-            for (int cc = c_lo; cc <= c_hi; ++cc)
-                for (int w = 0; w < NWARP_C; ++w) {
-                    const int64_t sl = ((int64_t)(cc + bh) * NWARP_C + w) * G + h;
-                    a += p.part_acc[sl * D + d] * exp2f(p.part_m[sl] - Mr);
-                }
-            for (int j = 0; j < hot; ++j) {
-                const int64_t vr = ((int64_t)bh * p.v_s_stride + p.n_full + j) * ND + d / BLK;
-                const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
-                const float v = gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
-                a += exp2f(sc[h * 16 + j] - Mr) * v;
-            }
-            if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Lsum);
-            else acc_out[row * D + d] = a;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, o);
+    if (lane == 0) red[4 + warp] = Ls;
+    __syncthreads();
+    Ls = (red[4] + red[5]) + (red[6] + red[7]);
+    const int64_t row = (int64_t)b * p.Hq + kvh * G + h;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float a = 0.f;
+        for (int i = 0; i < ns; ++i) a += p.part_acc[slot(i) * D + d] * w[i];
+        for (int j = 0; j < hot; ++j) {
+            const int64_t vr = ((int64_t)bh * p.v_s_stride + p.n_full + j) * ND + d / BLK;
+            const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
+            a += w[ns + j] * (gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v));
         }
-        if (mode == 1 && threadIdx.x == 0) { m_out[row] = M; l_out[row] = Lsum; }
+        if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
+        else acc_out[row * D + d] = a;
     }
+    if (mode == 1 && threadIdx.x == 0) { m_out[row] = M; l_out[row] = Ls; }
 }
 
 // Merge R records [R, rows], [R, rows, D] -> bf16 [rows, D].
@@ -729,10 +747,17 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
         int e = check_launch();
         if (e) return e;
     }
-    const size_t csm = (size_t)G * 16 * sizeof(float);
+    // a head of T tiles touches at most ceil(T / floor(W/N)) + 1 CTAs
+    int max_ctas = 0;
+    if (pl.W > 0) {
+        const int64_t per = std::max<int64_t>(pl.W / pl.N, 1);
+        max_ctas = (int)((pl.T + per - 1) / per) + 1;
+    }
+    const size_t csm = ((size_t)max_ctas * NWARP_C + 16 + 8) * sizeof(float);
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
-    if (fmt == FMT_NVFP4) combine_kernel<FMT_NVFP4><<<BH, 128, csm, st>>>(p, mode, o, m_out, l_out, acc_out);
-    else combine_kernel<FMT_INT4><<<BH, 128, csm, st>>>(p, mode, o, m_out, l_out, acc_out);
+    const dim3 cgrid(BH, G);
+    if (fmt == FMT_NVFP4) combine_kernel<FMT_NVFP4><<<cgrid, 128, csm, st>>>(p, mode, o, m_out, l_out, acc_out);
+    else combine_kernel<FMT_INT4><<<cgrid, 128, csm, st>>>(p, mode, o, m_out, l_out, acc_out);
     return check_launch();
 }
 
