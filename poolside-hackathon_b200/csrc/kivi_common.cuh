@@ -189,6 +189,10 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_
         " [%0], [%1, {%3, %4, %5}], [%2];"
         :: "r"(smem_u32(dst)), "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z) : "memory");
 }
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
+                 :: "l"(tmap), "r"(x), "r"(y) : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
 }

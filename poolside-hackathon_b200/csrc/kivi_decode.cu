@@ -34,7 +34,8 @@ constexpr int NWARP_C = 4;       // consumer warps, 32 tokens each
 constexpr int NTHREADS = (NWARP_C + 1) * 32;
 constexpr int NST = 3;           // pipeline depth
 constexpr int DH = 128;          // head_dim of the fast path
-constexpr int PB_PITCH = 40;     // halves per head row in the P staging buffer
+constexpr int PB_PITCH = 40;
+constexpr int PF_DIST = 0;       // L2 prefetch distance in tiles (0 = off)     // halves per head row in the P staging buffer
 
 struct DecodeParams {
     const __nv_bfloat16* q; int64_t q_sb, q_sh;
@@ -121,6 +122,37 @@ __device__ __forceinline__ void mma_pair(float (&c0)[4], float (&c1)[4], uint32_
     }
 }
 
+
+// Paired form (INT4, GQA group <= 4): the A operand is the raw exact codes and
+// the scales ride on B.  Columns n < 4 of B carry the query heads scaled for
+// the first page (K) / d-block (V) of the M-tile's rows, columns n >= 4 the
+// same heads scaled for the second, so one MMA serves both halves of the tile;
+// each thread later keeps the half that matches its rows.
+__device__ __forceinline__ void mma_raw(float (&c0)[4], float (&c1)[4], uint32_t wA, uint32_t wB,
+                                        uint32_t b0, uint32_t b1) {
+    uint32_t a0l, a0h, a1l, a1h, c0l, c0h, c1l, c1h;
+    codes4<FMT_INT4>(wA, a0l, a0h, a1l, a1h);
+    codes4<FMT_INT4>(wB, c0l, c0h, c1l, c1h);
+    mma_f16(c0, a0l, a0h, c0l, c0h, b0, b1);
+    mma_f16(c1, a1l, a1h, c1l, c1h, b0, b1);
+}
+__device__ __forceinline__ void mma_raw2(float (&c0)[4], float (&c1)[4], uint32_t wA, uint32_t wB,
+                                         uint32_t b0h, uint32_t b1h, uint32_t b0l, uint32_t b1l) {
+    uint32_t a0l, a0h, a1l, a1h, c0l, c0h, c1l, c1h;
+    codes4<FMT_INT4>(wA, a0l, a0h, a1l, a1h);
+    codes4<FMT_INT4>(wB, c0l, c0h, c1l, c1h);
+    mma_f16(c0, a0l, a0h, c0l, c0h, b0h, b1h);
+    mma_f16(c1, a1l, a1h, c1l, c1h, b0h, b1h);
+    mma_f16(c0, a0l, a0h, c0l, c0h, b0l, b1l);
+    mma_f16(c1, a1l, a1h, c1l, c1h, b0l, b1l);
+}
+// q (x) s as an exact hi + lo pair of fp16x2 values.
+__device__ __forceinline__ void split_prod(uint32_t q, uint32_t sc, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __hmul2(u32_as_h2(q), u32_as_h2(sc));
+    hi = h2_as_u32(h);
+    lo = h2_as_u32(__hfma2(u32_as_h2(q), u32_as_h2(sc), __hneg2(h)));
+}
+
 __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
     return row * 64u + 16u * (chunk ^ ((row >> 1) & 3u));
 }
@@ -128,7 +160,7 @@ __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
 // ---------------------------------------------------------------------------
 // Fast path kernel.
 // ---------------------------------------------------------------------------
-template <int FMT>
+template <int FMT, bool PAIRED>
 __global__ void __launch_bounds__(NTHREADS, 3)
 decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_constant__ CUtensorMap tm_ks,
                    const __grid_constant__ CUtensorMap tm_vc, const __grid_constant__ CUtensorMap tm_vs,
@@ -173,6 +205,13 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                 else tma_load_2d(st + L::KS, &tm_ks, &ctl->full[s], tl * 8, bh * DH);
                 const int vrow = bh * p.v_s_stride + tl * TILE;
                 tma_load_2d(st + L::VC, &tm_vc, &ctl->full[s], 0, vrow);
+                if (PF_DIST > 0 && i + PF_DIST < i1) {
+                    // warm L2 with the tile PF_DIST ahead (same head or the next one)
+                    int ptl = tl + PF_DIST, pbh = bh;
+                    while (ptl >= p.T) { ptl -= p.T; ++pbh; }
+                    tma_prefetch_2d(&tm_kc, ptl * 64, pbh * DH);
+                    tma_prefetch_2d(&tm_vc, 0, pbh * p.v_s_stride + ptl * TILE);
+                }
                 if (FMT == FMT_NVFP4) tma_load_2d(st + L::VS, &tm_vs, &ctl->full[s], 0, vrow >> 1);
                 else tma_load_2d(st + L::VS, &tm_vs, &ctl->full[s], 0, vrow);
             }
@@ -204,14 +243,18 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
         }
         const int64_t slot = ((int64_t)(c + bh) * NWARP_C + warp) * G;
         const float gv = (FMT == FMT_NVFP4) ? p.g_v : 1.0f;
+        // paired form: the acc columns of lane (g, tq) are heads 2(tq&1)(+1),
+        // valid where the column half matches the rows' d-block half
+        const bool acc_ok = PAIRED ? ((g < 4) == (tq < 2)) : true;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-            const int h = 2 * tq + hh;
+            const int h = (PAIRED ? 2 * (tq & 1) : 2 * tq) + hh;
             if (h < G) {
-                if (g == 0) {
+                if (g == 0 && tq < (PAIRED ? 2 : 4)) {
                     p.part_m[slot + h] = hh ? m1 : m0;
                     p.part_l[slot + h] = hh ? L1 : L0;
                 }
+                if (!acc_ok) continue;
                 float* a = p.part_acc + (slot + h) * DH;
 #pragma unroll
                 for (int sg = 0; sg < 4; ++sg) {
@@ -233,13 +276,14 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
 #pragma unroll
             for (int t = 0; t < 8; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
             const int b = bh / p.Hkv, kvh = bh % p.Hkv;
-            const __nv_bfloat16* qp = p.q + b * p.q_sb + (int64_t)(kvh * G + g) * p.q_sh;
+            const int qh = PAIRED ? (g & 3) : g;
+            const __nv_bfloat16* qp = p.q + b * p.q_sb + (int64_t)(kvh * G + qh) * p.q_sh;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     uint32_t v = 0;
-                    if (g < G) {
+                    if (qh < G) {
                         const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(qp + 16 * k + 8 * hf + 2 * tq);
                         v = h2_as_u32(__float22half2_rn(__bfloat1622float2(b2)));
                     }
@@ -300,14 +344,36 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                     s2 = __shfl_sync(0xffffffffu, s2, src_k);
                     s3 = __shfl_sync(0xffffffffu, s3, src_k);
                 }
-                mma_pair<FMT, true>(qa[j & 1], qb[j & 1], r0, r1, s0, s1, qB[2 * j][0], qB[2 * j][1]);
-                mma_pair<FMT, true>(qa[j & 1], qb[j & 1], r2, r3, s2, s3, qB[2 * j + 1][0], qB[2 * j + 1][1]);
+                if constexpr (PAIRED) {
+                    uint32_t h0, l0_, h1, l1_, h2, l2_, h3, l3_;
+                    split_prod(qB[2 * j][0], s0, h0, l0_);
+                    split_prod(qB[2 * j][1], s1, h1, l1_);
+                    split_prod(qB[2 * j + 1][0], s2, h2, l2_);
+                    split_prod(qB[2 * j + 1][1], s3, h3, l3_);
+                    mma_raw2(qa[j & 1], qb[j & 1], r0, r1, h0, h1, l0_, l1_);
+                    mma_raw2(qa[j & 1], qb[j & 1], r2, r3, h2, h3, l2_, l3_);
+                } else {
+                    mma_pair<FMT, true>(qa[j & 1], qb[j & 1], r0, r1, s0, s1, qB[2 * j][0], qB[2 * j][1]);
+                    mma_pair<FMT, true>(qa[j & 1], qb[j & 1], r2, r3, s2, s3, qB[2 * j + 1][0], qB[2 * j + 1][1]);
+                }
             }
             float ca[4], cb[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 ca[e] = qa[0][e] + qa[1][e];
                 cb[e] = qb[0][e] + qb[1][e];
+            }
+            if constexpr (PAIRED) {
+                // keep the column half that matches my rows' page; after this
+                // every lane holds heads 2(tq&1), 2(tq&1)+1 of its rows
+                const bool mine = (g < 4) == (tq < 2);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float oa = __shfl_xor_sync(0xffffffffu, ca[e], 2);
+                    const float ob = __shfl_xor_sync(0xffffffffu, cb[e], 2);
+                    ca[e] = mine ? ca[e] : oa;
+                    cb[e] = mine ? cb[e] : ob;
+                }
             }
             // ----------------------------- softmax ----------------------------
             // ca: tokens 4g (c0,c1), 4g+1 (c2,c3); cb: 4g+2, 4g+3; heads 2tq(+1)
@@ -360,8 +426,9 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
             
 #pragma unroll
             for (int lam = 0; lam < 2; ++lam) {
-                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pb + g * PB_PITCH + 16 * lam + 2 * tq);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(pb + g * PB_PITCH + 16 * lam + 8 + 2 * tq);
+                const int prow = PAIRED ? (g & 3) : g;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pb + prow * PB_PITCH + 16 * lam + 2 * tq);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(pb + prow * PB_PITCH + 16 * lam + 8 + 2 * tq);
 #pragma unroll
                 for (int sp = 0; sp < 2; ++sp) {          // segment pairs (2sp, 2sp+1)
                     const uint32_t trow = 32 * warp + 16 * lam + 8 * ((lane >> 3) & 1) + (lane & 7);
@@ -379,7 +446,12 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                             sa = (t0 + 1 < limit) ? sa : (t0 < limit ? (sa & 0x0000FFFFu) : 0u);
                             sb = (t0 + 9 < limit) ? sb : (t0 + 8 < limit ? (sb & 0x0000FFFFu) : 0u);
                         }
-                        mma_pair<FMT, false>(acc[2 * sg], acc[2 * sg + 1], hs ? w2 : w0, hs ? w3 : w1, sa, sb, b0, b1);
+                        if constexpr (PAIRED) {
+                            mma_raw(acc[2 * sg], acc[2 * sg + 1], hs ? w2 : w0, hs ? w3 : w1,
+                                    hmul2u(b0, sa), hmul2u(b1, sb));
+                        } else {
+                            mma_pair<FMT, false>(acc[2 * sg], acc[2 * sg + 1], hs ? w2 : w0, hs ? w3 : w1, sa, sb, b0, b1);
+                        }
                     }
                 }
             }
@@ -646,11 +718,13 @@ int fast_occupancy(int dev) {
     const int k = (FMT == FMT_NVFP4) ? 1 : 0;
     if (!di.occ[k]) {
         const size_t smem = fast_smem_bytes<FMT>();
-        if (cudaFuncSetAttribute(decode_fast_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(decode_fast_kernel<FMT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem) != cudaSuccess ||
+            cudaFuncSetAttribute(decode_fast_kernel<FMT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem) != cudaSuccess)
             return 0;
         int occ = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_fast_kernel<FMT>, NTHREADS, smem) !=
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_fast_kernel<FMT, false>, NTHREADS, smem) !=
             cudaSuccess)
             return 0;
         di.occ[k] = occ > 0 ? occ : 1;
@@ -737,9 +811,11 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
             }
             if (!ok) return KIVI_ERR_CUDA;
             if (fmt == FMT_NVFP4)
-                decode_fast_kernel<FMT_NVFP4><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>(), st>>>(tkc, tks, tvc, tvs, p);
+                decode_fast_kernel<FMT_NVFP4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>(), st>>>(tkc, tks, tvc, tvs, p);
+            else if (G <= 4)
+                decode_fast_kernel<FMT_INT4, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>(), st>>>(tkc, tks, tvc, tvs, p);
             else
-                decode_fast_kernel<FMT_INT4><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>(), st>>>(tkc, tks, tvc, tvs, p);
+                decode_fast_kernel<FMT_INT4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>(), st>>>(tkc, tks, tvc, tvs, p);
         } else {
             if (fmt == FMT_NVFP4) decode_generic_kernel<FMT_NVFP4><<<pl.N, 128, 0, st>>>(p);
             else decode_generic_kernel<FMT_INT4><<<pl.N, 128, 0, st>>>(p);
