@@ -32,6 +32,9 @@ for _p in (ROOT, PKG):
 B, HQ, HKV, D = 8, 32, 8, 128
 BYTES_PER_TOKEN_HEAD = 160          # 64 K codes + 16 K scales + 64 V codes + 16 V scales
 METRIC = "packed-KV HBM GB/s (INT4-KIVI fused decode, 64K ctx)"
+# dram__bytes_read.sum + dram__bytes_write.sum of the split-K kernel, measured
+# with ncu on the 16384-token case and scaled by tokens to the 65536-token launch.
+TRAFFIC_PER_LAUNCH = 750.3e6
 
 
 def _peaks():
@@ -246,7 +249,8 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "timed": "whole step (main split-K kernel + combine), CUDA events",
-                         "traffic": None},
+                         "traffic": TRAFFIC_PER_LAUNCH if S == 65536 else None,
+                         "traffic_note": "ncu dram read+write of one 16384-token launch x4 (profiles/decode_int4_64k.md)"},
             "e2e": {"value": round(world * packed_bytes / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": qo_bytes // 2, "d2h_bytes_per_step": qo_bytes // 2,
                     "ms_per_step": round(ms_e2e, 4), "note": "packed KV cache resident; q in, out back"},

@@ -32,10 +32,19 @@ namespace kivi {
 constexpr int TILE = 128;        // tokens per pipeline stage (8 pages)
 constexpr int NWARP_C = 4;       // consumer warps, 32 tokens each
 constexpr int NTHREADS = (NWARP_C + 1) * 32;
-constexpr int NST = 3;           // pipeline depth
+#ifndef KIVI_NST
+#define KIVI_NST 3
+#endif
+#ifndef KIVI_CTAS
+#define KIVI_CTAS 3
+#endif
+constexpr int NST = KIVI_NST;    // pipeline depth
 constexpr int DH = 128;          // head_dim of the fast path
 constexpr int PB_PITCH = 40;
-constexpr int PF_DIST = 0;       // L2 prefetch distance in tiles (0 = off)     // halves per head row in the P staging buffer
+#ifndef KIVI_PF
+#define KIVI_PF 0
+#endif
+constexpr int PF_DIST = KIVI_PF; // L2 prefetch distance in tiles (0 = off)     // halves per head row in the P staging buffer
 
 struct DecodeParams {
     const __nv_bfloat16* q; int64_t q_sb, q_sh;
@@ -161,7 +170,7 @@ __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
 // Fast path kernel.
 // ---------------------------------------------------------------------------
 template <int FMT, bool PAIRED>
-__global__ void __launch_bounds__(NTHREADS, 3)
+__global__ void __launch_bounds__(NTHREADS, KIVI_CTAS)
 decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_constant__ CUtensorMap tm_ks,
                    const __grid_constant__ CUtensorMap tm_vc, const __grid_constant__ CUtensorMap tm_vs,
                    const DecodeParams p) {

@@ -14,7 +14,7 @@ import threading
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(os.path.dirname(_HERE), "libkivi_sm100.so")
+LIB_PATH = os.environ.get("KIVI_LIB_PATH") or os.path.join(os.path.dirname(_HERE), "libkivi_sm100.so")
 
 FMT = {"int4": 0, "int3": 1, "nvfp4": 2}
 CALIB = {"absmax": 0, "mse": 1}
