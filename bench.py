@@ -145,6 +145,86 @@ def cpu_reference(S: int, steps: int, warmup: int, budget_s: float = 60.0):
     return gbs, text, oracle.num_threads(), t
 
 
+def graph_step(fn, warm: int = 3):
+    """Capture fn() (one decode step; sync-free) into a CUDA graph."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
+
+
+def time_graph(g, seconds: float = 1.5) -> float:
+    """Device ms per replay, CUDA events around a loop sized to ~seconds."""
+    import torch
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(); g.replay(); e1.record(); torch.cuda.synchronize()
+    n = max(10, int(seconds * 1e3 / max(e0.elapsed_time(e1), 1e-3)))
+    e0.record()
+    for _ in range(n):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / n
+
+
+def extra_configs(dev, peak: float) -> dict:
+    """Secondary BASELINE configs on one GPU, each step captured in a CUDA graph:
+    c1 (INT4, S=8192) and c2 (NVFP4 at 65536 tokens: a 16-token quant-store
+    into the cache followed by decode over the whole cache)."""
+    import torch
+    from int4_kivi import store_nvfp4_kivi
+    from int4_kivi.cache import store_into, full_views
+    from int4_kivi.decode import decode_packed
+    res = {}
+    # ---- c1: INT4, S = 8192 ----
+    S1 = 8192
+    k, v, q = make_inputs(S1, seed=7, device=dev)
+    st = build_stacked(k, v)
+    del k, v
+    out = torch.empty(B, HQ, D, dtype=torch.bfloat16, device=dev)
+    g = graph_step(lambda: decode_packed(q, st, HQ, out=out))
+    ms = time_graph(g)
+    by = B * HKV * S1 * BYTES_PER_TOKEN_HEAD
+    res["int4_c1_S8192"] = {"ms_per_step": round(ms, 4), "GB/s": round(by / ms / 1e6, 1),
+                            "frac": round(by / ms / 1e6 / peak, 4), "decode_tok_s": round(B / ms * 1e3, 1)}
+    del st, g
+    # ---- c2: NVFP4, 16-token store + decode at 65536 ----
+    S2 = 65536
+    k, v, q = make_inputs(S2, seed=8, device=dev)
+    BH = B * HKV
+    c = store_nvfp4_kivi(k.reshape(BH, S2, D)[:, :S2 - 16].contiguous(), v.reshape(BH, S2, D)[:, :S2 - 16].contiguous(),
+                         "absmax", "absmax", capacity=S2)
+    k_new = k.reshape(BH, S2, D)[:, S2 - 16:].contiguous()
+    v_new = v.reshape(BH, S2, D)[:, S2 - 16:].contiguous()
+    del k, v
+    kp, ks, vp, vs = full_views(c)
+    st2 = dict(k_packed=kp[:, :, :S2 // 16], k_scale=ks[:, :, :S2 // 16],
+               k_hot=torch.empty(BH, 0, D, dtype=torch.bfloat16, device=dev),
+               v_packed=vp[:, :S2], v_scale=vs[:, :S2], H=HKV, S=S2, D=D, B=B, fmt="nvfp4", g_k=1.0, g_v=1.0)
+
+    def c2_step():
+        store_into(k_new, v_new, "nvfp4", "absmax", "absmax", kp, ks, vp, vs, (S2 - 16) // 16, S2 - 16)
+        decode_packed(q, st2, HQ, out=out)
+    g2 = graph_step(c2_step)
+    ms2 = time_graph(g2)
+    by2 = BH * S2 * 144 + 2 * BH * 16 * D * 2 + BH * 16 * 144
+    res["nvfp4_c2_S65536_store16"] = {"ms_per_step": round(ms2, 4), "GB/s": round(by2 / ms2 / 1e6, 1),
+                                      "frac": round(by2 / ms2 / 1e6 / peak, 4),
+                                      "decode_tok_s": round(B / ms2 * 1e3, 1),
+                                      "bytes_per_step": by2}
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -237,6 +317,7 @@ def main():
         gbs = world * packed_bytes / (ms * 1e-3) / 1e9
         achieved = packed_bytes / (ms * 1e-3) / 1e9
         cpu_gbs, sample, thr, _ = cpu_reference(S, 3, 1, budget_s=15.0)
+        extra = extra_configs(dev, peak) if world == 1 else None
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
@@ -256,6 +337,7 @@ def main():
                     "ms_per_step": round(ms_e2e, 4), "note": "packed KV cache resident; q in, out back"},
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
+            "other_configs": extra,
             "cpu_baseline": {"value": round(cpu_gbs, 4), "unit": "GB/s", "cores": thr, "kind": "port",
                              "sample": sample},
         }

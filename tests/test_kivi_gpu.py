@@ -261,3 +261,24 @@ def test_decode_large_context_property(cuda_dev):
 def test_device_status_clear(cuda_dev):
     from int4_kivi import _native
     assert _native.device_status(cuda_dev) == 0
+
+
+def test_decode_cuda_graph_replay(cuda_dev):
+    """The decode step is sync-free: captured in a CUDA graph and replayed with
+    new query values it matches the eager call bit for bit."""
+    from int4_kivi.decode import decode_packed, stack_caches
+    k, v, q = gen_kv(8, 2000, D, seed=31, Hq=32, B=2)
+    st = stack_caches([_store("int4", k[b], v[b], cuda_dev) for b in range(2)])
+    qd = q[:, :, 0].to(cuda_dev).contiguous()
+    out = torch.empty(2, 32, D, dtype=torch.bfloat16, device=cuda_dev)
+    decode_packed(qd, st, 32, out=out)          # warm-up allocates the workspace
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        decode_packed(qd, st, 32, out=out)
+    q2 = torch.randn(2, 32, D, generator=torch.Generator().manual_seed(5)).bfloat16()
+    qd.copy_(q2.to(cuda_dev))
+    g.replay()
+    torch.cuda.synchronize()
+    want = decode_packed(qd, st, 32)
+    assert torch.equal(out, want)
