@@ -242,6 +242,17 @@ __device__ __forceinline__ uint32_t e2m1x2_to_h2(uint32_t byte_in_low8) {
     asm("{ .reg .b8 t; cvt.u8.u32 t, %1; cvt.rn.f16x2.e2m1x2 %0, t; }" : "=r"(d) : "r"(byte_in_low8));
     return d;
 }
+// Four e2m1 pairs (one 32-bit word) -> four fp16x2 values, byte i -> h_i.
+__device__ __forceinline__ void e2m1x8_to_h2x4(uint32_t w, uint32_t& h0, uint32_t& h1, uint32_t& h2,
+                                               uint32_t& h3) {
+    asm("{ .reg .b8 a, b, c, d;\n"
+        "  mov.b32 {a, b, c, d}, %4;\n"
+        "  cvt.rn.f16x2.e2m1x2 %0, a;\n"
+        "  cvt.rn.f16x2.e2m1x2 %1, b;\n"
+        "  cvt.rn.f16x2.e2m1x2 %2, c;\n"
+        "  cvt.rn.f16x2.e2m1x2 %3, d; }"
+        : "=r"(h0), "=r"(h1), "=r"(h2), "=r"(h3) : "r"(w));
+}
 __device__ __forceinline__ uint32_t e4m3x2_to_h2(uint16_t two) {
     uint32_t d;
     asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(two));

@@ -90,8 +90,8 @@ template <int FMT>
 __device__ __forceinline__ void codes4(uint32_t w, uint32_t& t0_lo, uint32_t& t0_hi,
                                        uint32_t& t1_lo, uint32_t& t1_hi) {
     if (FMT == FMT_NVFP4) {
-        uint32_t h0 = e2m1x2_to_h2(w & 0xFF), h1 = e2m1x2_to_h2((w >> 8) & 0xFF);
-        uint32_t h2 = e2m1x2_to_h2((w >> 16) & 0xFF), h3 = e2m1x2_to_h2(w >> 24);
+        uint32_t h0, h1, h2, h3;
+        e2m1x8_to_h2x4(w, h0, h1, h2, h3);
         t0_lo = __byte_perm(h0, h2, 0x5410);
         t0_hi = __byte_perm(h0, h2, 0x7632);
         t1_lo = __byte_perm(h1, h3, 0x5410);
@@ -137,11 +137,12 @@ __device__ __forceinline__ void mma_pair(float (&c0)[4], float (&c1)[4], uint32_
 // the first page (K) / d-block (V) of the M-tile's rows, columns n >= 4 the
 // same heads scaled for the second, so one MMA serves both halves of the tile;
 // each thread later keeps the half that matches its rows.
+template <int FMT>
 __device__ __forceinline__ void mma_raw(float (&c0)[4], float (&c1)[4], uint32_t wA, uint32_t wB,
                                         uint32_t b0, uint32_t b1) {
     uint32_t a0l, a0h, a1l, a1h, c0l, c0h, c1l, c1h;
-    codes4<FMT_INT4>(wA, a0l, a0h, a1l, a1h);
-    codes4<FMT_INT4>(wB, c0l, c0h, c1l, c1h);
+    codes4<FMT>(wA, a0l, a0h, a1l, a1h);
+    codes4<FMT>(wB, c0l, c0h, c1l, c1h);
     mma_f16(c0, a0l, a0h, c0l, c0h, b0, b1);
     mma_f16(c1, a1l, a1h, c1l, c1h, b0, b1);
 }
@@ -353,7 +354,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                     s2 = __shfl_sync(0xffffffffu, s2, src_k);
                     s3 = __shfl_sync(0xffffffffu, s3, src_k);
                 }
-                if constexpr (PAIRED) {
+                if constexpr (PAIRED && FMT == FMT_INT4) {
                     uint32_t h0, l0_, h1, l1_, h2, l2_, h3, l3_;
                     split_prod(qB[2 * j][0], s0, h0, l0_);
                     split_prod(qB[2 * j][1], s1, h1, l1_);
@@ -372,7 +373,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                 ca[e] = qa[0][e] + qa[1][e];
                 cb[e] = qb[0][e] + qb[1][e];
             }
-            if constexpr (PAIRED) {
+            if constexpr (PAIRED && FMT == FMT_INT4) {
                 // keep the column half that matches my rows' page; after this
                 // every lane holds heads 2(tq&1), 2(tq&1)+1 of its rows
                 const bool mine = (g < 4) == (tq < 2);
@@ -456,7 +457,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                             sb = (t0 + 9 < limit) ? sb : (t0 + 8 < limit ? (sb & 0x0000FFFFu) : 0u);
                         }
                         if constexpr (PAIRED) {
-                            mma_raw(acc[2 * sg], acc[2 * sg + 1], hs ? w2 : w0, hs ? w3 : w1,
+                            mma_raw<FMT>(acc[2 * sg], acc[2 * sg + 1], hs ? w2 : w0, hs ? w3 : w1,
                                     hmul2u(b0, sa), hmul2u(b1, sb));
                         } else {
                             mma_pair<FMT, false>(acc[2 * sg], acc[2 * sg + 1], hs ? w2 : w0, hs ? w3 : w1, sa, sb, b0, b1);
@@ -819,7 +820,9 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
                               CU_TENSOR_MAP_SWIZZLE_NONE);
             }
             if (!ok) return KIVI_ERR_CUDA;
-            if (fmt == FMT_NVFP4)
+            if (fmt == FMT_NVFP4 && G <= 4)
+                decode_fast_kernel<FMT_NVFP4, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>(), st>>>(tkc, tks, tvc, tvs, p);
+            else if (fmt == FMT_NVFP4)
                 decode_fast_kernel<FMT_NVFP4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>(), st>>>(tkc, tks, tvc, tvs, p);
             else if (G <= 4)
                 decode_fast_kernel<FMT_INT4, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>(), st>>>(tkc, tks, tvc, tvs, p);
