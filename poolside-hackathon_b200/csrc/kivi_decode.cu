@@ -472,6 +472,8 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
         if (lane == 0) mbar_arrive(&ctl->empty[s]);
     }
     if (cur >= 0 && !ctl->abort) flush(cur);
+    // let the dependent merge kernel start its prologue (programmatic launch)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -602,6 +604,9 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         for (int o = 16; o > 0; o >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, o);
         if (lane == 0) w[ns + j] = sdot * sc2;
     }
+    // partial slots are produced by the split kernel launched just before
+    // (programmatic dependent launch): wait for its results to be visible
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     auto slot = [&](int i) -> int64_t {
         return ((int64_t)(c_lo + i / NWARP_C + bh) * NWARP_C + (i % NWARP_C)) * G + h;
     };
@@ -844,8 +849,20 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     const size_t csm = ((size_t)max_ctas * NWARP_C + 16 + 8) * sizeof(float);
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
     const dim3 cgrid(BH, G);
-    if (fmt == FMT_NVFP4) combine_kernel<FMT_NVFP4><<<cgrid, 128, csm, st>>>(p, mode, o, m_out, l_out, acc_out);
-    else combine_kernel<FMT_INT4><<<cgrid, 128, csm, st>>>(p, mode, o, m_out, l_out, acc_out);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = cgrid;
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = csm;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t le = (fmt == FMT_NVFP4)
+        ? cudaLaunchKernelEx(&cfg, combine_kernel<FMT_NVFP4>, p, mode, o, m_out, l_out, acc_out)
+        : cudaLaunchKernelEx(&cfg, combine_kernel<FMT_INT4>, p, mode, o, m_out, l_out, acc_out);
+    if (le != cudaSuccess) return record_cuda_error(le);
     return check_launch();
 }
 
