@@ -225,6 +225,79 @@ def extra_configs(dev, peak: float) -> dict:
     return res
 
 
+def longctx_main(args, rank: int, world: int, local: int) -> None:
+    """Config 4: B=1, S=262144, INT4; the KV sequence is split in page-aligned
+    ranges across ranks; one step (captured in a CUDA graph) = local split-K
+    decode to (m, l, acc), NCCL all-gather of the partial states, log-sum-exp
+    merge.  Total work is fixed (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+    from int4_kivi import store_kivi
+    from int4_kivi.distributed import seq_parallel_decode, split_tokens
+    from int4_kivi.decode import decode_packed
+    S = 262144
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    a, b = split_tokens(S, world, rank)
+    g = torch.Generator(device=dev).manual_seed(4242 + rank)
+    f = torch.exp(torch.empty(1, HKV, 1, D, device=dev).uniform_(math.log(0.5), math.log(8.0), generator=g))
+    k = (torch.randn(HKV, b - a, D, device=dev, generator=g) * f[0]).bfloat16()
+    v = torch.randn(HKV, b - a, D, device=dev, generator=g).bfloat16()
+    gq = torch.Generator(device=dev).manual_seed(99)
+    q = torch.randn(1, HQ, D, device=dev, generator=gq).bfloat16()
+    c = store_kivi(k, v, "absmax", "absmax")
+    del k, v
+    st = dict(k_packed=c.k_packed, k_scale=c.k_scale, k_hot=c.k_hot, v_packed=c.v_packed, v_scale=c.v_scale,
+              H=HKV, S=b - a, D=D, B=1)
+
+    def step():
+        if world > 1:
+            return seq_parallel_decode(q, st, HQ)
+        return decode_packed(q, st, HQ)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    gr = graph_step(step)
+    barrier()
+    steps = min(args.steps, 2000)
+    for _ in range(3):
+        gr.replay()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        gr.replay()
+    e1.record()
+    barrier()
+    ms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = ms.item()
+    if rank == 0:
+        by = HKV * S * BYTES_PER_TOKEN_HEAD
+        peak, kind = _peaks()
+        line = {"metric": "packed-KV HBM GB/s (INT4-KIVI decode, one 262144-token sequence)",
+                "value": round(by / ms / 1e6, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int4 codes, f16 MMA, f32 accumulate",
+                "data": "synthetic (seeded, config-0 distribution)",
+                "config": {"workload": "c4: B=1, S=262144, Hq=32, Hkv=8, D=128, sequence split across GPUs",
+                           "parallelism": f"sequence-parallel x{world} + NCCL all_gather of (m,l,acc)"},
+                "decode_tok_s": round(1 / ms * 1e3, 1),
+                "per_gpu_frac_of_roof": round(by / world / ms / 1e6 / peak, 4)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -232,6 +305,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq", type=int, default=65536)
+    ap.add_argument("--workload", default="batch", choices=["batch", "longctx"],
+                    help="batch: B=8 sequences per GPU (weak scaling, no collective); "
+                         "longctx: one 262144-token sequence split across GPUs with an NCCL (m,l,o) merge")
     args = ap.parse_args()
     S = args.seq
     rank = int(os.environ.get("RANK", "0"))
@@ -239,6 +315,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     workload = f"INT4-KIVI fused decode, B={B}/GPU, Hq={HQ}, Hkv={HKV}, D={D}, S={S}"
 
+    if args.workload == "longctx" and args.impl == "ours":
+        return longctx_main(args, rank, world, local)
     if args.impl == "reference":
         if rank != 0:
             return

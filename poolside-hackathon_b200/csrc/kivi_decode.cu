@@ -635,6 +635,30 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     __syncthreads();
     Ls = (red[4] + red[5]) + (red[6] + red[7]);
     const int64_t row = (int64_t)b * p.Hq + kvh * G + h;
+    if (D == DH && ns >= 16) {
+        // many slots (long single sequences): warps split the slots, each lane
+        // owns 4 channels (float4 loads), then a shared-memory reduction
+        float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = warp; i < ns; i += 4) {
+            const float4 v4 = *reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane);
+            const float wi = w[i];
+            a4.x += v4.x * wi; a4.y += v4.y * wi; a4.z += v4.z * wi; a4.w += v4.w * wi;
+        }
+        float* sacc = red + 8;                           // [4][128]
+        *reinterpret_cast<float4*>(sacc + warp * DH + 4 * lane) = a4;
+        __syncthreads();
+        const int d = threadIdx.x;
+        float a = (sacc[d] + sacc[DH + d]) + (sacc[2 * DH + d] + sacc[3 * DH + d]);
+        for (int j = 0; j < hot; ++j) {
+            const int64_t vr = ((int64_t)bh * p.v_s_stride + p.n_full + j) * ND + d / BLK;
+            const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
+            a += w[ns + j] * (gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v));
+        }
+        if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
+        else acc_out[row * D + d] = a;
+        if (mode == 1 && threadIdx.x == 0) { m_out[row] = M; l_out[row] = Ls; }
+        return;
+    }
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float a = 0.f;
         for (int i = 0; i < ns; ++i) a += p.part_acc[slot(i) * D + d] * w[i];
@@ -846,7 +870,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
         const int64_t per = std::max<int64_t>(pl.W / pl.N, 1);
         max_ctas = (int)((pl.T + per - 1) / per) + 1;
     }
-    const size_t csm = ((size_t)max_ctas * NWARP_C + 16 + 8) * sizeof(float);
+    const size_t csm = ((size_t)max_ctas * NWARP_C + 16 + 8 + 4 * DH) * sizeof(float);
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
     const dim3 cgrid(BH, G);
     cudaLaunchConfig_t cfg = {};

@@ -1,0 +1,48 @@
+"""Sequence-parallel decode across 2 GPUs (NCCL): each rank decodes its
+page-aligned KV range to a partial (m, l, acc), the states are all-gathered and
+merged; the result must match the single-GPU decode of the whole sequence.
+Skipped when fewer than 2 GPUs are visible."""
+import os
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from conftest import gen_kv
+
+pytestmark = pytest.mark.gpu
+
+
+def _rank(rank, world, port, k, v, q, ret):
+    import torch.distributed as dist
+    from int4_kivi import store_kivi
+    from int4_kivi.distributed import seq_parallel_decode, split_tokens
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    a, b = split_tokens(k.shape[1], world, rank)
+    c = store_kivi(k[:, a:b].contiguous().to(dev), v[:, a:b].contiguous().to(dev))
+    st = dict(k_packed=c.k_packed, k_scale=c.k_scale, k_hot=c.k_hot, v_packed=c.v_packed, v_scale=c.v_scale,
+              H=c.H, S=c.S, D=c.D, B=1)
+    out = seq_parallel_decode(q.to(dev), st, q.shape[1])
+    ret[rank] = out.cpu()
+    dist.destroy_process_group()
+
+
+def test_seq_parallel_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from int4_kivi import store_kivi
+    from int4_kivi.decode import decode_packed
+    k, v, q = gen_kv(8, 5000, 128, seed=77, Hq=32)
+    q = q[None, :, 0]
+    ret = mp.Manager().dict()
+    mp.spawn(_rank, args=(2, 29600 + os.getpid() % 300, k, v, q, ret), nprocs=2, join=True)
+    c = store_kivi(k.cuda(), v.cuda())
+    st = dict(k_packed=c.k_packed, k_scale=c.k_scale, k_hot=c.k_hot, v_packed=c.v_packed, v_scale=c.v_scale,
+              H=8, S=5000, D=128, B=1)
+    want = decode_packed(q.cuda(), st, 32).cpu().float()
+    for r in range(2):
+        got = ret[r].float()
+        assert bool(((got - want).abs() <= 2e-3 + want.abs() * 2.0 ** -7).all())
