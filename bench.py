@@ -294,8 +294,14 @@ def longctx_main(args, rank: int, world: int, local: int) -> None:
                 "decode_tok_s": round(1 / ms * 1e3, 1),
                 "per_gpu_frac_of_roof": round(by / world / ms / 1e6 / peak, 4)}
         print(json.dumps(line), flush=True)
+    # Release the captured graph (it holds NCCL work) before tearing down; a
+    # process-group destroy with a live captured collective can block at exit.
+    del gr
+    torch.cuda.synchronize()
     if world > 1:
-        dist.destroy_process_group()
+        dist.barrier()
+        sys.stdout.flush()
+        os._exit(0)
 
 
 def main():
