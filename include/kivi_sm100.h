@@ -135,6 +135,24 @@ int kivi_decode(const void *q, int64_t q_sb, int64_t q_sh,
                 kivi_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* Variable-length batch decode.  Same as kivi_decode, but batch entry b      */
+/* attends only its first seq_lens[b] tokens (device int32 [B], each in      */
+/* [0, S_max]); pages, V tokens and the <16-token bf16 tail (k_hot[bh, 0:    */
+/* seq_lens[b] % 16]) of every sequence live in the stacked layout sized for */
+/* S_max.  Generalises the equal-length stacking of int4_kivi/decode.py:480- */
+/* 491 (the reference requires one S for the whole batch); sync-free, the    */
+/* per-head tile table is built on the device.                               */
+/* ------------------------------------------------------------------------ */
+int kivi_decode_varlen(const void *q, int64_t q_sb, int64_t q_sh,
+                       const uint8_t *k_packed, const void *k_scale, int k_np_stride,
+                       const void *k_hot, int hot_stride,
+                       const uint8_t *v_packed, const void *v_scale, int v_s_stride,
+                       const int *seq_lens, int B, int Hq, int Hkv, int S_max, int D, int fmt,
+                       float sm_scale, float g_k, float g_v,
+                       void *out, float *work, int64_t work_floats, int *err,
+                       kivi_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Partial-state variant for sequence-parallel decode across GPUs: instead   */
 /* of bf16 output, writes this rank's merged (m, l, acc) per (b, q-head):     */
 /* m_out/l_out fp32 [B*Hq] (m in log2 units of the scaled score), acc_out    */

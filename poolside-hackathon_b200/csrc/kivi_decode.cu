@@ -60,9 +60,79 @@ struct DecodeParams {
     int N;               // CTAs of the main kernel
     float* part_m; float* part_l; float* part_acc;
     int* err;
+    // varlen: per-sequence lengths (device, nullable) and the per-head tile
+    // offsets [B*Hkv + 1] the prologue kernel derives from them
+    const int* seq_lens;
+    int* tile_off;
 };
 
 __host__ __device__ inline int64_t tile_start(int64_t c, int64_t W, int N) { return c * W / N; }
+
+// Per-head geometry: uniform caches use (S, n_full, hot, T); varlen caches
+// read the sequence length of the head's batch entry.
+__device__ __forceinline__ int head_len(const DecodeParams& p, int bh) {
+    return p.seq_lens ? min(max(p.seq_lens[bh / p.Hkv], 0), p.S) : p.S;
+}
+__device__ __forceinline__ int64_t total_tiles(const DecodeParams& p) {
+    return p.tile_off ? (int64_t)p.tile_off[p.B * p.Hkv] : p.W;
+}
+__device__ __forceinline__ int64_t head_tile0(const DecodeParams& p, int bh) {
+    return p.tile_off ? (int64_t)p.tile_off[bh] : (int64_t)bh * p.T;
+}
+// Walk (head, tile) over a CTA's contiguous slice of the flattened tile list.
+struct TileCursor {
+    int bh, tl, T;
+    __device__ __forceinline__ void init(const DecodeParams& p, int64_t i) {
+        if (!p.tile_off) { bh = (int)(i / p.T); tl = (int)(i % p.T); T = p.T; return; }
+        int lo = 0, hi = p.B * p.Hkv - 1;            // last head with tile_off[bh] <= i
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (p.tile_off[mid] <= i) lo = mid; else hi = mid - 1;
+        }
+        bh = lo;
+        while (p.tile_off[bh + 1] <= i) ++bh;         // skip heads without tiles
+        tl = (int)(i - p.tile_off[bh]);
+        T = p.tile_off[bh + 1] - p.tile_off[bh];
+    }
+    __device__ __forceinline__ void next(const DecodeParams& p) {
+        if (++tl < T) return;
+        tl = 0;
+        ++bh;
+        if (p.tile_off) {
+            const int BH = p.B * p.Hkv;
+            while (bh < BH && p.tile_off[bh + 1] == p.tile_off[bh]) ++bh;
+            T = bh < BH ? p.tile_off[bh + 1] - p.tile_off[bh] : 1;
+        }
+    }
+};
+
+// Varlen prologue: tile_off[bh] = sum of ceil(full pages / 8) over earlier heads.
+__global__ void __launch_bounds__(1024) tile_offsets_kernel(const int* seq_lens, int B, int Hkv, int S,
+                                                            int* tile_off) {
+    __shared__ int part[1024];
+    const int BH = B * Hkv, t = threadIdx.x;
+    const int chunk = (BH + 1023) / 1024, a = t * chunk, e = min(a + chunk, BH);
+    int sum = 0;
+    for (int bh = a; bh < e; ++bh) {
+        const int L = min(max(seq_lens[bh / Hkv], 0), S);
+        sum += ((L / 16) * 16 + 127) / 128;
+    }
+    part[t] = sum;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {               // inclusive scan
+        const int v = t >= o ? part[t - o] : 0;
+        __syncthreads();
+        part[t] += v;
+        __syncthreads();
+    }
+    int run = part[t] - sum;                           // exclusive prefix of my chunk
+    for (int bh = a; bh < e; ++bh) {
+        tile_off[bh] = run;
+        const int L = min(max(seq_lens[bh / Hkv], 0), S);
+        run += ((L / 16) * 16 + 127) / 128;
+    }
+    if (t == 1023) tile_off[BH] = part[1023];
+}
 
 template <int FMT>
 struct StageLayout {
@@ -185,7 +255,9 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = blockIdx.x;
-    const int64_t i0 = tile_start(c, p.W, p.N), i1 = tile_start(c + 1, p.W, p.N);
+    const int64_t Wt = total_tiles(p);
+    const int64_t i0 = tile_start(c, Wt, p.N), i1 = tile_start(c + 1, Wt, p.N);
+    if (i0 >= i1) return;                    // varlen grids can hold idle CTAs
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NST; ++s) { mbar_init(&ctl->full[s], 1); mbar_init(&ctl->empty[s], NWARP_C); }
@@ -199,8 +271,10 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
         if (lane == 0) {
             prefetch_tmap(&tm_kc); prefetch_tmap(&tm_ks); prefetch_tmap(&tm_vc); prefetch_tmap(&tm_vs);
             int it = 0;
-            int bh = (int)(i0 / p.T), tl = (int)(i0 % p.T);
-            for (int64_t i = i0; i < i1; ++i, ++it, (++tl == p.T ? (tl = 0, ++bh) : 0)) {
+            TileCursor cu;
+            cu.init(p, i0);
+            for (int64_t i = i0; i < i1; ++i, ++it, cu.next(p)) {
+                const int bh = cu.bh, tl = cu.tl;
                 const int s = it % NST;
                 if (!mbar_wait_bounded(&ctl->empty[s], ((it / NST) & 1) ^ 1)) {
                     set_err(p.err, KIVI_ERR_TIMEOUT);
@@ -215,13 +289,6 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                 else tma_load_2d(st + L::KS, &tm_ks, &ctl->full[s], tl * 8, bh * DH);
                 const int vrow = bh * p.v_s_stride + tl * TILE;
                 tma_load_2d(st + L::VC, &tm_vc, &ctl->full[s], 0, vrow);
-                if (PF_DIST > 0 && i + PF_DIST < i1) {
-                    // warm L2 with the tile PF_DIST ahead (same head or the next one)
-                    int ptl = tl + PF_DIST, pbh = bh;
-                    while (ptl >= p.T) { ptl -= p.T; ++pbh; }
-                    tma_prefetch_2d(&tm_kc, ptl * 64, pbh * DH);
-                    tma_prefetch_2d(&tm_vc, 0, pbh * p.v_s_stride + ptl * TILE);
-                }
                 if (FMT == FMT_NVFP4) tma_load_2d(st + L::VS, &tm_vs, &ctl->full[s], 0, vrow >> 1);
                 else tma_load_2d(st + L::VS, &tm_vs, &ctl->full[s], 0, vrow);
             }
@@ -277,9 +344,13 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
     };
 
     int it = 0;
-    int bh = (int)(i0 / p.T), tl = (int)(i0 % p.T);
-    for (int64_t i = i0; i < i1; ++i, ++it, (++tl == p.T ? (tl = 0, ++bh) : 0)) {
+    TileCursor cu;
+    cu.init(p, i0);
+    int n_full_h = 0;
+    for (int64_t i = i0; i < i1; ++i, ++it, cu.next(p)) {
+        const int bh = cu.bh, tl = cu.tl;
         if (bh != cur) {
+            n_full_h = (head_len(p, bh) / BLK) * BLK;
             if (cur >= 0) flush(cur);
             cur = bh;
             m0 = m1 = -INFINITY; l0 = l1 = 0.f;
@@ -322,7 +393,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
         }
 
         const int t_span = tl * TILE + 32 * warp;      // first token of my span
-        const int limit = p.n_full - t_span;           // valid tokens in my span
+        const int limit = n_full_h - t_span;           // valid tokens in my span
         // Full spans take the branch-free body; only a sequence's last tile is masked.
         auto span = [&](auto masked_tag) {
             constexpr bool MASKED = decltype(masked_tag)::value;
@@ -498,7 +569,8 @@ template <int FMT>
 __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = blockIdx.x, G = p.G, D = p.D, ND = D / BLK;
-    const int64_t i0 = tile_start(c, p.W, p.N), i1 = tile_start(c + 1, p.W, p.N);
+    const int64_t Wt = total_tiles(p);
+    const int64_t i0 = tile_start(c, Wt, p.N), i1 = tile_start(c + 1, Wt, p.N);
     const float sc2 = p.sm_scale * 1.4426950408889634f;
     float q[GEN_MAXG][GEN_MAXC], acc[GEN_MAXG][GEN_MAXC], m[GEN_MAXG], l[GEN_MAXG];
     int cur = -1;
@@ -512,9 +584,13 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeParams 
             }
         }
     };
-    for (int64_t i = i0; i < i1; ++i) {
-        const int bh = (int)(i / p.T), tl = (int)(i % p.T);
+    TileCursor cu;
+    if (i0 < i1) cu.init(p, i0);
+    int n_full_h = 0;
+    for (int64_t i = i0; i < i1; ++i, cu.next(p)) {
+        const int bh = cu.bh, tl = cu.tl;
         if (bh != cur) {
+            n_full_h = (head_len(p, bh) / BLK) * BLK;
             if (cur >= 0) flush(cur);
             cur = bh;
             const int b = bh / p.Hkv, kvh = bh % p.Hkv;
@@ -528,7 +604,7 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeParams 
                 }
             }
         }
-        const int t_end = min(p.n_full, tl * TILE + 32 * warp + 32);
+        const int t_end = min(n_full_h, tl * TILE + 32 * warp + 32);
         for (int t = tl * TILE + 32 * warp; t < t_end; ++t) {
             float kv[GEN_MAXC], vv[GEN_MAXC];
             const int pg = t / BLK, j = t % BLK;
@@ -568,10 +644,9 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeParams 
 // reduces its channels over the slots with coalesced loads.
 // mode 0 -> normalised bf16 out; mode 1 -> merged (m, l, acc) records.
 // ---------------------------------------------------------------------------
-__host__ __device__ inline void head_cta_range(int bh, int T, int64_t W, int N, int& c_lo, int& c_hi) {
+__host__ __device__ inline void head_cta_range(int64_t a0, int64_t a1, int64_t W, int N, int& c_lo, int& c_hi) {
     c_lo = 0; c_hi = -1;
-    if (W <= 0) return;
-    const int64_t a0 = (int64_t)bh * T, a1 = a0 + T;
+    if (W <= 0 || a1 <= a0) return;
     int64_t cc = (a0 * N) / W;
     while (cc + 1 < N && tile_start(cc + 1, W, N) <= a0) ++cc;
     while (cc > 0 && tile_start(cc, W, N) > a0) --cc;
@@ -586,10 +661,13 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
                                                       float* m_out, float* l_out, float* acc_out) {
     extern __shared__ float csm[];
     const int bh = blockIdx.x, h = blockIdx.y, b = bh / p.Hkv, kvh = bh % p.Hkv;
-    const int G = p.G, D = p.D, ND = D / BLK, hot = p.hot;
+    const int G = p.G, D = p.D, ND = D / BLK;
+    const int Lh = head_len(p, bh), n_full = (Lh / BLK) * BLK, hot = Lh - n_full;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int c_lo, c_hi;
-    head_cta_range(bh, p.T, p.W, p.N, c_lo, c_hi);
+    int c_lo = 0, c_hi = -1;
+    const int64_t Wt = total_tiles(p);
+    const int64_t a0 = head_tile0(p, bh), a1 = head_tile0(p, bh + 1);
+    if (Wt > 0 && a1 > a0) head_cta_range(a0, a1, Wt, p.N, c_lo, c_hi);
     const int ns = (c_hi - c_lo + 1) * NWARP_C;          // partial slots of this head
     float* w = csm;                                      // [ns + 16] weights (slots, then hot tokens)
     float* red = csm + ns + 16;                          // [8] block reduction scratch
@@ -610,7 +688,12 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     auto slot = [&](int i) -> int64_t {
         return ((int64_t)(c_lo + i / NWARP_C + bh) * NWARP_C + (i % NWARP_C)) * G + h;
     };
-    for (int i = threadIdx.x; i < ns; i += blockDim.x) w[i] = p.part_m[slot(i)];
+    // an idle CTA (empty slice, possible on varlen grids) wrote no slots
+    auto live = [&](int i) -> bool {
+        const int64_t cc = c_lo + i / NWARP_C;
+        return tile_start(cc, Wt, p.N) < tile_start(cc + 1, Wt, p.N);
+    };
+    for (int i = threadIdx.x; i < ns; i += blockDim.x) w[i] = live(i) ? p.part_m[slot(i)] : -INFINITY;
     __syncthreads();
     // M = max over slots and hot tokens
     float M = -INFINITY;
@@ -626,7 +709,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     float Ls = 0.f;
     for (int i = threadIdx.x; i < ns + hot; i += blockDim.x) {
         const float e = exp2f(w[i] - Mr);
-        Ls += (i < ns) ? p.part_l[slot(i)] * e : e;
+        Ls += (i < ns) ? (e != 0.f ? p.part_l[slot(i)] * e : 0.f) : e;
         w[i] = e;
     }
 #pragma unroll
@@ -640,8 +723,9 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         // owns 4 channels (float4 loads), then a shared-memory reduction
         float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int i = warp; i < ns; i += 4) {
-            const float4 v4 = *reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane);
             const float wi = w[i];
+            if (wi == 0.f) continue;
+            const float4 v4 = *reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane);
             a4.x += v4.x * wi; a4.y += v4.y * wi; a4.z += v4.z * wi; a4.w += v4.w * wi;
         }
         float* sacc = red + 8;                           // [4][128]
@@ -650,7 +734,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         const int d = threadIdx.x;
         float a = (sacc[d] + sacc[DH + d]) + (sacc[2 * DH + d] + sacc[3 * DH + d]);
         for (int j = 0; j < hot; ++j) {
-            const int64_t vr = ((int64_t)bh * p.v_s_stride + p.n_full + j) * ND + d / BLK;
+            const int64_t vr = ((int64_t)bh * p.v_s_stride + n_full + j) * ND + d / BLK;
             const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
             a += w[ns + j] * (gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v));
         }
@@ -661,9 +745,9 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     }
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float a = 0.f;
-        for (int i = 0; i < ns; ++i) a += p.part_acc[slot(i) * D + d] * w[i];
+        for (int i = 0; i < ns; ++i) if (w[i] != 0.f) a += p.part_acc[slot(i) * D + d] * w[i];
         for (int j = 0; j < hot; ++j) {
-            const int64_t vr = ((int64_t)bh * p.v_s_stride + p.n_full + j) * ND + d / BLK;
+            const int64_t vr = ((int64_t)bh * p.v_s_stride + n_full + j) * ND + d / BLK;
             const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
             a += w[ns + j] * (gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v));
         }
@@ -790,7 +874,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
                 const uint8_t* v_packed, const void* v_scale, int v_s_stride, int B, int Hq, int Hkv,
                 int S, int D, int fmt, float sm_scale, float g_k, float g_v, void* out, float* m_out,
                 float* l_out, float* acc_out, float* work, int64_t work_floats, int* err,
-                kivi_stream_t stream) {
+                kivi_stream_t stream, const int* seq_lens = nullptr) {
     if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || S < 0 || D <= 0 || D % BLK) return KIVI_ERR_ARG;
     if (fmt != FMT_INT4 && fmt != FMT_NVFP4) return KIVI_ERR_ARG;
     const int G = Hq / Hkv, BH = B * Hkv;
@@ -812,8 +896,8 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     if (!fast && (G > GEN_MAXG || D > 32 * GEN_MAXC)) return KIVI_ERR_UNSUPPORTED;
     const int occ = fast ? (fmt == FMT_NVFP4 ? fast_occupancy<FMT_NVFP4>(dev) : fast_occupancy<FMT_INT4>(dev)) : 4;
     if (!occ) return record_cuda_error(cudaGetLastError());
-    const Plan pl = make_plan(BH, n_full, sms, occ);
-    const int64_t need = pl.slots * G * (2 + (int64_t)D);
+    const Plan pl = make_plan(BH, n_full, sms, occ);   // varlen: bounds from the max length S
+    const int64_t need = pl.slots * G * (2 + (int64_t)D) + (seq_lens ? BH + 2 : 0);
     if (need > 0 && (!work || work_floats < need)) return KIVI_ERR_ARG;
 
     DecodeParams p{};
@@ -827,7 +911,14 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     p.T = pl.T; p.W = pl.W; p.N = pl.N;
     p.part_m = work; p.part_l = work + pl.slots * G; p.part_acc = work + 2 * pl.slots * G;
     p.err = err;
+    p.seq_lens = seq_lens;
+    p.tile_off = seq_lens ? reinterpret_cast<int*>(work + pl.slots * G * (2 + (int64_t)D)) : nullptr;
     cudaStream_t st = (cudaStream_t)stream;
+    if (seq_lens && pl.W > 0) {
+        tile_offsets_kernel<<<1, 1024, 0, st>>>(seq_lens, B, Hkv, S, p.tile_off);
+        const int e = check_launch();
+        if (e) return e;
+    }
 
     if (pl.W > 0) {
         if (fast) {
@@ -868,7 +959,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     int max_ctas = 0;
     if (pl.W > 0) {
         const int64_t per = std::max<int64_t>(pl.W / pl.N, 1);
-        max_ctas = (int)((pl.T + per - 1) / per) + 1;
+        max_ctas = seq_lens ? pl.N + 1 : (int)((pl.T + per - 1) / per) + 1;
     }
     const size_t csm = ((size_t)max_ctas * NWARP_C + 16 + 8 + 4 * DH) * sizeof(float);
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
@@ -897,7 +988,19 @@ extern "C" int64_t kivi_decode_workspace_floats(int B, int Hq, int Hkv, int S, i
     int sms = num_sms(nullptr);
     if (!sms) sms = 148;
     const Plan pl = make_plan(B * Hkv, (S / BLK) * BLK, sms, MAX_CTAS_PER_SM);
-    return pl.slots * (Hq / Hkv) * (2 + (int64_t)D);
+    return pl.slots * (Hq / Hkv) * (2 + (int64_t)D) + B * Hkv + 2;   // + varlen tile table
+}
+
+extern "C" int kivi_decode_varlen(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,
+                                  const void* k_scale, int k_np_stride, const void* k_hot, int hot_stride,
+                                  const uint8_t* v_packed, const void* v_scale, int v_s_stride,
+                                  const int* seq_lens, int B, int Hq, int Hkv, int S_max, int D, int fmt,
+                                  float sm_scale, float g_k, float g_v, void* out, float* work,
+                                  int64_t work_floats, int* err, kivi_stream_t stream) {
+    if (!seq_lens) return KIVI_ERR_ARG;
+    return decode_impl(0, q, q_sb, q_sh, k_packed, k_scale, k_np_stride, k_hot, hot_stride, v_packed, v_scale,
+                       v_s_stride, B, Hq, Hkv, S_max, D, fmt, sm_scale, g_k, g_v, out, nullptr, nullptr, nullptr,
+                       work, work_floats, err, stream, seq_lens);
 }
 
 extern "C" int kivi_decode(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,

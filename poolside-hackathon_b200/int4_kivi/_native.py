@@ -57,6 +57,8 @@ def lib():
             L.kivi_decode_partial.argtypes = [P, I64, I64, P, P, I, P, I, P, P, I, I, I, I, I, I, I, F, F,
                                               F, P, P, P, P, I64, P, P]
             L.kivi_lse_merge.argtypes = [P, P, P, I, I, I, P, P]
+            L.kivi_decode_varlen.argtypes = [P, I64, I64, P, P, I, P, I, P, P, I, P, I, I, I, I, I, I, F, F,
+                                             F, P, P, I64, P, P]
             _lib = L
     return _lib
 

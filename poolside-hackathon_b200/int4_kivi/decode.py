@@ -89,6 +89,16 @@ def decode_packed(q: Tensor, st: dict, n_qh: int, sm_scale: Optional[float] = No
         return m, l, acc
     if out is None:
         out = torch.empty((B, n_qh, D), dtype=torch.bfloat16, device=dev)
+    if st.get("seq_lens") is not None:
+        sl = st["seq_lens"]
+        assert sl.is_cuda and sl.dtype == torch.int32 and sl.numel() == B
+        rc = L.kivi_decode_varlen(
+            N.ptr(q), q.stride(0), q.stride(1), N.ptr(st["k_packed"]), N.ptr(st["k_scale"]), nps,
+            N.ptr(khot), hot_stride, N.ptr(st["v_packed"]), N.ptr(st["v_scale"]), ss, N.ptr(sl),
+            B, n_qh, H, S, D, N.FMT[fmt], sm_scale, g_k, g_v, N.ptr(out), N.ptr(work), work.numel(),
+            N.ptr(err), N.stream_of(q))
+        N.check(rc, "kivi_decode_varlen")
+        return out
     rc = L.kivi_decode(
         N.ptr(q), q.stride(0), q.stride(1), N.ptr(st["k_packed"]), N.ptr(st["k_scale"]), nps,
         N.ptr(khot) if hot_stride else None, hot_stride, N.ptr(st["v_packed"]), N.ptr(st["v_scale"]), ss,
@@ -139,7 +149,9 @@ def stack_caches(caches: list) -> dict:
     16-aligned so the TMA fast path applies.  All caches must share S."""
     c0 = caches[0]
     H, S, D = c0.H, c0.S, c0.D
-    assert all(c.S == S and c.H == H and c.D == D for c in caches), "stack_caches needs equal S"
+    assert all(c.H == H and c.D == D for c in caches), "stack_caches needs equal H and D"
+    if any(c.S != S for c in caches):
+        return _stack_varlen(caches)
     B = len(caches)
     NP = c0.k_packed.shape[2]
     kp, ks, vp, vs = alloc_packed(B * H, S, D, c0.k_packed.device, c0.k_scale.dtype)
@@ -152,6 +164,35 @@ def stack_caches(caches: list) -> dict:
              k_hot=torch.cat([c.k_hot for c in caches], dim=0),
              v_packed=vp[:, :S], v_scale=vs[:, :S],
              H=H, S=S, D=D, NP=NP, ND=c0.v_packed.shape[2], B=B)
+    if getattr(c0, "fmt", "int4") != "int4":
+        d.update(fmt=c0.fmt, g_k=c0.g_k, g_v=c0.g_v)
+    return d
+
+
+def _stack_varlen(caches: list) -> dict:
+    """Unequal lengths (an extension over the reference, which requires one S):
+    the stacked buffers are sized for the longest sequence, each sequence's
+    bf16 tail sits in k_hot[:, :S_b % 16], and `seq_lens` (int32, device)
+    tells the decode kernel how many tokens each batch entry attends."""
+    c0 = caches[0]
+    H, D = c0.H, c0.D
+    B = len(caches)
+    S = max(c.S for c in caches)
+    NP = S // BLOCK
+    dev = c0.k_packed.device
+    kp, ks, vp, vs = alloc_packed(B * H, S, D, dev, c0.k_scale.dtype)
+    khot = torch.zeros(B * H, BLOCK, D, dtype=torch.bfloat16, device=dev)
+    for b, c in enumerate(caches):
+        npb = c.k_packed.shape[2]
+        kp[b * H:(b + 1) * H, :, :npb].copy_(c.k_packed)
+        ks[b * H:(b + 1) * H, :, :npb].copy_(c.k_scale)
+        vp[b * H:(b + 1) * H, :c.S].copy_(c.v_packed)
+        vs[b * H:(b + 1) * H, :c.S].copy_(c.v_scale)
+        if c.k_hot.shape[1]:
+            khot[b * H:(b + 1) * H, :c.k_hot.shape[1]].copy_(c.k_hot)
+    d = dict(k_packed=kp[:, :, :NP], k_scale=ks[:, :, :NP], k_hot=khot, v_packed=vp[:, :S], v_scale=vs[:, :S],
+             H=H, S=S, D=D, NP=NP, ND=c0.v_packed.shape[2], B=B,
+             seq_lens=torch.tensor([c.S for c in caches], dtype=torch.int32, device=dev))
     if getattr(c0, "fmt", "int4") != "int4":
         d.update(fmt=c0.fmt, g_k=c0.g_k, g_v=c0.g_v)
     return d

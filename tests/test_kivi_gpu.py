@@ -282,3 +282,38 @@ def test_decode_cuda_graph_replay(cuda_dev):
     torch.cuda.synchronize()
     want = decode_packed(qd, st, 32)
     assert torch.equal(out, want)
+
+
+@pytest.mark.parametrize("fmt", ["int4", "nvfp4"])
+def test_decode_varlen_batch(cuda_dev, fmt):
+    """Unequal sequence lengths in one launch (the config-3 serving shape):
+    every batch entry attends only its own tokens, hot tails included."""
+    from int4_kivi.decode import kivi_decode_attention_gqa, stack_caches
+    lens = [1, 15, 16, 17, 300, 1000, 4097]
+    Hkv, Hq = 8, 32
+    ks, vs, qs, caches = [], [], [], []
+    for i, L in enumerate(lens):
+        k, v, q = gen_kv(Hkv, L, D, seed=500 + i, Hq=Hq)
+        ks.append(k); vs.append(v); qs.append(q[:, 0])
+        caches.append(_store(fmt, k, v, cuda_dev))
+    st = stack_caches(caches)
+    assert st["seq_lens"].tolist() == lens
+    q = torch.stack(qs)
+    out = kivi_decode_attention_gqa(q.to(cuda_dev), st, Hq).cpu()
+    for i in range(len(lens)):
+        ref = _oracle_decode(ks[i][None], vs[i][None], q[i:i + 1], fmt)
+        _check_bf16(out[i:i + 1], ref)
+
+
+def test_decode_varlen_generic_path(cuda_dev):
+    from int4_kivi.decode import kivi_decode_attention_gqa, stack_caches
+    lens = [40, 333, 7]
+    ks, vs, qs, caches = [], [], [], []
+    for i, L in enumerate(lens):
+        k, v, q = gen_kv(2, L, 64, seed=700 + i, Hq=12)
+        ks.append(k); vs.append(v); qs.append(q[:, 0])
+        caches.append(_store("int4", k, v, cuda_dev))
+    q = torch.stack(qs)
+    out = kivi_decode_attention_gqa(q.to(cuda_dev), stack_caches(caches), 12).cpu()
+    for i in range(len(lens)):
+        _check_bf16(out[i:i + 1], _oracle_decode(ks[i][None], vs[i][None], q[i:i + 1], "int4"))
