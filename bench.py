@@ -304,6 +304,108 @@ def longctx_main(args, rank: int, world: int, local: int) -> None:
         os._exit(0)
 
 
+SERVE_LAYERS, SERVE_HIDDEN, SERVE_FFN = 24, 2048, 5632
+
+
+def serving_main(args, rank: int, world: int, local: int) -> None:
+    """Config 3: batch sweep 1..256, context lengths U[1K, 32K] per sequence
+    (seeded), random-init 24-layer GQA decoder (hidden 2048, 32 q / 8 kv heads,
+    head_dim 128, SwiGLU FFN 5632 -- the FFN width is this benchmark's choice,
+    BASELINE leaves it open).  Sequences are sharded across ranks by token
+    count (no collective); one step = one decode token for every sequence
+    through all 24 layers (cuBLAS GEMMs via torch + the varlen INT4 decode),
+    captured in a CUDA graph; the KV caches are fixed during the timed steps
+    (no append).  Each layer has its own cache while the total fits in 40 GB,
+    above that the layers share one cache (every layer still streams it from
+    HBM: it is far larger than L2)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from int4_kivi import store_kivi
+    from int4_kivi.decode import decode_packed
+    from int4_kivi.distributed import shard_sequences
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    L_, Hd, F_ = SERVE_LAYERS, SERVE_HIDDEN, SERVE_FFN
+    gw = torch.Generator(device=dev).manual_seed(17)
+
+    def w(i, o):
+        return (torch.randn(i, o, device=dev, generator=gw) / math.sqrt(i)).bfloat16()
+    layers = [dict(qkv=w(Hd, HQ * D + 2 * HKV * D), o=w(HQ * D, Hd), gu=w(Hd, 2 * F_), dn=w(F_, Hd))
+              for _ in range(L_)]
+    results = {}
+    rng = np.random.default_rng(3)
+    for Bg in (1, 2, 4, 8, 16, 32, 64, 128, 256):
+        lens_all = rng.integers(1024, 32769, size=Bg).tolist()
+        mine = shard_sequences(lens_all, world)[rank]
+        if not mine:
+            mine_lens = []
+        else:
+            mine_lens = [lens_all[i] for i in mine]
+        Bl = max(len(mine_lens), 1)
+        lens = mine_lens or [16]
+        S_max = max(lens)
+        per_layer = Bl * HKV * S_max * BYTES_PER_TOKEN_HEAD
+        n_caches = L_ if per_layer * L_ <= 40e9 else 1
+        caches = []
+        for li in range(n_caches):
+            g = torch.Generator(device=dev).manual_seed(1000 * Bg + li)
+            k = torch.randn(Bl * HKV, S_max, D, device=dev, generator=g).bfloat16()
+            v = torch.randn(Bl * HKV, S_max, D, device=dev, generator=g).bfloat16()
+            c = store_kivi(k, v, "absmax", "absmax")
+            khot = torch.zeros(Bl * HKV, 16, D, dtype=torch.bfloat16, device=dev)
+            for b, Lb in enumerate(lens):
+                nf = (Lb // 16) * 16
+                if Lb > nf:
+                    khot[b * HKV:(b + 1) * HKV, :Lb - nf] = k[b * HKV:(b + 1) * HKV, nf:Lb]
+            del k, v
+            NP = S_max // 16
+            caches.append(dict(k_packed=c.k_packed, k_scale=c.k_scale, k_hot=khot, v_packed=c.v_packed,
+                               v_scale=c.v_scale, H=HKV, S=S_max, D=D, B=Bl,
+                               seq_lens=torch.tensor(lens, dtype=torch.int32, device=dev)))
+        x0 = torch.randn(Bl, Hd, device=dev, generator=gw).bfloat16()
+        xbuf = x0.clone()
+        att_out = torch.empty(Bl, HQ, D, dtype=torch.bfloat16, device=dev)
+
+        def step():
+            x = xbuf.copy_(x0)
+            for li, Lw in enumerate(layers):
+                hsd = torch.nn.functional.rms_norm(x, (Hd,))
+                qkv = hsd @ Lw["qkv"]
+                q = qkv[:, :HQ * D].reshape(Bl, HQ, D)
+                decode_packed(q, caches[li % n_caches], HQ, out=att_out)
+                x = x + att_out.reshape(Bl, HQ * D) @ Lw["o"]
+                gu = torch.nn.functional.rms_norm(x, (Hd,)) @ Lw["gu"]
+                x = x + (torch.nn.functional.silu(gu[:, :F_]) * gu[:, F_:]) @ Lw["dn"]
+            return x
+        gr = graph_step(step)
+        ms = time_graph(gr, seconds=1.0)
+        t = torch.tensor([ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+        kv_bytes = sum(lens_all) * HKV * BYTES_PER_TOKEN_HEAD * L_
+        results[Bg] = {"ms_per_step": round(ms, 3), "tok_s": round(Bg / ms * 1e3, 1),
+                       "kv_GB_s": round(kv_bytes / ms / 1e6, 1), "caches_per_gpu": n_caches}
+        del gr, caches
+        torch.cuda.empty_cache()
+    if rank == 0:
+        line = {"metric": "decode tok/s, 24-layer GQA decoder with INT4-KIVI KV (serving sweep)",
+                "value": results[256]["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": None,
+                "warmup": 3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16 GEMMs, int4 KV", "data": "synthetic (random-init weights, seeded lengths U[1K,32K])",
+                "config": {"workload": "c3 serving sweep", "hidden": Hd, "ffn": F_, "layers": L_,
+                           "parallelism": f"sequence-shard x{world}"},
+                "sweep": results}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        sys.stdout.flush()
+        os._exit(0)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -311,7 +413,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq", type=int, default=65536)
-    ap.add_argument("--workload", default="batch", choices=["batch", "longctx"],
+    ap.add_argument("--workload", default="batch", choices=["batch", "longctx", "serving"],
                     help="batch: B=8 sequences per GPU (weak scaling, no collective); "
                          "longctx: one 262144-token sequence split across GPUs with an NCCL (m,l,o) merge")
     args = ap.parse_args()
@@ -323,6 +425,8 @@ def main():
 
     if args.workload == "longctx" and args.impl == "ours":
         return longctx_main(args, rank, world, local)
+    if args.workload == "serving" and args.impl == "ours":
+        return serving_main(args, rank, world, local)
     if args.impl == "reference":
         if rank != 0:
             return
