@@ -21,7 +21,7 @@ from torch import Tensor
 
 from transformers.cache_utils import Cache, CacheLayerMixin
 
-from .cache import BLOCK, KIVICache, append_kivi, dequant_kivi, store_kivi
+from .cache import BLOCK, KIVICache, alloc_packed, append_kivi, dequant_kivi, store_kivi
 
 
 class _Int4KiviLayer(CacheLayerMixin):
@@ -81,12 +81,34 @@ class _Int4KiviLayer(CacheLayerMixin):
         self.hot_k = self.hot_k[:, n_full:].contiguous()
         self.hot_v = self.hot_v[:, n_full:].contiguous()
 
-    def _evict_sliding(self) -> None:
+    def _evict_sliding(self, n_new: int) -> None:
+        """Drop whole pages from the front while the stored tokens still cover
+        what `get_mask_sizes` promises (window - 1 + the tokens of this call,
+        with one page of slack for the next call)."""
         if not self.is_sliding or self.store is None:
             return
-        keep = self.sliding_window - 1 + BLOCK
-        while self._frozen_len() - BLOCK >= keep:
-            self._offset += BLOCK       # drop whole pages from the front (view offset)
+        keep = self.sliding_window - 1 + max(BLOCK, n_new)
+        while self._frozen_len() >= BLOCK and self._stored_len() - BLOCK >= keep:
+            self._offset += BLOCK       # view offset
+        if self._offset >= 2048 and self._offset >= self._frozen_len():
+            self._compact()
+
+    def _compact(self) -> None:
+        """Move the retained pages to the front of a fresh buffer so evicted
+        pages do not accumulate over a long sliding-window generation."""
+        c, off = self.store, self._offset
+        S1 = c.S - off
+        kp, ks, vp, vs = alloc_packed(c.H, S1, c.D, c.k_packed.device, c.k_scale.dtype, s_cap=max(4 * S1, 1024))
+        NP1 = S1 // BLOCK
+        kp[:, :, :NP1].copy_(c.k_packed[:, :, off // BLOCK:])
+        ks[:, :, :NP1].copy_(c.k_scale[:, :, off // BLOCK:])
+        vp[:, :S1].copy_(c.v_packed[:, off:])
+        vs[:, :S1].copy_(c.v_scale[:, off:])
+        self.store = KIVICache(k_packed=kp[:, :, :NP1], k_scale=ks[:, :, :NP1], k_hot=c.k_hot,
+                               v_packed=vp[:, :S1], v_scale=vs[:, :S1], H=c.H, S=S1, D=c.D)
+        self._offset = 0
+        self._deq_k = self._deq_v = None
+        self._deq_len = 0
 
     def _dequant_frozen(self) -> tuple[Tensor, Tensor]:
         S = 0 if self.store is None else self.store.S
@@ -122,7 +144,7 @@ class _Int4KiviLayer(CacheLayerMixin):
             self.hot_k = torch.cat([self.hot_k, k_new], dim=1)
             self.hot_v = torch.cat([self.hot_v, v_new], dim=1)
         self._freeze_pages()
-        self._evict_sliding()
+        self._evict_sliding(n_new)
         ks, vs = [], []
         if self._frozen_len() > 0:
             fk, fv = self._dequant_frozen()
