@@ -81,8 +81,9 @@ def alloc_packed(H: int, S: int, D: int, device, scale_dtype, s_cap: Optional[in
 
 def cache_geometry(c) -> tuple[int, int]:
     """(k page stride, v token stride) of a cache's packed views; raises if the
-    tensors are not views with the (page, token)-strided layout the kernels use."""
-    kp, ks, vp, vs = c.k_packed, c.k_scale, c.v_packed, c.v_scale
+    tensors are not views with the (page, token)-strided layout the kernels use.
+    `c` is a cache object or a (k_packed, k_scale, v_packed, v_scale) tuple."""
+    kp, ks, vp, vs = c if isinstance(c, tuple) else (c.k_packed, c.k_scale, c.v_packed, c.v_scale)
     np_stride = kp.stride(1) // PACK if kp.dim() == 4 else 0
     s_stride = vp.stride(0) // (vp.shape[2] * PACK) if vp.dim() == 4 and vp.shape[2] else 0
     ok = (kp.dim() == 4 and kp.stride(3) == 1 and kp.stride(2) == PACK and kp.stride(1) == np_stride * PACK
@@ -220,7 +221,7 @@ def dequant_packed(cache) -> tuple[Tensor, Tensor]:
         np_stride, s_stride = cache_geometry(cache)
     except ValueError:
         kp, ks, vp, vs = relayout(cache)
-        np_stride, s_stride = cache_geometry(type("C", (), dict(k_packed=kp, k_scale=ks, v_packed=vp, v_scale=vs))())
+        np_stride, s_stride = cache_geometry((kp, ks, vp, vs))
     kout = torch.empty((H, S, D), dtype=torch.bfloat16, device=dev)
     vout = torch.empty((H, S, D), dtype=torch.bfloat16, device=dev)
     st = N.lib().kivi_dequant(N.ptr(kp), N.ptr(ks), np_stride, N.ptr(vp), N.ptr(vs), s_stride, H, S, D,

@@ -28,13 +28,8 @@ from .cache import BLOCK, PACK, KIVICache, alloc_packed, cache_geometry
 def _stacked_geometry(st: dict) -> tuple[int, int, dict]:
     """(page stride, token stride, tensors) for a stacked dict, re-laid out into
     aligned buffers if needed (slow path for externally built dicts)."""
-    class _V:  # attribute view for cache_geometry
-        pass
-    v = _V()
-    for f in ("k_packed", "k_scale", "v_packed", "v_scale"):
-        setattr(v, f, st[f])
     try:
-        nps, ss = cache_geometry(v)
+        nps, ss = cache_geometry((st["k_packed"], st["k_scale"], st["v_packed"], st["v_scale"]))
         return nps, ss, st
     except ValueError:
         BH, D, NP, _ = st["k_packed"].shape

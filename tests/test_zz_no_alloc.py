@@ -59,9 +59,7 @@ def test_noalloc_matches_workspace_decode_twice(cuda_dev):
     for seed, (B, Hkv, Hq, S) in ((1, (2, 8, 32, 3000)), (2, (3, 4, 16, 1037))):
         q, st = _case(cuda_dev, seed, B, Hkv, Hq, S)
 
-        class _C:
-            k_packed, k_scale, v_packed, v_scale = st["k_packed"], st["k_scale"], st["v_packed"], st["v_scale"]
-        nps, ss = cache_geometry(_C)
+        nps, ss = cache_geometry((st["k_packed"], st["k_scale"], st["v_packed"], st["v_scale"]))
         want = decode_packed(q, st, Hq)
         got = torch.empty_like(want)
         rc = L.kivi_decode_noalloc(*_args(q, st, Hq, nps, ss), N.ptr(got), N.ptr(err), N.stream_of(q))
