@@ -40,11 +40,7 @@ constexpr int NTHREADS = (NWARP_C + 1) * 32;
 #endif
 constexpr int NST = KIVI_NST;    // pipeline depth
 constexpr int DH = 128;          // head_dim of the fast path
-constexpr int PB_PITCH = 40;
-#ifndef KIVI_PF
-#define KIVI_PF 0
-#endif
-constexpr int PF_DIST = KIVI_PF; // L2 prefetch distance in tiles (0 = off)     // halves per head row in the P staging buffer
+constexpr int PB_PITCH = 40;     // halves per head row in the P staging buffer
 
 struct DecodeParams {
     const __nv_bfloat16* q; int64_t q_sb, q_sh;
