@@ -198,6 +198,63 @@ int kivi_decode_noalloc(const void *q, int64_t q_sb, int64_t q_sh,
 int kivi_lse_merge(const float *m, const float *l, const float *acc, int R, int rows,
                    int D, void *out, kivi_stream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* Paged cache (vLLM block layout).                                          */
+/*                                                                           */
+/* Replaces the fork kernels the reference calls through                     */
+/* vllm/v1/attention/ops/triton_{int4,nvfp4}_kivi.py (source not in the      */
+/* reference tree; call sites scripts/validate_paged_decode.py:59,72,91,     */
+/* scripts/validate_store_equiv.py:50-51, scripts/validate_nvfp4_kivi.py:    */
+/* 67-75,136-150, scripts/bench_paged_decode.py:97-100): int4_kivi_store,    */
+/* int4_kivi_gather_dequant, int4_kivi_paged_decode and the nvfp4_* twins.   */
+/*                                                                           */
+/* kv_cache: uint8 [num_blocks, 2, 16, H, FD], FD = kivi_paged_full_dim(D)   */
+/*   = D/2 + D/16; dim 1 = K (0) / V (1); a row is D/2 code bytes (element   */
+/*   2j in the low nibble of byte j) then D/16 e4m3 scale bytes.  V and K of */
+/*   a partial block: per token (scale j covers channels 16j..16j+15).  K of */
+/*   a full block ((b+1)*16 <= seq_len): per channel over its 16 tokens,     */
+/*   channel c's scale at row c / (D/16), byte c % (D/16).                   */
+/*   fmt INT4: codes in [-7, 7]; NVFP4: e2m1 codes (sign = bit 3).           */
+/* ------------------------------------------------------------------------ */
+int kivi_paged_full_dim(int D);
+
+/* Quantise N tokens k, v [N, H, D] (dtype in_dtype, strides in elements for */
+/* token, head, channel) into kv_cache at slot_mapping[N] (int64, device;    */
+/* slot = block * 16 + offset; negative = padding, skipped).  A call that    */
+/* writes a block's last slot quantises that block's K per channel (rows not */
+/* in the call are dequantised from the cache first); other K rows go per    */
+/* token.  calib: KIVI_CALIB_MSE (16-point e4m3 clip search) or ABSMAX.      */
+/* Out-of-range slots set *err = KIVI_ERR_ARG and are skipped.  D <= 256.    */
+int kivi_paged_store(const void *k, const void *v, int in_dtype,
+                     int64_t sk_t, int64_t sk_h, int64_t sk_d,
+                     int64_t sv_t, int64_t sv_h, int64_t sv_d,
+                     int N, int H, int D, int fmt, int calib,
+                     const int64_t *slot_mapping, uint8_t *kv_cache, int64_t num_blocks,
+                     int *err, kivi_stream_t stream);
+
+/* bf16 k_out, v_out [B, H, max_seq, D] from block_table int32 [B, bt_stride] */
+/* and seq_lens int32 [B]; positions at or past seq_len are written as 0.    */
+int kivi_paged_gather_dequant(const uint8_t *kv_cache, int64_t num_blocks,
+                              const int *block_table, int64_t bt_stride, const int *seq_lens,
+                              int B, int H, int D, int fmt, int max_seq,
+                              void *k_out, void *v_out, int *err, kivi_stream_t stream);
+
+/* Fused decode, one query token per sequence: q bf16 [B, Hq, D] (strides    */
+/* q_sb, q_sh) -> out bf16 [B, Hq, D] contiguous.  Sequence b attends its    */
+/* first min(seq_lens[b], 16 * bt_stride) tokens (0 gives zeros).  The grid  */
+/* is sized from bt_stride, never from seq_lens, so the call never reads     */
+/* device data on the host and is graph-capturable.  work: fp32 scratch of   */
+/* kivi_paged_decode_workspace_floats(B, Hq, Hkv, bt_stride, D) floats.      */
+/* Fast path: D == 128, Hkv <= 16, Hq/Hkv <= 8; otherwise a CUDA-core path.  */
+int64_t kivi_paged_decode_workspace_floats(int B, int Hq, int Hkv, int64_t bt_stride, int D);
+
+int kivi_paged_decode(const void *q, int64_t q_sb, int64_t q_sh,
+                      const uint8_t *kv_cache, int64_t num_blocks,
+                      const int *block_table, int64_t bt_stride, const int *seq_lens,
+                      int B, int Hq, int Hkv, int D, int fmt, float sm_scale,
+                      void *out, float *work, int64_t work_floats, int *err,
+                      kivi_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

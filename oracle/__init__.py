@@ -13,6 +13,9 @@ Reference behaviour restated (paths inside a1exxd0/poolside-hackathon):
   * scripts/validate_int4_kivi_decode.py:37-84 -- fp32-exact decode reference
   * scripts/diag_kernel_perchannel.py:30-48, WRITEUP.md:97-107 -- e4m3 block
     scales rounded inside the MSE search (NVFP4 variant)
+  * WRITEUP.md:82-95,117-124, scripts/validate_paged_decode.py:32-64,
+    scripts/validate_store_equiv.py:34-65 -- the paged vLLM cache layout
+    (store, gather-dequant; decode is gather + decode_attention)
 
 Pinned against the reference by tests/golden/*.npz (made by
 tests/golden/make_golden.py, which runs the reference's own Python on CPU).
@@ -65,6 +68,11 @@ def lib():
         L.orc_e4m3_to_f32.argtypes = [ctypes.c_uint8]
         L.orc_e4m3_to_f32.restype = F
         L.orc_num_threads.restype = I
+        L.orc_paged_calib.argtypes = [P, I, I]
+        L.orc_paged_calib.restype = ctypes.c_uint8
+        L.orc_paged_store.argtypes = [P, P, I, I, I, I, I, P, P, Lg]
+        L.orc_paged_store.restype = I
+        L.orc_paged_gather.argtypes = [P, Lg, P, Lg, P, I, I, I, I, I, P, P]
         _lib = L
     return _lib
 
@@ -223,3 +231,55 @@ def lse_merge(m: np.ndarray, l: np.ndarray, o: np.ndarray) -> np.ndarray:
     L = (l * w).sum(-1)
     acc = (o * w[..., None]).sum(-2)
     return (acc / L[..., None]).astype(np.float32)
+
+
+# ----------------------------------------------------------------------------
+# Paged (vLLM-style) cache: kv[num_blocks, 2, 16, H, D/2 + D/16] uint8
+# ----------------------------------------------------------------------------
+def paged_full_dim(D: int) -> int:
+    return D // 2 + D // 16
+
+
+def paged_calib(blocks, fmt: str = "int4", calib: str = "mse") -> np.ndarray:
+    """e4m3 scale bytes of blocks [..., 16] (scripts/diag_kernel_perchannel.py:30-48)."""
+    xb = _f32(blocks)
+    flat = xb.reshape(-1, BLOCK)
+    out = np.empty(flat.shape[0], np.uint8)
+    L = lib()
+    for i in range(flat.shape[0]):
+        row = np.ascontiguousarray(flat[i])
+        out[i] = L.orc_paged_calib(_p(row), FMT[fmt], CALIB[calib])
+    return out.reshape(xb.shape[:-1])
+
+
+def paged_store(k, v, slot_mapping, kv: np.ndarray, fmt: str = "int4", calib: str = "mse") -> int:
+    """Quantise k, v [N, H, D] into the uint8 cache `kv` (modified in place)."""
+    kf, vf = _f32(k), _f32(v)
+    N, H, D = kf.shape
+    sl = np.ascontiguousarray(np.asarray(slot_mapping, dtype=np.int64))
+    assert kv.dtype == np.uint8 and kv.flags.c_contiguous and kv.shape[1:] == (2, BLOCK, H, paged_full_dim(D))
+    return lib().orc_paged_store(_p(kf), _p(vf), N, H, D, FMT[fmt], CALIB[calib], _p(sl), _p(kv), kv.shape[0])
+
+
+def paged_gather(kv: np.ndarray, block_table, seq_lens, H: int, D: int, fmt: str, max_seq: int):
+    """Dequantised fp32 k, v [B, H, max_seq, D] (zeros past each sequence's length)."""
+    bt = np.ascontiguousarray(np.asarray(block_table, dtype=np.int32))
+    sl = np.ascontiguousarray(np.asarray(seq_lens, dtype=np.int32))
+    B = bt.shape[0]
+    k = np.empty((B, H, max_seq, D), np.float32)
+    v = np.empty((B, H, max_seq, D), np.float32)
+    kvc = np.ascontiguousarray(kv)
+    lib().orc_paged_gather(_p(kvc), kvc.shape[0], _p(bt), bt.shape[1], _p(sl), B, H, D, FMT[fmt], max_seq,
+                           _p(k), _p(v))
+    return k, v
+
+
+def paged_decode(q, kv: np.ndarray, block_table, seq_lens, sm_scale: float, fmt: str = "int4") -> np.ndarray:
+    """Paged decode attention in double: gather-dequant then softmax(q.k) v per sequence."""
+    qf = _f32(q)
+    B, Hq, D = qf.shape
+    H = kv.shape[3]
+    sl = np.asarray(seq_lens, dtype=np.int32)
+    ms = max(int(sl.max()) if sl.size else 0, 1)
+    k, v = paged_gather(kv, block_table, sl, H, D, fmt, ms)
+    return decode_attention(qf, k, v, sm_scale, seq_lens=sl)

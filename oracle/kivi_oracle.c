@@ -460,3 +460,165 @@ int orc_num_threads(void) {
     return 1;
 #endif
 }
+
+/* ------------------------------------------------------------------------- */
+/* Paged cache (the vLLM-fork layout named by WRITEUP.md:82-95,117-124 and     */
+/* used at scripts/validate_paged_decode.py:32-64,                             */
+/* scripts/validate_store_equiv.py:34-65): kv[nb, 2, 16, H, FD] u8,            */
+/* FD = D/2 + D/16, row = codes then e4m3 scale bytes; V and the K rows of a   */
+/* partial block per token; K of a full block per channel, channel c's scale  */
+/* at row c / (D/16), byte c % (D/16).                                         */
+/* ------------------------------------------------------------------------- */
+static float sum16(const float e[BLK]) {
+    float v[8];
+    for (int j = 0; j < 8; ++j) v[j] = e[j] + e[j + 8];
+    float s = v[0];
+    for (int j = 1; j < 8; ++j) s = s + v[j];
+    return s;
+}
+
+/* scripts/diag_kernel_perchannel.py:30-48 `fp8` + `mse_scale`: absmax (clamp
+ * 1e-9), 16-point alpha grid 0.5 + i*(0.5/15) with e4m3-rounded scales inside
+ * the search, squared error summed, strict '<' from e4m3(amax/qmax).  The code
+ * of a value is rint(x/s) clamped to +-7 (INT4) or the e2m1 grid (NVFP4); a
+ * zero scale (e4m3 underflow) gives code 0.  Returns the e4m3 byte. */
+uint8_t orc_paged_calib(const float *x, int fmt, int calib) {
+    float qmax = qmax_of(fmt);
+    float amax = absmax16(x);
+    uint8_t best = orc_f32_to_e4m3(amax / qmax);
+    if (calib == CAL_ABSMAX) return best;
+    float best_err = 1e38f;
+    for (int i = 0; i < 16; ++i) {
+        float a = (float)(0.5 + i * (0.5 / 15.0));
+        uint8_t sc = orc_f32_to_e4m3((a * amax) / qmax);
+        float s = orc_e4m3_to_f32(sc);
+        float e[BLK];
+        for (int k = 0; k < BLK; ++k) {
+            float q = (s == 0.0f) ? 0.0f : q_grid(x[k] / s, fmt);
+            float d = x[k] - q * s;
+            e[k] = d * d;
+        }
+        float err = sum16(e);
+        if (err < best_err) { best_err = err; best = sc; }
+    }
+    return best;
+}
+
+static uint32_t paged_nibble(float x, float s, int fmt) {
+    if (s == 0.0f) return 0;
+    float y = x / s;
+    if (fmt == FMT_NVFP4) {
+        int neg, idx = e2m1_index(y, &neg);
+        return (uint32_t)idx | (neg ? 8u : 0u);
+    }
+    return (uint32_t)(int)q_grid(y, fmt) & 0xFu;
+}
+
+static float paged_code_value(uint32_t nib, int fmt) {
+    if (fmt == FMT_NVFP4) {
+        float l = E2M1_LEVELS[nib & 7];
+        return (nib & 8) ? -l : l;
+    }
+    return (float)(nib >= 8 ? (int)nib - 16 : (int)nib);
+}
+
+static uint8_t *paged_row(uint8_t *kv, int H, int D, long slot, int sel, int h) {
+    long FD = D / 2 + D / 16, RB = (long)H * FD;
+    return kv + ((slot / 16) * 2 + sel) * 16 * RB + (slot % 16) * RB + (long)h * FD;
+}
+
+/* Store N tokens k, v fp32 [N, H, D] at slot_mapping[N] (negative = skip).
+ * A block whose last slot is written by this call, with its earlier slots at
+ * the consecutive indices before it (or already in the cache), is quantised
+ * per channel over its 16 tokens; rows of that block not in this call are
+ * first dequantised from the cache.  Every other token's K row goes per
+ * token.  Returns 0, or 1 if a slot is out of range (that token skipped). */
+int orc_paged_store(const float *k, const float *v, int N, int H, int D, int fmt, int calib,
+                    const int64_t *slots, uint8_t *kv, long nb) {
+    int ND = D / 16, bad = 0;
+    for (int i = 0; i < N; ++i) {
+        long s = (long)slots[i];
+        if (s < 0) continue;
+        if (s >= nb * 16) { bad = 1; continue; }
+        int o = (int)(s % 16), e = i + 15 - o;
+        int deferred = e < N && slots[e] == s - o + 15;
+        for (int h = 0; h < H; ++h)
+            for (int sel = 0; sel < 2; ++sel) {
+                if (sel == 0 && deferred) continue;
+                const float *src = (sel ? v : k) + ((size_t)i * H + h) * D;
+                uint8_t *row = paged_row(kv, H, D, s, sel, h);
+                for (int db = 0; db < ND; ++db) {
+                    uint8_t sc = orc_paged_calib(src + db * 16, fmt, calib);
+                    float sv = orc_e4m3_to_f32(sc);
+                    for (int j = 0; j < 8; ++j)
+                        row[8 * db + j] = (uint8_t)(paged_nibble(src[db * 16 + 2 * j], sv, fmt) |
+                                                    (paged_nibble(src[db * 16 + 2 * j + 1], sv, fmt) << 4));
+                    row[D / 2 + db] = sc;
+                }
+            }
+    }
+    for (int i = 0; i < N; ++i) {
+        long s = (long)slots[i];
+        if (s < 0 || s >= nb * 16 || s % 16 != 15) continue;
+        long s0 = s - 15;
+        for (int h = 0; h < H; ++h) {
+            float *x = (float *)malloc(sizeof(float) * 16 * D);   /* [token][channel] */
+            for (int j = 0; j < 16; ++j) {
+                int idx = i - 15 + j;
+                if (idx >= 0 && slots[idx] == s0 + j) {
+                    memcpy(x + (size_t)j * D, k + ((size_t)idx * H + h) * D, sizeof(float) * D);
+                } else {
+                    uint8_t *row = paged_row(kv, H, D, s0 + j, 0, h);
+                    for (int c = 0; c < D; ++c) {
+                        float sc = orc_e4m3_to_f32(row[D / 2 + c / 16]);
+                        x[(size_t)j * D + c] = paged_code_value((row[c / 2] >> (4 * (c & 1))) & 0xF, fmt) * sc;
+                    }
+                }
+            }
+            for (int c = 0; c < D; ++c) {
+                float col[BLK];
+                for (int j = 0; j < 16; ++j) col[j] = x[(size_t)j * D + c];
+                uint8_t sc = orc_paged_calib(col, fmt, calib);
+                float sv = orc_e4m3_to_f32(sc);
+                for (int j = 0; j < 16; ++j) {
+                    uint8_t *row = paged_row(kv, H, D, s0 + j, 0, h);
+                    uint32_t nib = paged_nibble(col[j], sv, fmt);
+                    row[c / 2] = (uint8_t)((c & 1) ? ((row[c / 2] & 0x0F) | (nib << 4))
+                                                   : ((row[c / 2] & 0xF0) | nib));
+                }
+                paged_row(kv, H, D, s0 + c / ND, 0, h)[D / 2 + c % ND] = sc;
+            }
+            free(x);
+        }
+    }
+    return bad;
+}
+
+/* Gather-dequant to fp32 k, v [B, H, max_seq, D]; block b of a sequence of
+ * length L is per channel iff (b+1)*16 <= L; tokens >= L are 0. */
+void orc_paged_gather(const uint8_t *kv, long nb, const int *bt, long bt_stride, const int *seq_lens,
+                      int B, int H, int D, int fmt, int max_seq, float *k_out, float *v_out) {
+    int ND = D / 16;
+    (void)nb;
+    for (int b = 0; b < B; ++b) {
+        long L = seq_lens[b] < 0 ? 0 : seq_lens[b];
+        if (L > bt_stride * 16) L = bt_stride * 16;
+        for (int h = 0; h < H; ++h)
+            for (int t = 0; t < max_seq; ++t) {
+                float *ko = k_out + (((size_t)b * H + h) * max_seq + t) * D;
+                float *vo = v_out + (((size_t)b * H + h) * max_seq + t) * D;
+                if (t >= L) { memset(ko, 0, sizeof(float) * D); memset(vo, 0, sizeof(float) * D); continue; }
+                long pg = t / 16, phys = bt[(size_t)b * bt_stride + pg];
+                int full = (pg + 1) * 16 <= L;
+                const uint8_t *kr = paged_row((uint8_t *)kv, H, D, phys * 16 + t % 16, 0, h);
+                const uint8_t *vr = paged_row((uint8_t *)kv, H, D, phys * 16 + t % 16, 1, h);
+                for (int c = 0; c < D; ++c) {
+                    float ks = orc_e4m3_to_f32(kr[D / 2 + c / 16]);
+                    if (full) ks = orc_e4m3_to_f32(paged_row((uint8_t *)kv, H, D, phys * 16 + c / ND, 0, h)[D / 2 + c % ND]);
+                    ko[c] = paged_code_value((kr[c / 2] >> (4 * (c & 1))) & 0xF, fmt) * ks;
+                    vo[c] = paged_code_value((vr[c / 2] >> (4 * (c & 1))) & 0xF, fmt) *
+                            orc_e4m3_to_f32(vr[D / 2 + c / 16]);
+                }
+            }
+    }
+}

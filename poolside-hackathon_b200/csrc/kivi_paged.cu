@@ -1,0 +1,1018 @@
+// kivi_paged.cu -- the vLLM-style paged 4-bit KV cache: store, gather-dequant
+// and fused paged flash-decode.
+//
+// Replaces the fork kernels named by the reference (vllm/v1/attention/ops/
+// triton_{int4,nvfp4}_kivi.py: int4_kivi_store, int4_kivi_gather_dequant,
+// int4_kivi_paged_decode and the nvfp4_* twins; called at
+// scripts/validate_paged_decode.py:59,72,91, scripts/validate_store_equiv.py:
+// 50-51, scripts/validate_nvfp4_kivi.py:67-75,136-150).  The fork source is not
+// part of the reference checkout; the layout below is the one its write-up
+// states (WRITEUP.md:82-95,117-124) and its call sites imply.
+//
+// Cache: one uint8 tensor kv[num_blocks, 2, 16, H, FD], FD = D/2 + D/16;
+// dim 1 selects K (0) or V (1); a row (block, kv, slot, head) holds D/2 code
+// bytes (element 2j in the low nibble of byte j) then D/16 e4m3 scale bytes.
+//   V, and K of a partial block: per token, scale byte j = 16 channels 16j..
+//   K of a full block (16 tokens, (b+1)*16 <= seq_len): per channel over the
+//     16 tokens; the 16 rows' scale bytes are read as D per-channel scales,
+//     channel c at row c / (D/16), byte c % (D/16).
+// INT4 codes are two's-complement in [-7, 7]; NVFP4 codes are e2m1 with the
+// sign in bit 3; both scale with an e4m3 byte (value = code * fp32(scale)).
+//
+// Calibration (scripts/diag_kernel_perchannel.py:30-48): absmax over the 16
+// values, then a 16-point clip grid alpha_i = 0.5 + i * (0.5 / 15) with the
+// scale rounded to e4m3 inside the search, squared error summed over the
+// block, strict '<' argmin starting from e4m3(amax / qmax).
+#include "kivi_common.cuh"
+#include "kivi_internal.h"
+#include <algorithm>
+#include <type_traits>
+
+namespace kivi {
+namespace paged {
+
+constexpr int PG = 16;                 // tokens per block (page)
+
+__host__ __device__ __forceinline__ int full_dim(int D) { return D / 2 + D / 16; }
+
+__device__ __forceinline__ void set_err_flag(int* err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+struct Geo {
+    int H, D, FD;
+    int64_t RB;    // bytes per (block, kv, slot) row: H * FD
+    int64_t PGB;   // bytes per (block, kv): 16 * RB
+};
+__host__ __device__ __forceinline__ Geo make_geo(int H, int D) {
+    Geo g;
+    g.H = H; g.D = D; g.FD = full_dim(D);
+    g.RB = (int64_t)H * g.FD;
+    g.PGB = PG * g.RB;
+    return g;
+}
+__device__ __forceinline__ uint8_t* row_at(uint8_t* kv, const Geo& g, int64_t slot, int sel, int h) {
+    return kv + ((slot / PG) * 2 + sel) * g.PGB + (slot % PG) * g.RB + (int64_t)h * g.FD;
+}
+__device__ __forceinline__ const uint8_t* row_at(const uint8_t* kv, const Geo& g, int64_t slot, int sel, int h) {
+    return kv + ((slot / PG) * 2 + sel) * g.PGB + (slot % PG) * g.RB + (int64_t)h * g.FD;
+}
+
+// Sum of 16 values in torch's CPU order for a contiguous row (pairs j, j+8,
+// then left to right).
+__device__ __forceinline__ float sum16(const float e[BLK]) {
+    float s = __fadd_rn(e[0], e[8]);
+#pragma unroll
+    for (int j = 1; j < 8; ++j) s = __fadd_rn(s, __fadd_rn(e[j], e[j + 8]));
+    return s;
+}
+
+__device__ __forceinline__ float grid_code(float y, int fmt) {
+    return q_grid(y, fmt);               // INT4: rint + clamp(+-7); NVFP4: e2m1 level
+}
+
+// Squared reconstruction error of a block under the e4m3-rounded scale s.
+__device__ __forceinline__ float sq_err(const float x[BLK], float s, int fmt) {
+    float e[BLK];
+#pragma unroll
+    for (int i = 0; i < BLK; ++i) {
+        const float q = (s == 0.0f) ? 0.0f : grid_code(__fdiv_rn(x[i], s), fmt);
+        const float d = __fsub_rn(x[i], __fmul_rn(q, s));
+        e[i] = __fmul_rn(d, d);
+    }
+    return sum16(e);
+}
+
+// Pick the e4m3 scale byte of one 16-value block.
+__device__ __forceinline__ uint8_t calib_e4m3(const float x[BLK], int fmt, int calib) {
+    const float qmax = qmax_of(fmt);
+    const float amax = absmax16(x);
+    uint8_t best = f32_to_e4m3(__fdiv_rn(amax, qmax));
+    if (calib == CAL_ABSMAX) return best;
+    float best_err = 1e38f;
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i) {
+        const float a = __double2float_rn(0.5 + i * (0.5 / 15.0));
+        const uint8_t sc = f32_to_e4m3(__fdiv_rn(__fmul_rn(a, amax), qmax));
+        const float err = sq_err(x, e4m3_to_f32(sc), fmt);
+        if (err < best_err) { best_err = err; best = sc; }
+    }
+    return best;
+}
+
+__device__ __forceinline__ uint32_t nibble_of(float x, float s, int fmt) {
+    if (s == 0.0f) return 0u;
+    const float y = __fdiv_rn(x, s);
+    if (fmt == FMT_NVFP4) return (uint32_t)e2m1_index(fabsf(y)) | (y < 0.0f ? 8u : 0u);
+    return (uint32_t)(int)grid_code(y, fmt) & 0xFu;
+}
+
+__device__ __forceinline__ float code_value(uint32_t nib, int fmt) {
+    if (fmt == FMT_NVFP4) {
+        const float l = e2m1_level(nib & 7);
+        return (nib & 8) ? -l : l;
+    }
+    return (float)sx4((int)nib);
+}
+
+template <typename T>
+__device__ __forceinline__ float ld_in(const void* p, int64_t i) {
+    return to_f32<T>(reinterpret_cast<const T*>(p)[i]);
+}
+__device__ __forceinline__ float ld_any(const void* p, int dt, int64_t i) {
+    if (dt == KIVI_DT_BF16) return ld_in<__nv_bfloat16>(p, i);
+    if (dt == KIVI_DT_F16) return ld_in<__half>(p, i);
+    return ld_in<float>(p, i);
+}
+
+struct StoreP {
+    const void* k; const void* v; int dt;
+    int64_t sk_t, sk_h, sk_d, sv_t, sv_h, sv_d;
+    int N; Geo g; int fmt, calib;
+    const int64_t* slots; uint8_t* kv; int64_t nb; int* err;
+};
+
+__device__ __forceinline__ bool slot_ok(const StoreP& p, int64_t s) {
+    return s >= 0 && s < p.nb * PG;
+}
+
+// A token's K goes per channel when its block is completed by this call: the
+// token at index i + (15 - slot % 16) exists and holds the block's last slot.
+__device__ __forceinline__ bool k_deferred(const StoreP& p, int i, int64_t s) {
+    const int o = (int)(s % PG);
+    const int e = i + (PG - 1 - o);
+    return e < p.N && p.slots[e] == s - o + (PG - 1);
+}
+
+// Per-token blocks: one thread per (token, head, 16-value block), blocks
+// 0..ND-1 are V, ND..2ND-1 are K (skipped when the token's block completes).
+__global__ void __launch_bounds__(128) store_token_kernel(const StoreP p) {
+    const int ND = p.g.D / BLK;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t total = (int64_t)p.N * p.g.H * 2 * ND;
+    if (tid >= total) return;
+    const int j = (int)(tid % (2 * ND));
+    const int h = (int)((tid / (2 * ND)) % p.g.H);
+    const int i = (int)(tid / (2 * ND * p.g.H));
+    const int64_t s = p.slots[i];
+    if (s < 0) return;                                   // padding token
+    if (!slot_ok(p, s)) { set_err_flag(p.err, KIVI_ERR_ARG); return; }
+    const bool isv = j < ND;
+    const int db = isv ? j : j - ND;
+    if (!isv && k_deferred(p, i, s)) return;
+    float x[BLK];
+    const void* src = isv ? p.v : p.k;
+    const int64_t st = isv ? p.sv_t : p.sk_t, sh = isv ? p.sv_h : p.sk_h, sd = isv ? p.sv_d : p.sk_d;
+    const int64_t base = (int64_t)i * st + (int64_t)h * sh + (int64_t)(db * BLK) * sd;
+#pragma unroll
+    for (int e = 0; e < BLK; ++e) x[e] = ld_any(src, p.dt, base + e * sd);
+    const uint8_t sc = calib_e4m3(x, p.fmt, p.calib);
+    const float sv = e4m3_to_f32(sc);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int e = 0; e < BLK; ++e) {
+        const uint32_t nib = nibble_of(x[e], sv, p.fmt);
+        if (e < 8) lo |= nib << (4 * e); else hi |= nib << (4 * (e - 8));
+    }
+    uint8_t* row = row_at(p.kv, p.g, s, isv ? 1 : 0, h);
+    if ((reinterpret_cast<uintptr_t>(row) & 7) == 0) {
+        *reinterpret_cast<uint2*>(row + 8 * db) = make_uint2(lo, hi);
+    } else {                                             // rows of D % 128 != 0 are not 8-aligned
+#pragma unroll
+        for (int e = 0; e < 4; ++e) { row[8 * db + e] = (uint8_t)(lo >> (8 * e)); row[8 * db + 4 + e] = (uint8_t)(hi >> (8 * e)); }
+    }
+    row[p.g.D / 2 + db] = sc;
+}
+
+// Per-channel K of blocks completed by this call.  One CTA of D/2 threads per
+// 16 input tokens and head; thread cp owns channels 2cp, 2cp+1.  Rows of the block that
+// are not in this call come from the cache (stored per token by an earlier
+// call) and are dequantised first.
+__global__ void __launch_bounds__(128) store_channel_kernel(const StoreP p) {
+    const int h = blockIdx.y;
+    const int i_lo = blockIdx.x * PG, i_hi = min(i_lo + PG, p.N);
+    const int D = p.g.D, ND = D / BLK, cp = threadIdx.x;
+    for (int i = i_lo; i < i_hi; ++i) {
+        const int64_t s = p.slots[i];                    // uniform over the CTA
+        if (!slot_ok(p, s) || s % PG != PG - 1) continue;
+        const int64_t s0 = s - (PG - 1);
+        {
+            float x[2][BLK];
+#pragma unroll 1
+            for (int j = 0; j < PG; ++j) {
+                const int idx = i - (PG - 1) + j;
+                if (idx >= 0 && p.slots[idx] == s0 + j) {
+                    const int64_t base = (int64_t)idx * p.sk_t + (int64_t)h * p.sk_h;
+                    x[0][j] = ld_any(p.k, p.dt, base + (int64_t)(2 * cp) * p.sk_d);
+                    x[1][j] = ld_any(p.k, p.dt, base + (int64_t)(2 * cp + 1) * p.sk_d);
+                } else {
+                    const uint8_t* row = row_at(p.kv, p.g, s0 + j, 0, h);
+                    const uint32_t b = row[cp];
+                    const float sc = e4m3_to_f32(row[D / 2 + (2 * cp) / BLK]);
+                    x[0][j] = __fmul_rn(code_value(b & 0xF, p.fmt), sc);
+                    x[1][j] = __fmul_rn(code_value(b >> 4, p.fmt), sc);
+                }
+            }
+            uint8_t sc[2];
+            float sv[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) { sc[u] = calib_e4m3(x[u], p.fmt, p.calib); sv[u] = e4m3_to_f32(sc[u]); }
+            // every thread has read its rows before any row of the block is rewritten
+            __syncthreads();
+#pragma unroll 1
+            for (int j = 0; j < PG; ++j) {
+                uint8_t* row = row_at(p.kv, p.g, s0 + j, 0, h);
+                row[cp] = (uint8_t)(nibble_of(x[0][j], sv[0], p.fmt) | (nibble_of(x[1][j], sv[1], p.fmt) << 4));
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int c = 2 * cp + u;
+                row_at(p.kv, p.g, s0 + c / ND, 0, h)[D / 2 + c % ND] = sc[u];
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// Gather-dequant: bf16 k/v [B, H, max_seq, D]; tokens at or past seq_len are 0.
+struct GatherP {
+    const uint8_t* kv; int64_t nb; Geo g; int fmt;
+    const int* bt; int64_t bt_stride; const int* seq_lens;
+    int B, max_seq;
+    __nv_bfloat16* k_out; __nv_bfloat16* v_out; int* err;
+};
+__global__ void __launch_bounds__(128) gather_kernel(const GatherP p) {
+    const int D = p.g.D, ND = D / BLK, H = p.g.H;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t total = (int64_t)p.B * H * p.max_seq * ND;
+    if (tid >= total) return;
+    const int db = (int)(tid % ND);
+    const int t = (int)((tid / ND) % p.max_seq);
+    const int h = (int)((tid / ((int64_t)ND * p.max_seq)) % H);
+    const int b = (int)(tid / ((int64_t)ND * p.max_seq * H));
+    const int64_t cap = p.bt_stride * PG;
+    const int L = (int)(p.seq_lens[b] < 0 ? 0 : (p.seq_lens[b] > cap ? cap : p.seq_lens[b]));
+    const int64_t o = (((int64_t)b * H + h) * p.max_seq + t) * D + db * BLK;
+    __align__(16) __nv_bfloat16 kk[BLK], vv[BLK];
+    if (t >= L) {
+#pragma unroll
+        for (int e = 0; e < BLK; ++e) kk[e] = vv[e] = __float2bfloat16_rn(0.0f);
+    } else {
+        const int pg = t / PG;
+        int64_t phys = p.bt[(int64_t)b * p.bt_stride + pg];
+        if (phys < 0 || phys >= p.nb) { set_err_flag(p.err, KIVI_ERR_ARG); phys = 0; }
+        const int64_t slot = phys * PG + t % PG;
+        const bool full = (pg + 1) * PG <= L;
+        const uint8_t* kr = row_at(p.kv, p.g, slot, 0, h);
+        const uint8_t* vr = row_at(p.kv, p.g, slot, 1, h);
+        const float vs = e4m3_to_f32(vr[D / 2 + db]);
+        const float ks_tok = e4m3_to_f32(kr[D / 2 + db]);
+#pragma unroll
+        for (int e = 0; e < BLK; ++e) {
+            const int c = db * BLK + e;
+            const uint32_t kb = kr[c / 2], vb = vr[c / 2];
+            float ks = ks_tok;
+            if (full) {
+                const uint8_t* sr = row_at(p.kv, p.g, phys * PG + c / ND, 0, h);
+                ks = e4m3_to_f32(sr[D / 2 + c % ND]);
+            }
+            kk[e] = __float2bfloat16_rn(__fmul_rn(code_value((kb >> (4 * (c & 1))) & 0xF, p.fmt), ks));
+            vv[e] = __float2bfloat16_rn(__fmul_rn(code_value((vb >> (4 * (c & 1))) & 0xF, p.fmt), vs));
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < BLK; ++e) { p.k_out[o + e] = kk[e]; p.v_out[o + e] = vv[e]; }
+}
+
+// ---------------------------------------------------------------------------
+// Fused paged decode.
+//
+// Work = flattened (sequence, TP-page tile) list split evenly over a
+// persistent grid.  A CTA has one consumer warp per KV head plus a producer
+// warp; the producer copies whole blocks (K and V of a block are one
+// contiguous 2 * 16 * H * FD byte range) with cp.async.bulk into a ring of
+// stages guarded by mbarriers, so every byte of the cache is read once and in
+// full rows.  Consumer warp h runs, per 16-token block:
+//   QK^T  m16n8k16 with the block's 16 tokens as M, the GQA heads as N; the
+//         A fragments come from 64-bit shared loads of the token rows, the
+//         channel order inside each k-step is permuted to match the nibble
+//         order the fp16 magic / e2m1 cvt produce (Q uses the same order);
+//   PV    with channels as M and tokens as K: two token rows are interleaved
+//         with a byte permute so one 32-bit word yields (token, token) pairs;
+//   code * e4m3 scale is exact in fp16 (3 + 4 significant bits), so the
+//   scales are applied to the A operand and every product is exact.
+// Softmax is online in base 2 with lazy rescaling; per-(CTA, sequence) partial
+// states are merged by paged_merge_kernel.
+// ---------------------------------------------------------------------------
+constexpr int DD = 128;               // head_dim of the fast path
+constexpr int FDD = 72;               // row bytes per head at D = 128
+#ifndef KIVI_PG_TP
+#define KIVI_PG_TP 2
+#endif
+#ifndef KIVI_PG_NST
+#define KIVI_PG_NST 6
+#endif
+constexpr int TP = KIVI_PG_TP;        // blocks per pipeline stage
+constexpr int PNST = KIVI_PG_NST;     // most pipeline stages (the launch picks what fits)
+constexpr int PBP = 16 * TP + 8;     // halves per head row of the P staging buffer
+constexpr int MAX_H = 16;             // KV heads (consumer warps) of the fast path
+
+struct DecP {
+    const __nv_bfloat16* q; int64_t q_sb, q_sh;
+    const uint8_t* kv; int64_t nb; Geo g;
+    const int* bt; int64_t bt_stride; const int* seq_lens;
+    int B, Hq, G;
+    float scale2;                     // sm_scale * log2(e)
+    int N;                            // CTAs of the main kernel
+    int nst;                          // pipeline stages of this launch (<= PNST)
+    float* part_m; float* part_l; float* part_acc;
+    int* tile_off;                    // [B + 1]
+    int* err;
+    __nv_bfloat16* out;
+};
+
+__device__ __forceinline__ int seq_len_of(const DecP& p, int b) {
+    const int64_t cap = p.bt_stride * PG;
+    const int L = p.seq_lens[b];
+    return L < 0 ? 0 : (L > cap ? (int)cap : L);
+}
+__host__ __device__ __forceinline__ int64_t pslice(int64_t c, int64_t W, int N) { return c * W / N; }
+
+// tile_off[b] = sum over earlier sequences of ceil(ceil(L / 16) / TP).
+__global__ void __launch_bounds__(1024) paged_tile_offsets_kernel(const DecP p) {
+    __shared__ int part[1024];
+    const int t = threadIdx.x;
+    const int chunk = (p.B + 1023) / 1024, a = t * chunk, e = min(a + chunk, p.B);
+    auto tiles = [&](int b) { const int np = (seq_len_of(p, b) + PG - 1) / PG; return (np + TP - 1) / TP; };
+    int sum = 0;
+    for (int b = a; b < e; ++b) sum += tiles(b);
+    part[t] = sum;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {
+        const int v = t >= o ? part[t - o] : 0;
+        __syncthreads();
+        part[t] += v;
+        __syncthreads();
+    }
+    int run = part[t] - sum;
+    for (int b = a; b < e; ++b) { p.tile_off[b] = run; run += tiles(b); }
+    if (t == 1023) p.tile_off[p.B] = part[1023];
+}
+
+struct PCursor {
+    int b, t, T;
+    __device__ __forceinline__ void init(const DecP& p, int64_t i) {
+        int lo = 0, hi = p.B - 1;                     // last b with tile_off[b] <= i
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (p.tile_off[mid] <= i) lo = mid; else hi = mid - 1;
+        }
+        b = lo;
+        while (p.tile_off[b + 1] <= i) ++b;           // skip empty sequences
+        t = (int)(i - p.tile_off[b]);
+        T = p.tile_off[b + 1] - p.tile_off[b];
+    }
+    __device__ __forceinline__ void next(const DecP& p) {
+        if (++t < T) return;
+        t = 0;
+        ++b;
+        while (b < p.B && p.tile_off[b + 1] == p.tile_off[b]) ++b;
+        T = b < p.B ? p.tile_off[b + 1] - p.tile_off[b] : 1;
+    }
+};
+
+struct __align__(8) PCtl {
+    uint64_t full[PNST];
+    uint64_t empty[PNST];
+    int abort;
+};
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+    return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
+}
+__device__ __forceinline__ uint32_t e4m3_pair(uint32_t lo_byte, uint32_t hi_byte) {
+    return e4m3x2_to_h2((uint16_t)(lo_byte | (hi_byte << 8)));
+}
+// Eight nibbles n0..n7 of a word -> fp16x2 (n0,n4), (n1,n5), (n2,n6), (n3,n7).
+template <int FMT>
+__device__ __forceinline__ void nib4(uint32_t w, uint32_t (&r)[4]) {
+    if (FMT == FMT_NVFP4) {
+        uint32_t h0, h1, h2, h3;
+        e2m1x8_to_h2x4(w, h0, h1, h2, h3);
+        r[0] = __byte_perm(h0, h2, 0x5410);
+        r[1] = __byte_perm(h0, h2, 0x7632);
+        r[2] = __byte_perm(h1, h3, 0x5410);
+        r[3] = __byte_perm(h1, h3, 0x7632);
+    } else {
+        const uint32_t w8 = w >> 8;
+        r[0] = h2_as_u32(int4_lo_to_h2(w));
+        r[1] = h2_as_u32(int4_hi_to_h2(w));
+        r[2] = h2_as_u32(int4_lo_to_h2(w8));
+        r[3] = h2_as_u32(int4_hi_to_h2(w8));
+    }
+}
+
+// NW = warps the launch may use (KV heads + 1); it sets the register budget.
+template <int FMT, int NW>
+__global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecP p) {
+    extern __shared__ __align__(128) uint8_t psm[];
+    const int H = p.g.H, G = p.G;
+    const int64_t RB = p.g.RB, PGB = p.g.PGB;
+    const int64_t SB = 2 * TP * PGB;                                  // stage bytes
+    uint8_t* stages = psm;
+    __half* pbuf = reinterpret_cast<__half*>(psm + p.nst * SB);        // [H][8][PBP]
+    PCtl* ctl = reinterpret_cast<PCtl*>(pbuf + H * 8 * PBP);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x;
+    const int64_t Wt = p.tile_off[p.B];
+    const int64_t i0 = pslice(c, Wt, p.N), i1 = pslice(c + 1, Wt, p.N);
+    if (i0 >= i1) return;                                             // idle CTA
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.nst; ++s) { mbar_init(&ctl->full[s], 1); mbar_init(&ctl->empty[s], H); }
+        ctl->abort = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == H) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            int it = 0;
+            PCursor cu;
+            cu.init(p, i0);
+            for (int64_t i = i0; i < i1; ++i, ++it, cu.next(p)) {
+                const int s = it % p.nst;
+                if (!mbar_wait_bounded(&ctl->empty[s], ((it / p.nst) & 1) ^ 1)) {
+                    set_err_flag(p.err, KIVI_ERR_TIMEOUT);
+                    ctl->abort = 1;
+                    break;
+                }
+                if (ctl->abort) break;
+                const int np = (seq_len_of(p, cu.b) + PG - 1) / PG;
+                const int pg0 = cu.t * TP, npg = min(TP, np - pg0);
+                uint8_t* st = stages + s * SB;
+                mbar_arrive_expect_tx(&ctl->full[s], (uint32_t)(npg * 2 * PGB));
+                for (int j = 0; j < npg; ++j) {
+                    int64_t phys = p.bt[(int64_t)cu.b * p.bt_stride + pg0 + j];
+                    if (phys < 0 || phys >= p.nb) { set_err_flag(p.err, KIVI_ERR_ARG); phys = 0; }
+                    bulk_g2s(st + j * 2 * PGB, p.kv + phys * 2 * PGB, (uint32_t)(2 * PGB), &ctl->full[s]);
+                }
+            }
+            for (int j = (it > p.nst ? it - p.nst : 0); j < it; ++j)
+                if (!mbar_wait_bounded(&ctl->full[j % p.nst], (j / p.nst) & 1)) set_err_flag(p.err, KIVI_ERR_TIMEOUT);
+        }
+        return;
+    }
+
+    // ------------------------------- consumers --------------------------------
+    const int h = warp, g = lane >> 2, tq = lane & 3;
+    __half* pb = pbuf + warp * 8 * PBP;
+    uint32_t qf[2][4][2];
+    float acc[8][4];
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    int cur = -1;
+
+    auto flush = [&](int b) {
+        float L0 = l0, L1 = l1;
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            L0 += __shfl_xor_sync(0xffffffffu, L0, o);
+            L1 += __shfl_xor_sync(0xffffffffu, L1, o);
+        }
+        const int64_t rec = ((int64_t)(c + b) * H + h) * G;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int n = 2 * tq + hh;
+            if (n >= G) continue;
+            if (g == 0) { p.part_m[rec + n] = hh ? m1 : m0; p.part_l[rec + n] = hh ? L1 : L0; }
+            float* a = p.part_acc + (rec + n) * DD + 16 * g;
+            *reinterpret_cast<float4*>(a) = make_float4(acc[0][hh], acc[1][hh], acc[2][hh], acc[3][hh]);
+            *reinterpret_cast<float4*>(a + 4) = make_float4(acc[4][hh], acc[5][hh], acc[6][hh], acc[7][hh]);
+            *reinterpret_cast<float4*>(a + 8) = make_float4(acc[0][2 + hh], acc[1][2 + hh], acc[2][2 + hh], acc[3][2 + hh]);
+            *reinterpret_cast<float4*>(a + 12) = make_float4(acc[4][2 + hh], acc[5][2 + hh], acc[6][2 + hh], acc[7][2 + hh]);
+        }
+    };
+
+    int it = 0;
+    PCursor cu;
+    cu.init(p, i0);
+    int Lb = 0;
+    for (int64_t i = i0; i < i1; ++i, ++it, cu.next(p)) {
+        const int b = cu.b;
+        if (b != cur) {
+            if (cur >= 0) flush(cur);
+            cur = b;
+            Lb = seq_len_of(p, b);
+            m0 = m1 = -INFINITY; l0 = l1 = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e][0] = acc[e][1] = acc[e][2] = acc[e][3] = 0.f;
+            // B fragments of Q in the permuted channel order of the K loads
+            const __nv_bfloat16* qp = p.q + (int64_t)b * p.q_sb + (int64_t)(h * G + g) * p.q_sh;
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int ch = 64 * cc + 16 * tq + 8 * (e >> 1) + 2 * (e & 1);
+                    uint32_t b0 = 0, b1 = 0;
+                    if (g < G) {
+                        b0 = h2_as_u32(__floats2half2_rn(__bfloat162float(qp[ch]), __bfloat162float(qp[ch + 4])));
+                        b1 = h2_as_u32(__floats2half2_rn(__bfloat162float(qp[ch + 1]), __bfloat162float(qp[ch + 5])));
+                    }
+                    qf[cc][e][0] = b0; qf[cc][e][1] = b1;
+                }
+        }
+        const int s = it % p.nst;
+        if (!mbar_wait_bounded(&ctl->full[s], (it / p.nst) & 1)) {
+            set_err_flag(p.err, KIVI_ERR_TIMEOUT);
+            ctl->abort = 1;
+        }
+        if (ctl->abort) break;
+        const uint8_t* st = stages + s * SB;
+        const int pg0 = cu.t * TP;
+        // All TP blocks of the stage are processed together (TP independent
+        // MMA chains per phase); only a stage holding a sequence's partial or
+        // missing last block takes the masked body.
+        auto stage_body = [&](auto masked_tag) {
+            constexpr bool MASKED = decltype(masked_tag)::value;
+            int lim[TP];
+#pragma unroll
+            for (int j = 0; j < TP; ++j) lim[j] = MASKED ? Lb - (pg0 + j) * PG : PG;
+            // ------------------------------ QK^T ------------------------------
+            float sc[TP][4];
+#pragma unroll
+            for (int j = 0; j < TP; ++j) {
+                sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+                const uint8_t* kpg = st + j * 2 * PGB + h * FDD;
+                const bool full = !MASKED || lim[j] >= PG;
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                    const uint2 ra = lds64(kpg + g * RB + 32 * cc + 8 * tq);
+                    const uint2 rb = lds64(kpg + (g + 8) * RB + 32 * cc + 8 * tq);
+                    uint32_t A0[4], A1[4], B0[4], B1[4];
+                    nib4<FMT>(ra.x, A0); nib4<FMT>(ra.y, A1); nib4<FMT>(rb.x, B0); nib4<FMT>(rb.y, B1);
+                    uint32_t S[8], T0 = 0, T1 = 0;
+                    if (full) {
+#pragma unroll
+                        for (int sw = 0; sw < 2; ++sw) {
+                            const uint2 sr = lds64(kpg + (8 * cc + 2 * tq + sw) * RB + DD / 2);
+                            const uint32_t x = __byte_perm(sr.x, sr.y, 0x5140), y = __byte_perm(sr.x, sr.y, 0x7362);
+                            S[4 * sw + 0] = e4m3x2_to_h2((uint16_t)x);
+                            S[4 * sw + 1] = e4m3x2_to_h2((uint16_t)(x >> 16));
+                            S[4 * sw + 2] = e4m3x2_to_h2((uint16_t)y);
+                            S[4 * sw + 3] = e4m3x2_to_h2((uint16_t)(y >> 16));
+                        }
+                    } else {
+                        const uint32_t s0 = kpg[g * RB + DD / 2 + 4 * cc + tq];
+                        const uint32_t s1 = kpg[(g + 8) * RB + DD / 2 + 4 * cc + tq];
+                        T0 = e4m3_pair(s0, s0);
+                        T1 = e4m3_pair(s1, s1);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int sw = e >> 1, k = 2 * (e & 1);
+                        uint32_t a0 = sw ? A1[k] : A0[k], a2 = sw ? A1[k + 1] : A0[k + 1];
+                        uint32_t a1 = sw ? B1[k] : B0[k], a3 = sw ? B1[k + 1] : B0[k + 1];
+                        if (full) {
+                            const uint32_t sa = S[4 * sw + k], sb = S[4 * sw + k + 1];
+                            a0 = hmul2u(a0, sa); a1 = hmul2u(a1, sa); a2 = hmul2u(a2, sb); a3 = hmul2u(a3, sb);
+                        } else {
+                            a0 = hmul2u(a0, T0); a2 = hmul2u(a2, T0); a1 = hmul2u(a1, T1); a3 = hmul2u(a3, T1);
+                        }
+                        mma_f16(sc[j], a0, a1, a2, a3, qf[cc][e][0], qf[cc][e][1]);
+                    }
+                }
+            }
+            // ----------------------------- softmax ----------------------------
+            // sc[j]: (token g, head 2tq), (g, 2tq+1), (g+8, 2tq), (g+8, 2tq+1)
+            float x[TP][4];
+            float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < TP; ++j) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) x[j][e] = sc[j][e] * p.scale2;
+                if (MASKED) {
+                    if (g >= lim[j]) x[j][0] = x[j][1] = -INFINITY;
+                    if (g + 8 >= lim[j]) x[j][2] = x[j][3] = -INFINITY;
+                }
+                mx0 = fmaxf(mx0, fmaxf(x[j][0], x[j][2]));
+                mx1 = fmaxf(mx1, fmaxf(x[j][1], x[j][3]));
+            }
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+            }
+            // the running reference max moves only when a score exceeds it by
+            // more than 2^8, so p <= 256 stays exact in fp16 staging
+            const bool need = (mx0 > m0 + 8.f) || (mx1 > m1 + 8.f);
+            if (__any_sync(0xffffffffu, need)) {
+                const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+                const float al0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - mn0);
+                const float al1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - mn1);
+                m0 = mn0; m1 = mn1;
+                l0 *= al0; l1 *= al1;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) { acc[e][0] *= al0; acc[e][2] *= al0; acc[e][1] *= al1; acc[e][3] *= al1; }
+            }
+            const float r0 = (m0 == -INFINITY) ? 0.f : m0, r1 = (m1 == -INFINITY) ? 0.f : m1;
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < TP; ++j) {
+                const float p0 = exp2f(x[j][0] - r0), p2 = exp2f(x[j][2] - r0);
+                const float p1 = exp2f(x[j][1] - r1), p3 = exp2f(x[j][3] - r1);
+                l0 += p0 + p2;
+                l1 += p1 + p3;
+                pb[(2 * tq) * PBP + 16 * j + g] = __float2half_rn(p0);
+                pb[(2 * tq + 1) * PBP + 16 * j + g] = __float2half_rn(p1);
+                pb[(2 * tq) * PBP + 16 * j + g + 8] = __float2half_rn(p2);
+                pb[(2 * tq + 1) * PBP + 16 * j + g + 8] = __float2half_rn(p3);
+            }
+            __syncwarp();
+            // ------------------------------- PV -------------------------------
+#pragma unroll
+            for (int j = 0; j < TP; ++j) {
+                const uint8_t* vpg = st + j * 2 * PGB + PGB + h * FDD;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pb + g * PBP + 16 * j + 2 * tq);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(pb + g * PBP + 16 * j + 2 * tq + 8);
+                const int tA = 2 * tq, tC = 2 * tq + 8;
+                const uint2 wa = lds64(vpg + tA * RB + 8 * g), wb = lds64(vpg + (tA + 1) * RB + 8 * g);
+                const uint2 wc = lds64(vpg + tC * RB + 8 * g), wd = lds64(vpg + (tC + 1) * RB + 8 * g);
+                uint32_t sA = vpg[tA * RB + DD / 2 + g], sB = vpg[(tA + 1) * RB + DD / 2 + g];
+                uint32_t sC = vpg[tC * RB + DD / 2 + g], sD = vpg[(tC + 1) * RB + DD / 2 + g];
+                if (MASKED) {                 // rows past the end may be unwritten (NaN scales)
+                    sA = tA < lim[j] ? sA : 0u; sB = tA + 1 < lim[j] ? sB : 0u;
+                    sC = tC < lim[j] ? sC : 0u; sD = tC + 1 < lim[j] ? sD : 0u;
+                }
+                const uint32_t sAB = e4m3_pair(sA, sB), sCD = e4m3_pair(sC, sD);
+                uint32_t X0[4], Y0[4], X1[4], Y1[4], U0[4], V0[4], U1[4], V1[4];
+                nib4<FMT>(__byte_perm(wa.x, wb.x, 0x5410), X0);   // ch 16g+0..3, tokens (tA, tA+1)
+                nib4<FMT>(__byte_perm(wa.x, wb.x, 0x7632), Y0);   // ch 16g+4..7
+                nib4<FMT>(__byte_perm(wa.y, wb.y, 0x5410), X1);   // ch 16g+8..11
+                nib4<FMT>(__byte_perm(wa.y, wb.y, 0x7632), Y1);   // ch 16g+12..15
+                nib4<FMT>(__byte_perm(wc.x, wd.x, 0x5410), U0);
+                nib4<FMT>(__byte_perm(wc.x, wd.x, 0x7632), V0);
+                nib4<FMT>(__byte_perm(wc.y, wd.y, 0x5410), U1);
+                nib4<FMT>(__byte_perm(wc.y, wd.y, 0x7632), V1);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const uint32_t a0 = hmul2u(e < 4 ? X0[e & 3] : Y0[e & 3], sAB);   // row g:   ch 16g+e
+                    const uint32_t a1 = hmul2u(e < 4 ? X1[e & 3] : Y1[e & 3], sAB);   // row g+8: ch 16g+8+e
+                    const uint32_t a2 = hmul2u(e < 4 ? U0[e & 3] : V0[e & 3], sCD);
+                    const uint32_t a3 = hmul2u(e < 4 ? U1[e & 3] : V1[e & 3], sCD);
+                    mma_f16(acc[e], a0, a1, a2, a3, b0, b1);
+                }
+            }
+        };
+        if ((pg0 + TP) * PG <= Lb) stage_body(std::false_type{});
+        else stage_body(std::true_type{});
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->empty[s]);
+    }
+    if (cur >= 0 && !ctl->abort) flush(cur);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Merge of the per-(CTA, sequence) partial states of one (sequence, kv head,
+// q head); one 128-thread block each.  Sequences of length 0 give zeros.
+__global__ void __launch_bounds__(128) paged_merge_kernel(const DecP p) {
+    extern __shared__ __align__(16) float msm[];
+    const int b = blockIdx.x / p.g.H, h = blockIdx.x % p.g.H, n = blockIdx.y;
+    const int G = p.G, D = DD;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int64_t Wt = p.tile_off[p.B];
+    const int64_t a0 = p.tile_off[b], a1 = p.tile_off[b + 1];
+    int c_lo = 0, c_hi = -1;
+    if (Wt > 0 && a1 > a0) {
+        int64_t cc = (a0 * p.N) / Wt;
+        while (cc + 1 < p.N && pslice(cc + 1, Wt, p.N) <= a0) ++cc;
+        while (cc > 0 && pslice(cc, Wt, p.N) > a0) --cc;
+        c_lo = (int)cc;
+        int64_t ch = cc;
+        while (ch + 1 < p.N && pslice(ch + 1, Wt, p.N) < a1) ++ch;
+        c_hi = (int)ch;
+    }
+    const int ns = c_hi - c_lo + 1;
+    float* w = msm;                       // [ns], padded to a multiple of 4
+    float* red = msm + ((ns + 3) & ~3);   // [8]
+    float* sacc = red + 8;                // [4][D], 16-byte aligned for float4
+    auto rec = [&](int k) -> int64_t { return ((int64_t)(c_lo + k + b) * p.g.H + h) * G + n; };
+    // CTAs with an empty slice (grids sized from bt_stride) wrote no record
+    auto live = [&](int k) -> bool { return pslice(c_lo + k, Wt, p.N) < pslice(c_lo + k + 1, Wt, p.N); };
+    for (int k = threadIdx.x; k < ns; k += blockDim.x) w[k] = live(k) ? p.part_m[rec(k)] : -INFINITY;
+    __syncthreads();
+    float M = -INFINITY;
+    for (int k = threadIdx.x; k < ns; k += blockDim.x) M = fmaxf(M, w[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if (lane == 0) red[warp] = M;
+    __syncthreads();
+    M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const float Mr = (M == -INFINITY) ? 0.f : M;
+    __syncthreads();
+    float Ls = 0.f;
+    for (int k = threadIdx.x; k < ns; k += blockDim.x) {
+        const float e = exp2f(w[k] - Mr);
+        Ls += e != 0.f ? p.part_l[rec(k)] * e : 0.f;
+        w[k] = e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, o);
+    if (lane == 0) red[4 + warp] = Ls;
+    __syncthreads();
+    Ls = (red[4] + red[5]) + (red[6] + red[7]);
+    float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = warp; k < ns; k += 4) {
+        const float wk = w[k];
+        if (wk == 0.f) continue;
+        const float4 v4 = *reinterpret_cast<const float4*>(p.part_acc + rec(k) * D + 4 * lane);
+        a4.x += v4.x * wk; a4.y += v4.y * wk; a4.z += v4.z * wk; a4.w += v4.w * wk;
+    }
+    *reinterpret_cast<float4*>(sacc + warp * D + 4 * lane) = a4;
+    __syncthreads();
+    const int d = threadIdx.x;
+    const float a = (sacc[d] + sacc[D + d]) + (sacc[2 * D + d] + sacc[3 * D + d]);
+    const int64_t row = (int64_t)b * p.Hq + h * G + n;
+    p.out[row * D + d] = __float2bfloat16_rn(ns > 0 && Ls > 0.f ? a / Ls : 0.f);
+}
+
+// Any head_dim (multiple of 16, <= 256), group <= 16: one CTA per (sequence,
+// kv head), four warps stride over the blocks, CUDA-core arithmetic, the four
+// warp states merged in shared memory.
+constexpr int GP_MAXG = 16, GP_MAXC = 8;
+template <int FMT>
+__global__ void __launch_bounds__(128) paged_decode_generic_kernel(const DecP p) {
+    __shared__ float sm_m[4][GP_MAXG], sm_l[4][GP_MAXG];
+    extern __shared__ float sm_acc[];                 // [4][G][D]
+    const int b = blockIdx.x / p.g.H, h = blockIdx.x % p.g.H;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = p.G, D = p.g.D, ND = D / BLK;
+    const int L = seq_len_of(p, b);
+    float q[GP_MAXG][GP_MAXC], acc[GP_MAXG][GP_MAXC], m[GP_MAXG], l[GP_MAXG];
+    for (int n = 0; n < G; ++n) {
+        m[n] = -INFINITY; l[n] = 0.f;
+        const __nv_bfloat16* qp = p.q + (int64_t)b * p.q_sb + (int64_t)(h * G + n) * p.q_sh;
+        for (int e = 0; e < GP_MAXC; ++e) {
+            const int d = lane + 32 * e;
+            q[n][e] = d < D ? __bfloat162float(qp[d]) : 0.f;
+            acc[n][e] = 0.f;
+        }
+    }
+    const float sc2 = p.scale2;
+    for (int t = warp; t < L; t += 4) {
+        const int pg = t / PG;
+        int64_t phys = p.bt[(int64_t)b * p.bt_stride + pg];
+        if (phys < 0 || phys >= p.nb) { set_err_flag(p.err, KIVI_ERR_ARG); phys = 0; }
+        const bool full = (pg + 1) * PG <= L;
+        const uint8_t* kr = row_at(p.kv, p.g, phys * PG + t % PG, 0, h);
+        const uint8_t* vr = row_at(p.kv, p.g, phys * PG + t % PG, 1, h);
+        float kv[GP_MAXC], vv[GP_MAXC];
+        for (int e = 0; e < GP_MAXC; ++e) {
+            const int d = lane + 32 * e;
+            kv[e] = vv[e] = 0.f;
+            if (d < D) {
+                float ks = e4m3_to_f32(kr[D / 2 + d / BLK]);
+                if (full) ks = e4m3_to_f32(row_at(p.kv, p.g, phys * PG + d / ND, 0, h)[D / 2 + d % ND]);
+                kv[e] = code_value((kr[d / 2] >> (4 * (d & 1))) & 0xF, FMT) * ks;
+                vv[e] = code_value((vr[d / 2] >> (4 * (d & 1))) & 0xF, FMT) * e4m3_to_f32(vr[D / 2 + d / BLK]);
+            }
+        }
+        for (int n = 0; n < G; ++n) {
+            float s = 0.f;
+            for (int e = 0; e < GP_MAXC; ++e) s += q[n][e] * kv[e];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            s *= sc2;
+            const float mn = fmaxf(m[n], s);
+            const float al = exp2f(m[n] - mn), pr = exp2f(s - mn);
+            m[n] = mn;
+            l[n] = l[n] * al + pr;
+            for (int e = 0; e < GP_MAXC; ++e) acc[n][e] = acc[n][e] * al + pr * vv[e];
+        }
+    }
+    for (int n = 0; n < G; ++n) {
+        if (lane == 0) { sm_m[warp][n] = m[n]; sm_l[warp][n] = l[n]; }
+        for (int e = 0; e < GP_MAXC; ++e) {
+            const int d = lane + 32 * e;
+            if (d < D) sm_acc[(warp * G + n) * D + d] = acc[n][e];
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+        const int n = idx / D, d = idx % D;
+        float M = -INFINITY;
+        for (int w2 = 0; w2 < 4; ++w2) M = fmaxf(M, sm_m[w2][n]);
+        const float Mr = (M == -INFINITY) ? 0.f : M;
+        float Ls = 0.f, a = 0.f;
+        for (int w2 = 0; w2 < 4; ++w2) {
+            const float e = exp2f(sm_m[w2][n] - Mr);
+            Ls += sm_l[w2][n] * e;
+            a += sm_acc[(w2 * G + n) * D + d] * e;
+        }
+        p.out[((int64_t)b * p.Hq + h * G + n) * D + d] = __float2bfloat16_rn(Ls > 0.f ? a / Ls : 0.f);
+    }
+}
+
+}  // namespace paged
+}  // namespace kivi
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+namespace {
+using namespace kivi;
+using namespace kivi::paged;
+
+constexpr int PAGED_MAX_OCC = 4;
+
+size_t paged_stage_bytes(int H) { return (size_t)2 * TP * PG * H * FDD; }
+size_t paged_fixed_bytes(int H) { return (size_t)H * 8 * PBP * sizeof(__half) + sizeof(PCtl) + 16; }
+// As many stages as fit one CTA's shared memory (227 KB on sm_100), at most PNST.
+int paged_stages(int H) {
+    const size_t cap = 232448, fixed = paged_fixed_bytes(H), sb = paged_stage_bytes(H);
+    const int n = (int)((cap - fixed) / sb);
+    return n < PNST ? n : PNST;
+}
+size_t paged_smem(int H) { return paged_stages(H) * paged_stage_bytes(H) + paged_fixed_bytes(H); }
+
+int cur_device_sms(int* dev_out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    static int sms[64] = {0};
+    if (dev < 0 || dev >= 64) return 0;
+    if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (dev_out) *dev_out = dev;
+    return sms[dev];
+}
+
+template <int FMT, int NW>
+int paged_occupancy(int dev, int H) {
+    static int occ[64][MAX_H + 1] = {{0}};
+    static bool attr[64] = {false};
+    if (!attr[dev]) {
+        if (cudaFuncSetAttribute(paged_decode_kernel<FMT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 232448) != cudaSuccess)
+            return 0;
+        attr[dev] = true;
+    }
+    if (!occ[dev][H]) {
+        int o = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, paged_decode_kernel<FMT, NW>, (H + 1) * 32,
+                                                          paged_smem(H)) != cudaSuccess)
+            return 0;
+        occ[dev][H] = o > 0 ? (o < PAGED_MAX_OCC ? o : PAGED_MAX_OCC) : 1;
+    }
+    return occ[dev][H];
+}
+
+struct PagedPlan { int64_t W; int N; int64_t records; int64_t off_m, off_l, off_acc, floats; };
+PagedPlan paged_plan(int B, int Hkv, int G, int64_t bt_stride, int D, int sms, int occ) {
+    PagedPlan pl;
+    pl.W = (int64_t)B * ((bt_stride + TP - 1) / TP);
+    const int64_t cap = (int64_t)sms * occ;
+    pl.N = (int)(pl.W < cap ? pl.W : cap);
+    if (pl.N < 1) pl.N = 1;
+    pl.records = ((int64_t)pl.N + B) * Hkv * G;
+    pl.off_m = ((int64_t)B + 1 + 3) / 4 * 4;           // tile table first (int32 in float slots)
+    pl.off_l = pl.off_m + pl.records;
+    pl.off_acc = (pl.off_l + pl.records + 3) / 4 * 4;
+    pl.floats = pl.off_acc + pl.records * D;
+    return pl;
+}
+
+bool dtype_ok(int dt) { return dt == KIVI_DT_BF16 || dt == KIVI_DT_F16 || dt == KIVI_DT_F32; }
+bool fmt_ok(int fmt) { return fmt == FMT_INT4 || fmt == FMT_NVFP4; }
+}  // namespace
+
+extern "C" int kivi_paged_full_dim(int D) { return D > 0 && D % 16 == 0 ? full_dim(D) : 0; }
+
+extern "C" int kivi_paged_store(const void* k, const void* v, int in_dtype, int64_t sk_t, int64_t sk_h,
+                                int64_t sk_d, int64_t sv_t, int64_t sv_h, int64_t sv_d, int N, int H, int D,
+                                int fmt, int calib, const int64_t* slot_mapping, uint8_t* kv_cache,
+                                int64_t num_blocks, int* err, kivi_stream_t stream) {
+    if (N < 0 || H <= 0 || D <= 0 || D % 16 || D > 256 || !fmt_ok(fmt) || !dtype_ok(in_dtype)) return KIVI_ERR_ARG;
+    if (calib != CAL_ABSMAX && calib != CAL_MSE) return KIVI_ERR_ARG;
+    if (N == 0) return KIVI_OK;
+    if (!k || !v || !slot_mapping || !kv_cache || num_blocks <= 0) return KIVI_ERR_ARG;
+    StoreP p{};
+    p.k = k; p.v = v; p.dt = in_dtype;
+    p.sk_t = sk_t; p.sk_h = sk_h; p.sk_d = sk_d; p.sv_t = sv_t; p.sv_h = sv_h; p.sv_d = sv_d;
+    p.N = N; p.g = make_geo(H, D); p.fmt = fmt; p.calib = calib;
+    p.slots = slot_mapping; p.kv = kv_cache; p.nb = num_blocks; p.err = err;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t total = (int64_t)N * H * 2 * (D / BLK);
+    store_token_kernel<<<(unsigned)((total + 127) / 128), 128, 0, st>>>(p);
+    int e = check_launch();
+    if (e) return e;
+    store_channel_kernel<<<dim3((unsigned)((N + PG - 1) / PG), (unsigned)H), D / 2, 0, st>>>(p);
+    return check_launch();
+}
+
+extern "C" int kivi_paged_gather_dequant(const uint8_t* kv_cache, int64_t num_blocks, const int* block_table,
+                                         int64_t bt_stride, const int* seq_lens, int B, int H, int D, int fmt,
+                                         int max_seq, void* k_out, void* v_out, int* err,
+                                         kivi_stream_t stream) {
+    if (B < 0 || H <= 0 || D <= 0 || D % 16 || !fmt_ok(fmt) || max_seq < 0 || bt_stride < 0) return KIVI_ERR_ARG;
+    if (B == 0 || max_seq == 0) return KIVI_OK;
+    if (!kv_cache || !block_table || !seq_lens || !k_out || !v_out || num_blocks <= 0) return KIVI_ERR_ARG;
+    GatherP p{};
+    p.kv = kv_cache; p.nb = num_blocks; p.g = make_geo(H, D); p.fmt = fmt;
+    p.bt = block_table; p.bt_stride = bt_stride; p.seq_lens = seq_lens; p.B = B; p.max_seq = max_seq;
+    p.k_out = reinterpret_cast<__nv_bfloat16*>(k_out); p.v_out = reinterpret_cast<__nv_bfloat16*>(v_out);
+    p.err = err;
+    const int64_t total = (int64_t)B * H * max_seq * (D / BLK);
+    gather_kernel<<<(unsigned)((total + 127) / 128), 128, 0, (cudaStream_t)stream>>>(p);
+    return check_launch();
+}
+
+extern "C" int64_t kivi_paged_decode_workspace_floats(int B, int Hq, int Hkv, int64_t bt_stride, int D) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || bt_stride < 0 || D <= 0) return 0;
+    int sms = cur_device_sms(nullptr);
+    if (!sms) sms = 148;
+    return paged_plan(B, Hkv, Hq / Hkv, bt_stride, D, sms, PAGED_MAX_OCC).floats;
+}
+
+extern "C" int kivi_paged_decode(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* kv_cache,
+                                 int64_t num_blocks, const int* block_table, int64_t bt_stride,
+                                 const int* seq_lens, int B, int Hq, int Hkv, int D, int fmt, float sm_scale,
+                                 void* out, float* work, int64_t work_floats, int* err, kivi_stream_t stream) {
+    if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || D <= 0 || D % 16 || D > 256 || !fmt_ok(fmt) || bt_stride < 0)
+        return KIVI_ERR_ARG;
+    if (B == 0) return KIVI_OK;
+    if (!q || !kv_cache || !block_table || !seq_lens || !out || num_blocks <= 0) return KIVI_ERR_ARG;
+    const int G = Hq / Hkv;
+    int dev = 0;
+    const int sms = cur_device_sms(&dev);
+    if (!sms) return record_cuda_error(cudaGetLastError());
+    DecP p{};
+    p.q = reinterpret_cast<const __nv_bfloat16*>(q); p.q_sb = q_sb; p.q_sh = q_sh;
+    p.kv = kv_cache; p.nb = num_blocks; p.g = make_geo(Hkv, D);
+    p.bt = block_table; p.bt_stride = bt_stride; p.seq_lens = seq_lens;
+    p.B = B; p.Hq = Hq; p.G = G;
+    p.scale2 = sm_scale * 1.4426950408889634f;
+    p.err = err; p.out = reinterpret_cast<__nv_bfloat16*>(out);
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool fast = D == DD && Hkv <= MAX_H && G <= 8 && (uintptr_t)kv_cache % 16 == 0 &&
+                      (uintptr_t)q % 4 == 0 && q_sh % 2 == 0 && q_sb % 2 == 0;
+    if (!fast) {
+        if (G > GP_MAXG || D > 32 * GP_MAXC) return KIVI_ERR_UNSUPPORTED;
+        const size_t smem = (size_t)4 * G * D * sizeof(float);
+        if (smem > 48 * 1024) {
+            cudaError_t ae = (fmt == FMT_NVFP4)
+                ? cudaFuncSetAttribute(paged_decode_generic_kernel<FMT_NVFP4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                : cudaFuncSetAttribute(paged_decode_generic_kernel<FMT_INT4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (ae != cudaSuccess) return record_cuda_error(ae);
+        }
+        if (fmt == FMT_NVFP4) paged_decode_generic_kernel<FMT_NVFP4><<<B * Hkv, 128, smem, st>>>(p);
+        else paged_decode_generic_kernel<FMT_INT4><<<B * Hkv, 128, smem, st>>>(p);
+        return check_launch();
+    }
+    const bool wide = Hkv > 8;
+    const int occ = fmt == FMT_NVFP4 ? (wide ? paged_occupancy<FMT_NVFP4, 17>(dev, Hkv) : paged_occupancy<FMT_NVFP4, 9>(dev, Hkv))
+                                     : (wide ? paged_occupancy<FMT_INT4, 17>(dev, Hkv) : paged_occupancy<FMT_INT4, 9>(dev, Hkv));
+    if (!occ) return record_cuda_error(cudaGetLastError());
+    const PagedPlan pl = paged_plan(B, Hkv, G, bt_stride, D, sms, occ);
+    if (!work || work_floats < pl.floats) return KIVI_ERR_ARG;
+    p.N = pl.N;
+    p.nst = paged_stages(Hkv);
+    p.tile_off = reinterpret_cast<int*>(work);
+    p.part_m = work + pl.off_m; p.part_l = work + pl.off_l; p.part_acc = work + pl.off_acc;
+    paged_tile_offsets_kernel<<<1, 1024, 0, st>>>(p);
+    int e = check_launch();
+    if (e) return e;
+    const size_t smem = paged_smem(Hkv);
+    const dim3 blk((Hkv + 1) * 32);
+    if (fmt == FMT_NVFP4 && wide) paged_decode_kernel<FMT_NVFP4, 17><<<pl.N, blk, smem, st>>>(p);
+    else if (fmt == FMT_NVFP4) paged_decode_kernel<FMT_NVFP4, 9><<<pl.N, blk, smem, st>>>(p);
+    else if (wide) paged_decode_kernel<FMT_INT4, 17><<<pl.N, blk, smem, st>>>(p);
+    else paged_decode_kernel<FMT_INT4, 9><<<pl.N, blk, smem, st>>>(p);
+    e = check_launch();
+    if (e) return e;
+    // a sequence's tiles touch at most N + 1 CTAs
+    const size_t msm = ((size_t)pl.N + 4 + 8 + 4 * DD) * sizeof(float);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(B * Hkv), (unsigned)G);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = msm;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (msm > 48 * 1024) {
+        cudaError_t ae = cudaFuncSetAttribute(paged_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msm);
+        if (ae != cudaSuccess) return record_cuda_error(ae);
+    }
+    cudaError_t le = cudaLaunchKernelEx(&cfg, paged_merge_kernel, p);
+    if (le != cudaSuccess) return record_cuda_error(le);
+    return check_launch();
+}

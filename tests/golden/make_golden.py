@@ -12,6 +12,9 @@ Everything here is computed by the reference's OWN Python code on CPU:
     `dequant_fp32_exact` helper                                  (scripts/validate_int4_kivi_decode.py:37-84)
   * torch's float16 / float8_e4m3fn casts, the scale storage the
     reference uses (int4_kivi/cache.py:54,59; scripts/diag_kernel_perchannel.py:30-31)
+  * the paged cache's e4m3 MSE calibration `fp8` / `mse_scale` / `rt`
+    (scripts/diag_kernel_perchannel.py:30-53), taken from the script's source
+    text (its module-level vLLM import and GPU code are not executed)
 
 The only code of ours is the nibble packer (element 2j -> low nibble of byte j,
 int4_kivi/triton_kernels.py:21-24) and the input generator.
@@ -157,6 +160,30 @@ def main():
         "linspace7": torch.linspace(0.5, 1.0, 7).numpy(),
     }
     np.savez_compressed(os.path.join(HERE, "casts.npz"), **casts)
+
+    # ---------------- 5. paged-cache e4m3 calibration -------------------------
+    import ast
+    src_path = os.path.join(args.reference, "scripts", "diag_kernel_perchannel.py")
+    tree = ast.parse(open(src_path).read())
+    defs = [n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name in ("fp8", "mse_scale", "rt")]
+    ns = {"torch": torch, "QMAX": qmax, "BLOCK": 16}
+    exec(compile(ast.Module(body=defs, type_ignores=[]), src_path, "exec"), ns)
+    g = torch.Generator().manual_seed(9)
+    tok = (torch.randn(3000, 16, generator=g) *
+           torch.exp(torch.empty(3000, 1).uniform_(-4.0, 4.0, generator=g))).bfloat16().float()
+    s_tok = ns["mse_scale"](tok, -1)                                  # per token: blocks of 16 channels
+    chan = (torch.randn(16, 4, 128, generator=g) *
+            torch.exp(torch.empty(1, 4, 128).uniform_(-2.0, 2.0, generator=g))).bfloat16().float()
+    s_ch = ns["mse_scale"](chan, 0)                                   # per channel over 16 tokens
+    paged = {
+        "tok": tok.numpy(),
+        "tok_scale": s_tok.to(torch.float8_e4m3fn).view(torch.uint8).numpy()[:, 0],
+        "tok_deq": ns["rt"](tok, s_tok).numpy(),
+        "chan": chan.numpy(),
+        "chan_scale": s_ch.to(torch.float8_e4m3fn).view(torch.uint8).numpy()[0],
+        "chan_deq": ns["rt"](chan, s_ch).numpy(),
+    }
+    np.savez_compressed(os.path.join(HERE, "paged_calib.npz"), **paged)
     print("golden fixtures written to", HERE)
 
 

@@ -65,3 +65,30 @@ def test_no_cpu_fallback():
         import kv_quant
         with pytest.raises(RuntimeError):
             kv_quant.roundtrip(k, "int4", "channel", "mse")
+
+
+def test_paged_argument_errors_without_device_work():
+    from int4_kivi import _native
+    L = _native.lib()
+    assert L.kivi_paged_full_dim(128) == 72 and L.kivi_paged_full_dim(15) == 0
+    # D not a multiple of 16
+    assert L.kivi_paged_store(None, None, 0, 0, 0, 0, 0, 0, 0, 4, 2, 24, 0, 1, None, None, 1, None, None) == 1
+    # bad format
+    assert L.kivi_paged_store(None, None, 0, 0, 0, 0, 0, 0, 0, 4, 2, 128, 7, 1, None, None, 1, None, None) == 1
+    # zero tokens is a no-op
+    assert L.kivi_paged_store(None, None, 0, 0, 0, 0, 0, 0, 0, 0, 2, 128, 0, 1, None, None, 1, None, None) == 0
+    # Hq not a multiple of Hkv
+    assert L.kivi_paged_decode(None, 0, 0, None, 1, None, 4, None, 1, 6, 4, 128, 0, 0.1,
+                               None, None, 0, None, None) == 1
+    assert L.kivi_paged_decode_workspace_floats(1, 6, 4, 4, 128) == 0
+    assert L.kivi_paged_decode_workspace_floats(2, 32, 8, 64, 128) > 0
+    assert L.kivi_paged_gather_dequant(None, 1, None, 4, None, 1, 2, 100, 0, 8, None, None, None, None) == 1
+
+
+def test_paged_python_api_surface():
+    from int4_kivi import paged
+    for name in ("int4_kivi_store", "int4_kivi_gather_dequant", "int4_kivi_paged_decode",
+                 "nvfp4_kivi_store", "nvfp4_kivi_gather_dequant", "nvfp4_kivi_paged_decode",
+                 "int4_kivi_kv_cache_full_dim"):
+        assert callable(getattr(paged, name))
+    assert paged.BLOCK == 16 and paged.QMAX == 7 and paged.int4_kivi_kv_cache_full_dim(128) == 72

@@ -116,3 +116,77 @@ def test_nvfp4_store_semantics():
             want = np.array([oracle.lib().orc_f32_to_e4m3(float(np.float32(a) / np.float32(6)))
                              for a in am.ravel()], np.uint8).reshape(am.shape)
             assert np.array_equal(want, c["v_scale"])
+
+
+# ---------------------------------------------------------------------------
+# Paged cache: the e4m3 calibration of scripts/diag_kernel_perchannel.py:30-53
+# ---------------------------------------------------------------------------
+def test_paged_calib_per_token_bit_exact():
+    g = load_golden("paged_calib.npz")
+    got = oracle.paged_calib(g["tok"], "int4", "mse")
+    assert np.array_equal(got, g["tok_scale"])
+    # dequantised values: rint(x / s) clamped to +-7, times s
+    s = np.array([oracle.lib().orc_e4m3_to_f32(int(b)) for b in got], np.float32)[:, None]
+    deq = np.clip(np.rint(g["tok"] / s), -7, 7) * s
+    assert np.array_equal(deq.astype(np.float32), g["tok_deq"])
+
+
+def test_paged_calib_per_channel_bit_exact():
+    g = load_golden("paged_calib.npz")
+    chan = g["chan"]                                            # [16 tokens, H, D]
+    got = oracle.paged_calib(np.ascontiguousarray(chan.transpose(1, 2, 0)), "int4", "mse")
+    assert np.array_equal(got, g["chan_scale"])
+
+
+def _paged_prefill(L, H=2, D=128, seed=0, fmt="int4"):
+    rng = np.random.default_rng(seed)
+    k = (rng.standard_normal((L, H, D)) * np.exp(rng.uniform(-1, 2, (1, H, D)))).astype(np.float32)
+    v = rng.standard_normal((L, H, D)).astype(np.float32)
+    nb = (L + 15) // 16
+    kv = np.zeros((nb + 2, 2, 16, H, oracle.paged_full_dim(D)), np.uint8)
+    phys = np.arange(1, nb + 1)
+    slots = np.array([phys[t // 16] * 16 + t % 16 for t in range(L)], np.int64)
+    assert oracle.paged_store(k, v, slots, kv, fmt) == 0
+    return k, v, kv, phys
+
+
+@pytest.mark.parametrize("L", (15, 16, 40, 64))
+def test_paged_oracle_store_geometry(L):
+    """Full blocks carry per-channel K scales, the partial tail per-token ones;
+    the gather reproduces the per-channel / per-token calibration exactly."""
+    H, D = 2, 128
+    k, v, kv, phys = _paged_prefill(L, H, D)
+    kd, vd = oracle.paged_gather(kv, phys[None].astype(np.int32), [L], H, D, "int4", L)
+    for h in range(H):
+        for b in range(L // 16):
+            blk = k[16 * b:16 * b + 16, h]                       # [16, D]
+            sc = oracle.paged_calib(np.ascontiguousarray(blk.T), "int4", "mse")
+            s = np.array([oracle.lib().orc_e4m3_to_f32(int(x)) for x in sc], np.float32)
+            want = np.clip(np.rint(blk / s[None]), -7, 7) * s[None]
+            assert np.array_equal(kd[0, h, 16 * b:16 * b + 16], want)
+        for t in range((L // 16) * 16, L):
+            blocks = k[t, h].reshape(-1, 16)
+            sc = oracle.paged_calib(blocks, "int4", "mse")
+            s = np.array([oracle.lib().orc_e4m3_to_f32(int(x)) for x in sc], np.float32)[:, None]
+            want = (np.clip(np.rint(blocks / s), -7, 7) * s).reshape(-1)
+            assert np.array_equal(kd[0, h, t], want)
+    assert np.abs(vd[0] - v.transpose(1, 0, 2)).max() < 0.6
+
+
+def test_paged_oracle_block_completion_across_calls():
+    """A block grown token by token becomes per channel when its 16th slot is
+    written; the earlier rows are requantised from their per-token values."""
+    H, D = 1, 64
+    rng = np.random.default_rng(3)
+    k = rng.standard_normal((16, H, D)).astype(np.float32)
+    v = rng.standard_normal((16, H, D)).astype(np.float32)
+    kv = np.zeros((2, 2, 16, H, oracle.paged_full_dim(D)), np.uint8)
+    for t in range(15):
+        oracle.paged_store(k[t:t + 1], v[t:t + 1], np.array([16 + t]), kv)
+    kd15, _ = oracle.paged_gather(kv, np.array([[1]], np.int32), [15], H, D, "int4", 15)
+    oracle.paged_store(k[15:], v[15:], np.array([31]), kv)
+    kd16, _ = oracle.paged_gather(kv, np.array([[1]], np.int32), [16], H, D, "int4", 16)
+    src = np.concatenate([kd15[0, 0], k[15, 0][None]], 0)       # [16, D]
+    sc = oracle.paged_calib(np.ascontiguousarray(src.T), "int4", "mse")
+    s = np.array([oracle.lib().orc_e4m3_to_f32(int(x)) for x in sc], np.float32)
+    assert np.array_equal(kd16[0, 0], np.clip(np.rint(src / s[None]), -7, 7) * s[None])
