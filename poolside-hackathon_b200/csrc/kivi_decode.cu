@@ -641,15 +641,14 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeParams 
 // mode 0 -> normalised bf16 out; mode 1 -> merged (m, l, acc) records.
 // ---------------------------------------------------------------------------
 __host__ __device__ inline void head_cta_range(int64_t a0, int64_t a1, int64_t W, int N, int& c_lo, int& c_hi) {
+    // CTA c owns tiles [floor(cW/N), floor((c+1)W/N)).  c_lo is the last CTA
+    // whose slice starts at or before a0 (floor(cW/N) <= a0 <=> cW < (a0+1)N),
+    // c_hi the last whose slice starts before a1 (cW < a1 N).
     c_lo = 0; c_hi = -1;
     if (W <= 0 || a1 <= a0) return;
-    int64_t cc = (a0 * N) / W;
-    while (cc + 1 < N && tile_start(cc + 1, W, N) <= a0) ++cc;
-    while (cc > 0 && tile_start(cc, W, N) > a0) --cc;
-    c_lo = (int)cc;
-    int64_t ch = cc;
-    while (ch + 1 < N && tile_start(ch + 1, W, N) < a1) ++ch;
-    c_hi = (int)ch;
+    const int64_t lo = ((a0 + 1) * N - 1) / W, hi = (a1 * N - 1) / W;
+    c_lo = (int)(lo < N - 1 ? lo : N - 1);
+    c_hi = (int)(hi < N - 1 ? hi : N - 1);
 }
 
 template <int FMT>
@@ -718,11 +717,20 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         // many slots (long single sequences): warps split the slots, each lane
         // owns 4 channels (float4 loads), then a shared-memory reduction
         float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int i = warp; i < ns; i += 4) {
-            const float wi = w[i];
-            if (wi == 0.f) continue;
-            const float4 v4 = *reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane);
-            a4.x += v4.x * wi; a4.y += v4.y * wi; a4.z += v4.z * wi; a4.w += v4.w * wi;
+        for (int i0 = warp; i0 < ns; i0 += 16) {        // four loads in flight per iteration
+            float4 v4[4];
+            float wi[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + 4 * u;
+                wi[u] = i < ns ? w[i] : 0.f;
+                v4[u] = wi[u] != 0.f ? *reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                a4.x += v4[u].x * wi[u]; a4.y += v4[u].y * wi[u]; a4.z += v4[u].z * wi[u]; a4.w += v4[u].w * wi[u];
+            }
         }
         float* sacc = red + 8;                           // [4][128]
         *reinterpret_cast<float4*>(sacc + warp * DH + 4 * lane) = a4;

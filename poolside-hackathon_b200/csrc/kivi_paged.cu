@@ -26,7 +26,9 @@
 #include "kivi_common.cuh"
 #include "kivi_internal.h"
 #include <algorithm>
+#include <cstring>
 #include <type_traits>
+#include <cuda.h>
 
 namespace kivi {
 namespace paged {
@@ -307,7 +309,7 @@ __global__ void __launch_bounds__(128) gather_kernel(const GatherP p) {
 constexpr int DD = 128;               // head_dim of the fast path
 constexpr int FDD = 72;               // row bytes per head at D = 128
 #ifndef KIVI_PG_TP
-#define KIVI_PG_TP 2
+#define KIVI_PG_TP 4
 #endif
 #ifndef KIVI_PG_NST
 #define KIVI_PG_NST 6
@@ -325,6 +327,8 @@ struct DecP {
     float scale2;                     // sm_scale * log2(e)
     int N;                            // CTAs of the main kernel
     int nst;                          // pipeline stages of this launch (<= PNST)
+    int rowp;                         // smem pitch of a token row (>= H * FD)
+    int use_tma;                      // 1: blocks arrive by TMA at the padded pitch
     float* part_m; float* part_l; float* part_acc;
     int* tile_off;                    // [B + 1]
     int* err;
@@ -393,6 +397,17 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+// 32-bit shared-window addresses keep the consumer's many smem pointers in one register each
+__device__ __forceinline__ uint2 lds64s(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds8s(uint32_t a) {
+    uint16_t v;
+    asm volatile("ld.shared.u8 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
 __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
     return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
 }
@@ -418,13 +433,16 @@ __device__ __forceinline__ void nib4(uint32_t w, uint32_t (&r)[4]) {
     }
 }
 
-// NW = warps the launch may use (KV heads + 1); it sets the register budget.
+// NW = warps the launch may use (KV heads + the producer warp); it sets the
+// register budget.
 template <int FMT, int NW>
-__global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecP p) {
-    extern __shared__ __align__(128) uint8_t psm[];
+__global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const __grid_constant__ CUtensorMap tm_kv,
+                                                                  const DecP p) {
+    extern __shared__ __align__(128) uint8_t psm_raw[];
+    uint8_t* psm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(psm_raw) + 127) & ~uintptr_t(127));
     const int H = p.g.H, G = p.G;
-    const int64_t RB = p.g.RB, PGB = p.g.PGB;
-    const int64_t SB = 2 * TP * PGB;                                  // stage bytes
+    const int64_t PGB = p.g.PGB, ROWP = p.rowp;
+    const int64_t SB = (int64_t)TP * 32 * ROWP;                       // stage bytes
     uint8_t* stages = psm;
     __half* pbuf = reinterpret_cast<__half*>(psm + p.nst * SB);        // [H][8][PBP]
     PCtl* ctl = reinterpret_cast<PCtl*>(pbuf + H * 8 * PBP);
@@ -444,7 +462,13 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecP p) 
 
     if (warp == H) {
         // ------------------------------ producer ------------------------------
+        // One TMA load per block: a (rowp/8 x 16 x 2) box of 8-byte elements
+        // whose rows are wider than the cache row, so each token row lands at
+        // the padded smem pitch (the extra columns are out of bounds and
+        // zero-filled, not read).  Without a tensor map (odd H) the block
+        // arrives by one bulk copy at the natural pitch.
         if (lane == 0) {
+            if (p.use_tma) prefetch_tmap(&tm_kv);
             int it = 0;
             PCursor cu;
             cu.init(p, i0);
@@ -459,11 +483,12 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecP p) 
                 const int np = (seq_len_of(p, cu.b) + PG - 1) / PG;
                 const int pg0 = cu.t * TP, npg = min(TP, np - pg0);
                 uint8_t* st = stages + s * SB;
-                mbar_arrive_expect_tx(&ctl->full[s], (uint32_t)(npg * 2 * PGB));
+                mbar_arrive_expect_tx(&ctl->full[s], (uint32_t)(npg * 32 * ROWP));
                 for (int j = 0; j < npg; ++j) {
                     int64_t phys = p.bt[(int64_t)cu.b * p.bt_stride + pg0 + j];
                     if (phys < 0 || phys >= p.nb) { set_err_flag(p.err, KIVI_ERR_ARG); phys = 0; }
-                    bulk_g2s(st + j * 2 * PGB, p.kv + phys * 2 * PGB, (uint32_t)(2 * PGB), &ctl->full[s]);
+                    if (p.use_tma) tma_load_3d(st + j * 32 * ROWP, &tm_kv, &ctl->full[s], 0, 0, (int)(phys * 2));
+                    else bulk_g2s(st + j * 32 * ROWP, p.kv + phys * 2 * PGB, (uint32_t)(2 * PGB), &ctl->full[s]);
                 }
             }
             for (int j = (it > p.nst ? it - p.nst : 0); j < it; ++j)
@@ -474,6 +499,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecP p) 
 
     // ------------------------------- consumers --------------------------------
     const int h = warp, g = lane >> 2, tq = lane & 3;
+    const uint32_t rowp = (uint32_t)p.rowp;
     __half* pb = pbuf + warp * 8 * PBP;
     uint32_t qf[2][4][2];
     float acc[8][4];
@@ -535,7 +561,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecP p) 
             ctl->abort = 1;
         }
         if (ctl->abort) break;
-        const uint8_t* st = stages + s * SB;
+        const uint32_t st_s = smem_u32(stages + s * SB);
         const int pg0 = cu.t * TP;
         // All TP blocks of the stage are processed together (TP independent
         // MMA chains per phase); only a stage holding a sequence's partial or
@@ -550,19 +576,19 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecP p) 
 #pragma unroll
             for (int j = 0; j < TP; ++j) {
                 sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
-                const uint8_t* kpg = st + j * 2 * PGB + h * FDD;
+                const uint32_t kpg = st_s + (uint32_t)(j * 32 * rowp + h * FDD);
                 const bool full = !MASKED || lim[j] >= PG;
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
-                    const uint2 ra = lds64(kpg + g * RB + 32 * cc + 8 * tq);
-                    const uint2 rb = lds64(kpg + (g + 8) * RB + 32 * cc + 8 * tq);
+                    const uint2 ra = lds64s(kpg + g * rowp + 32 * cc + 8 * tq);
+                    const uint2 rb = lds64s(kpg + (g + 8) * rowp + 32 * cc + 8 * tq);
                     uint32_t A0[4], A1[4], B0[4], B1[4];
                     nib4<FMT>(ra.x, A0); nib4<FMT>(ra.y, A1); nib4<FMT>(rb.x, B0); nib4<FMT>(rb.y, B1);
                     uint32_t S[8], T0 = 0, T1 = 0;
                     if (full) {
 #pragma unroll
                         for (int sw = 0; sw < 2; ++sw) {
-                            const uint2 sr = lds64(kpg + (8 * cc + 2 * tq + sw) * RB + DD / 2);
+                            const uint2 sr = lds64s(kpg + (8 * cc + 2 * tq + sw) * rowp + DD / 2);
                             const uint32_t x = __byte_perm(sr.x, sr.y, 0x5140), y = __byte_perm(sr.x, sr.y, 0x7362);
                             S[4 * sw + 0] = e4m3x2_to_h2((uint16_t)x);
                             S[4 * sw + 1] = e4m3x2_to_h2((uint16_t)(x >> 16));
@@ -570,8 +596,8 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecP p) 
                             S[4 * sw + 3] = e4m3x2_to_h2((uint16_t)(y >> 16));
                         }
                     } else {
-                        const uint32_t s0 = kpg[g * RB + DD / 2 + 4 * cc + tq];
-                        const uint32_t s1 = kpg[(g + 8) * RB + DD / 2 + 4 * cc + tq];
+                        const uint32_t s0 = lds8s(kpg + g * rowp + DD / 2 + 4 * cc + tq);
+                        const uint32_t s1 = lds8s(kpg + (g + 8) * rowp + DD / 2 + 4 * cc + tq);
                         T0 = e4m3_pair(s0, s0);
                         T1 = e4m3_pair(s1, s1);
                     }
@@ -623,6 +649,9 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecP p) 
                 for (int e = 0; e < 8; ++e) { acc[e][0] *= al0; acc[e][2] *= al0; acc[e][1] *= al1; acc[e][3] *= al1; }
             }
             const float r0 = (m0 == -INFINITY) ? 0.f : m0, r1 = (m1 == -INFINITY) ? 0.f : m1;
+            // PV k-slot of token t: 2 (t & 3) + ((t >> 2) & 1) + 8 (t >> 3), so the
+            // four rows one PV load touches (t = tq + 4i) sit in distinct banks
+            const int ks = 2 * (g & 3) + ((g >> 2) & 1);
             __syncwarp();
 #pragma unroll
             for (int j = 0; j < TP; ++j) {
@@ -630,34 +659,35 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const DecP p) 
                 const float p1 = exp2f(x[j][1] - r1), p3 = exp2f(x[j][3] - r1);
                 l0 += p0 + p2;
                 l1 += p1 + p3;
-                pb[(2 * tq) * PBP + 16 * j + g] = __float2half_rn(p0);
-                pb[(2 * tq + 1) * PBP + 16 * j + g] = __float2half_rn(p1);
-                pb[(2 * tq) * PBP + 16 * j + g + 8] = __float2half_rn(p2);
-                pb[(2 * tq + 1) * PBP + 16 * j + g + 8] = __float2half_rn(p3);
+                pb[(2 * tq) * PBP + 16 * j + ks] = __float2half_rn(p0);
+                pb[(2 * tq + 1) * PBP + 16 * j + ks] = __float2half_rn(p1);
+                pb[(2 * tq) * PBP + 16 * j + ks + 8] = __float2half_rn(p2);
+                pb[(2 * tq + 1) * PBP + 16 * j + ks + 8] = __float2half_rn(p3);
             }
             __syncwarp();
             // ------------------------------- PV -------------------------------
 #pragma unroll
             for (int j = 0; j < TP; ++j) {
-                const uint8_t* vpg = st + j * 2 * PGB + PGB + h * FDD;
+                const uint32_t vpg = st_s + (uint32_t)((j * 32 + 16) * rowp + h * FDD);
                 const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pb + g * PBP + 16 * j + 2 * tq);
                 const uint32_t b1 = *reinterpret_cast<const uint32_t*>(pb + g * PBP + 16 * j + 2 * tq + 8);
-                const int tA = 2 * tq, tC = 2 * tq + 8;
-                const uint2 wa = lds64(vpg + tA * RB + 8 * g), wb = lds64(vpg + (tA + 1) * RB + 8 * g);
-                const uint2 wc = lds64(vpg + tC * RB + 8 * g), wd = lds64(vpg + (tC + 1) * RB + 8 * g);
-                uint32_t sA = vpg[tA * RB + DD / 2 + g], sB = vpg[(tA + 1) * RB + DD / 2 + g];
-                uint32_t sC = vpg[tC * RB + DD / 2 + g], sD = vpg[(tC + 1) * RB + DD / 2 + g];
+                // k-slots (2tq, 2tq+1) = tokens (tq, tq+4); (2tq+8, 2tq+9) = (tq+8, tq+12)
+                const int tA = tq, tB = tq + 4, tC = tq + 8, tD = tq + 12;
+                const uint2 wa = lds64s(vpg + tA * rowp + 8 * g), wb = lds64s(vpg + tB * rowp + 8 * g);
+                const uint2 wc = lds64s(vpg + tC * rowp + 8 * g), wd = lds64s(vpg + tD * rowp + 8 * g);
+                uint32_t sA = lds8s(vpg + tA * rowp + DD / 2 + g), sB = lds8s(vpg + tB * rowp + DD / 2 + g);
+                uint32_t sC = lds8s(vpg + tC * rowp + DD / 2 + g), sD = lds8s(vpg + tD * rowp + DD / 2 + g);
                 if (MASKED) {                 // rows past the end may be unwritten (NaN scales)
-                    sA = tA < lim[j] ? sA : 0u; sB = tA + 1 < lim[j] ? sB : 0u;
-                    sC = tC < lim[j] ? sC : 0u; sD = tC + 1 < lim[j] ? sD : 0u;
+                    sA = tA < lim[j] ? sA : 0u; sB = tB < lim[j] ? sB : 0u;
+                    sC = tC < lim[j] ? sC : 0u; sD = tD < lim[j] ? sD : 0u;
                 }
                 const uint32_t sAB = e4m3_pair(sA, sB), sCD = e4m3_pair(sC, sD);
                 uint32_t X0[4], Y0[4], X1[4], Y1[4], U0[4], V0[4], U1[4], V1[4];
-                nib4<FMT>(__byte_perm(wa.x, wb.x, 0x5410), X0);   // ch 16g+0..3, tokens (tA, tA+1)
+                nib4<FMT>(__byte_perm(wa.x, wb.x, 0x5410), X0);   // ch 16g+0..3, tokens (tA, tB)
                 nib4<FMT>(__byte_perm(wa.x, wb.x, 0x7632), Y0);   // ch 16g+4..7
                 nib4<FMT>(__byte_perm(wa.y, wb.y, 0x5410), X1);   // ch 16g+8..11
                 nib4<FMT>(__byte_perm(wa.y, wb.y, 0x7632), Y1);   // ch 16g+12..15
-                nib4<FMT>(__byte_perm(wc.x, wd.x, 0x5410), U0);
+                nib4<FMT>(__byte_perm(wc.x, wd.x, 0x5410), U0);   // same channels, tokens (tC, tD)
                 nib4<FMT>(__byte_perm(wc.x, wd.x, 0x7632), V0);
                 nib4<FMT>(__byte_perm(wc.y, wd.y, 0x5410), U1);
                 nib4<FMT>(__byte_perm(wc.y, wd.y, 0x7632), V1);
@@ -690,15 +720,14 @@ __global__ void __launch_bounds__(128) paged_merge_kernel(const DecP p) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int64_t Wt = p.tile_off[p.B];
     const int64_t a0 = p.tile_off[b], a1 = p.tile_off[b + 1];
+    // CTA c owns tiles [floor(cW/N), floor((c+1)W/N)): the first CTA holding
+    // tile a0 is the last with cW < (a0+1)N, the last holding a1-1 the last
+    // with cW < a1 N
     int c_lo = 0, c_hi = -1;
     if (Wt > 0 && a1 > a0) {
-        int64_t cc = (a0 * p.N) / Wt;
-        while (cc + 1 < p.N && pslice(cc + 1, Wt, p.N) <= a0) ++cc;
-        while (cc > 0 && pslice(cc, Wt, p.N) > a0) --cc;
-        c_lo = (int)cc;
-        int64_t ch = cc;
-        while (ch + 1 < p.N && pslice(ch + 1, Wt, p.N) < a1) ++ch;
-        c_hi = (int)ch;
+        const int64_t lo = ((a0 + 1) * p.N - 1) / Wt, hi = (a1 * p.N - 1) / Wt;
+        c_lo = (int)(lo < p.N - 1 ? lo : p.N - 1);
+        c_hi = (int)(hi < p.N - 1 ? hi : p.N - 1);
     }
     const int ns = c_hi - c_lo + 1;
     float* w = msm;                       // [ns], padded to a multiple of 4
@@ -729,12 +758,22 @@ __global__ void __launch_bounds__(128) paged_merge_kernel(const DecP p) {
     if (lane == 0) red[4 + warp] = Ls;
     __syncthreads();
     Ls = (red[4] + red[5]) + (red[6] + red[7]);
+    // four independent record loads in flight per warp iteration
     float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = warp; k < ns; k += 4) {
-        const float wk = w[k];
-        if (wk == 0.f) continue;
-        const float4 v4 = *reinterpret_cast<const float4*>(p.part_acc + rec(k) * D + 4 * lane);
-        a4.x += v4.x * wk; a4.y += v4.y * wk; a4.z += v4.z * wk; a4.w += v4.w * wk;
+    for (int k0 = warp; k0 < ns; k0 += 16) {
+        float4 v4[4];
+        float wk[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int k = k0 + 4 * u;
+            wk[u] = k < ns ? w[k] : 0.f;
+            v4[u] = wk[u] != 0.f ? *reinterpret_cast<const float4*>(p.part_acc + rec(k) * D + 4 * lane)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            a4.x += v4[u].x * wk[u]; a4.y += v4[u].y * wk[u]; a4.z += v4[u].z * wk[u]; a4.w += v4[u].w * wk[u];
+        }
     }
     *reinterpret_cast<float4*>(sacc + warp * D + 4 * lane) = a4;
     __syncthreads();
@@ -833,8 +872,42 @@ using namespace kivi::paged;
 
 constexpr int PAGED_MAX_OCC = 4;
 
-size_t paged_stage_bytes(int H) { return (size_t)2 * TP * PG * H * FDD; }
-size_t paged_fixed_bytes(int H) { return (size_t)H * 8 * PBP * sizeof(__half) + sizeof(PCtl) + 16; }
+typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                             const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                             CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeFn paged_encode_fn() {
+    static EncodeFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeFn>(ptr);
+    }
+    return fn;
+}
+
+// smem pitch of a token row: H * FD rounded up so that consecutive rows start
+// 24 or 8 words apart mod 32 (rows g..g+3 then cover distinct banks).  The
+// padded pitch needs the TMA path (rows of whole 16-byte multiples, even H);
+// odd H keeps the natural pitch.
+#ifndef KIVI_PG_PAD
+#define KIVI_PG_PAD 1
+#endif
+bool paged_tma_ok(int H) { return KIVI_PG_PAD && (H * FDD) % 16 == 0; }
+int paged_rowp(int H) {
+    const int rb = H * FDD;
+    if (!paged_tma_ok(H)) return rb;
+    for (int pad = 0; pad < 128; pad += 16) {
+        const int w = ((rb + pad) / 4) % 32;
+        if (w == 8 || w == 24) return rb + pad;
+    }
+    return rb;
+}
+size_t paged_stage_bytes(int H) { return (size_t)TP * 32 * paged_rowp(H); }
+size_t paged_fixed_bytes(int H) { return (size_t)H * 8 * PBP * sizeof(__half) + sizeof(PCtl) + 16 + 128; }
 // As many stages as fit one CTA's shared memory (227 KB on sm_100), at most PNST.
 int paged_stages(int H) {
     const size_t cap = 232448, fixed = paged_fixed_bytes(H), sb = paged_stage_bytes(H);
@@ -983,6 +1056,23 @@ extern "C" int kivi_paged_decode(const void* q, int64_t q_sb, int64_t q_sh, cons
     if (!work || work_floats < pl.floats) return KIVI_ERR_ARG;
     p.N = pl.N;
     p.nst = paged_stages(Hkv);
+    p.rowp = paged_rowp(Hkv);
+    p.use_tma = paged_tma_ok(Hkv) && (uintptr_t)kv_cache % 16 == 0 && 2 * num_blocks < (1LL << 31);
+    CUtensorMap tm;
+    memset(&tm, 0, sizeof(tm));
+    if (p.use_tma) {
+        // [2 * num_blocks][16 rows][H * FD / 8] of 8-byte elements; box rows
+        // are rowp / 8 elements wide (the tail past H * FD is zero fill)
+        EncodeFn enc = paged_encode_fn();
+        cuuint64_t dims[3] = {(cuuint64_t)(Hkv * FDD / 8), (cuuint64_t)PG, (cuuint64_t)(2 * num_blocks)};
+        cuuint64_t strides[2] = {(cuuint64_t)(Hkv * FDD), (cuuint64_t)(PG * Hkv * FDD)};
+        cuuint32_t box[3] = {(cuuint32_t)(p.rowp / 8), (cuuint32_t)PG, 2u};
+        cuuint32_t es[3] = {1, 1, 1};
+        if (!enc || enc(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(kv_cache), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return KIVI_ERR_CUDA;
+    }
     p.tile_off = reinterpret_cast<int*>(work);
     p.part_m = work + pl.off_m; p.part_l = work + pl.off_l; p.part_acc = work + pl.off_acc;
     paged_tile_offsets_kernel<<<1, 1024, 0, st>>>(p);
@@ -990,10 +1080,10 @@ extern "C" int kivi_paged_decode(const void* q, int64_t q_sb, int64_t q_sh, cons
     if (e) return e;
     const size_t smem = paged_smem(Hkv);
     const dim3 blk((Hkv + 1) * 32);
-    if (fmt == FMT_NVFP4 && wide) paged_decode_kernel<FMT_NVFP4, 17><<<pl.N, blk, smem, st>>>(p);
-    else if (fmt == FMT_NVFP4) paged_decode_kernel<FMT_NVFP4, 9><<<pl.N, blk, smem, st>>>(p);
-    else if (wide) paged_decode_kernel<FMT_INT4, 17><<<pl.N, blk, smem, st>>>(p);
-    else paged_decode_kernel<FMT_INT4, 9><<<pl.N, blk, smem, st>>>(p);
+    if (fmt == FMT_NVFP4 && wide) paged_decode_kernel<FMT_NVFP4, 17><<<pl.N, blk, smem, st>>>(tm, p);
+    else if (fmt == FMT_NVFP4) paged_decode_kernel<FMT_NVFP4, 9><<<pl.N, blk, smem, st>>>(tm, p);
+    else if (wide) paged_decode_kernel<FMT_INT4, 17><<<pl.N, blk, smem, st>>>(tm, p);
+    else paged_decode_kernel<FMT_INT4, 9><<<pl.N, blk, smem, st>>>(tm, p);
     e = check_launch();
     if (e) return e;
     // a sequence's tiles touch at most N + 1 CTAs
