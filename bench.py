@@ -180,7 +180,8 @@ def time_graph(g, seconds: float = 1.5) -> float:
 def extra_configs(dev, peak: float) -> dict:
     """Secondary BASELINE configs on one GPU, each step captured in a CUDA graph:
     c1 (INT4, S=8192) and c2 (NVFP4 at 65536 tokens: a 16-token quant-store
-    into the cache followed by decode over the whole cache)."""
+    into the cache followed by decode over the whole cache), then the same
+    at 65536 tokens in the paged vLLM block layout (paged_configs)."""
     import torch
     from int4_kivi import store_nvfp4_kivi
     from int4_kivi.cache import store_into, full_views
@@ -222,6 +223,61 @@ def extra_configs(dev, peak: float) -> dict:
                                       "frac": round(by2 / ms2 / 1e6 / peak, 4),
                                       "decode_tok_s": round(B / ms2 * 1e3, 1),
                                       "bytes_per_step": by2}
+    del st2, c, g2, kp, ks, vp, vs
+    torch.cuda.empty_cache()
+    res.update(paged_configs(dev, peak))
+    return res
+
+
+def paged_configs(dev, peak: float) -> dict:
+    """The vLLM block layout (kv[num_blocks, 2, 16, Hkv, 72], e4m3 scales,
+    shuffled block table) at 65536 tokens: INT4 decode alone, and NVFP4 with
+    the config-2 step (16 new tokens per sequence stored into a fresh block,
+    then decode over the whole context).  144 packed bytes per token and head."""
+    import torch
+    from int4_kivi import paged
+    S = 65536
+    nbs = S // 16
+    res = {}
+    for fmt in ("int4", "nvfp4"):
+        k, v, q = make_inputs(S, seed=11, device=dev)
+        gp = torch.Generator(device="cpu").manual_seed(5)
+        bt = (torch.randperm(B * nbs, generator=gp) + 1).to(torch.int32).view(B, nbs).to(dev)
+        kv = torch.zeros(B * nbs + 1, 2, 16, HKV, paged.int4_kivi_kv_cache_full_dim(D), dtype=torch.uint8,
+                         device=dev)
+        store = paged.int4_kivi_store if fmt == "int4" else paged.nvfp4_kivi_store
+        ar = torch.arange(16, device=dev)
+        for b in range(B):
+            slots = (bt[b].long()[:, None] * 16 + ar[None]).reshape(-1)
+            store(k[b].permute(1, 0, 2), v[b].permute(1, 0, 2), kv, slots, D)
+        # the config-2 step's 16 new tokens per sequence go to each sequence's last block
+        k_new = k[:, :, S - 16:].permute(0, 2, 1, 3).reshape(B * 16, HKV, D).contiguous()
+        v_new = v[:, :, S - 16:].permute(0, 2, 1, 3).reshape(B * 16, HKV, D).contiguous()
+        new_slots = (bt[:, -1].long()[:, None] * 16 + ar[None]).reshape(-1)
+        del k, v
+        sl = torch.full((B,), S, dtype=torch.int32, device=dev)
+        out = torch.empty(B, HQ, D, dtype=torch.bfloat16, device=dev)
+        dec = paged.int4_kivi_paged_decode if fmt == "int4" else paged.nvfp4_kivi_paged_decode
+        by = B * HKV * S * 144
+        if fmt == "int4":
+            g = graph_step(lambda: dec(q, kv, bt, sl, out=out))
+            ms = time_graph(g)
+            res["int4_paged_S65536"] = {"ms_per_step": round(ms, 4), "GB/s": round(by / ms / 1e6, 1),
+                                        "frac": round(by / ms / 1e6 / peak, 4),
+                                        "decode_tok_s": round(B / ms * 1e3, 1), "bytes_per_step": by}
+        else:
+            def c2_step():
+                store(k_new, v_new, kv, new_slots, D)
+                dec(q, kv, bt, sl, out=out)
+            g = graph_step(c2_step)
+            ms = time_graph(g)
+            by2 = by + B * 16 * HKV * D * 2 * 2
+            res["nvfp4_paged_c2_S65536_store16"] = {"ms_per_step": round(ms, 4), "GB/s": round(by2 / ms / 1e6, 1),
+                                                    "frac": round(by2 / ms / 1e6 / peak, 4),
+                                                    "decode_tok_s": round(B / ms * 1e3, 1),
+                                                    "bytes_per_step": by2}
+        del g, kv
+        torch.cuda.empty_cache()
     return res
 
 

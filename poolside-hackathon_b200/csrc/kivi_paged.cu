@@ -146,91 +146,109 @@ __device__ __forceinline__ bool k_deferred(const StoreP& p, int i, int64_t s) {
     return e < p.N && p.slots[e] == s - o + (PG - 1);
 }
 
-// Per-token blocks: one thread per (token, head, 16-value block), blocks
-// 0..ND-1 are V, ND..2ND-1 are K (skipped when the token's block completes).
-__global__ void __launch_bounds__(128) store_token_kernel(const StoreP p) {
+// The 16-point clip search of one block on a half-warp: lane a (0..15)
+// evaluates alpha_a; the strict-'<' first-index argmin of the sequential
+// search is kept by reducing (err, index) pairs with ties to the lower index
+// (NaN errors never win).  x[16] is the block, identical in every lane.
+// Returns the e4m3 scale byte (same in all 16 lanes).
+__device__ __forceinline__ uint8_t calib_e4m3_hw(const float x[BLK], int fmt, int calib, int a) {
+    const float qmax = qmax_of(fmt);
+    const float amax = absmax16(x);
+    const uint8_t init = f32_to_e4m3(__fdiv_rn(amax, qmax));
+    if (calib == CAL_ABSMAX) return init;
+    const float al = __double2float_rn(0.5 + a * (0.5 / 15.0));
+    const uint8_t sc = f32_to_e4m3(__fdiv_rn(__fmul_rn(al, amax), qmax));
+    float err = sq_err(x, e4m3_to_f32(sc), fmt);
+    if (!(err < 1e38f)) err = INFINITY;                 // cannot beat the initial 1e38 (or is NaN)
+    int idx = a;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) {
+        const float e2 = __shfl_xor_sync(0xffffffffu, err, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (e2 < err || (e2 == err && i2 < idx)) { err = e2; idx = i2; }
+    }
+    const uint32_t best = __shfl_sync(0xffffffffu, (uint32_t)sc, (threadIdx.x & 16) | idx);
+    return err == INFINITY ? init : (uint8_t)best;
+}
+
+// Per-token blocks: one half-warp per (token, head, 16-value block); blocks
+// 0..ND-1 are V, ND..2ND-1 are K (skipped when the token's block completes in
+// this call).  Lane e also quantises element e; lanes 2j, 2j+1 form byte j.
+__global__ void __launch_bounds__(256) store_token_kernel(const StoreP p) {
     const int ND = p.g.D / BLK;
-    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int lane = threadIdx.x & 31, a = lane & 15;
+    const int64_t task = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;   // half-warp index
     const int64_t total = (int64_t)p.N * p.g.H * 2 * ND;
-    if (tid >= total) return;
-    const int j = (int)(tid % (2 * ND));
-    const int h = (int)((tid / (2 * ND)) % p.g.H);
-    const int i = (int)(tid / (2 * ND * p.g.H));
+    const bool in = task < total;
+    const int64_t tk = in ? task : total - 1;          // out-of-range half-warps shadow a valid task
+    const int j = (int)(tk % (2 * ND));
+    const int h = (int)((tk / (2 * ND)) % p.g.H);
+    const int i = (int)(tk / (2 * ND * p.g.H));
     const int64_t s = p.slots[i];
-    if (s < 0) return;                                   // padding token
-    if (!slot_ok(p, s)) { set_err_flag(p.err, KIVI_ERR_ARG); return; }
     const bool isv = j < ND;
     const int db = isv ? j : j - ND;
-    if (!isv && k_deferred(p, i, s)) return;
+    bool live = in && s >= 0;
+    if (live && !slot_ok(p, s)) { if (a == 0) set_err_flag(p.err, KIVI_ERR_ARG); live = false; }
+    if (live && !isv && k_deferred(p, i, s)) live = false;
+    // both half-warps of a warp reach the shuffles; a dead one computes on a valid block
     float x[BLK];
     const void* src = isv ? p.v : p.k;
     const int64_t st = isv ? p.sv_t : p.sk_t, sh = isv ? p.sv_h : p.sk_h, sd = isv ? p.sv_d : p.sk_d;
     const int64_t base = (int64_t)i * st + (int64_t)h * sh + (int64_t)(db * BLK) * sd;
 #pragma unroll
     for (int e = 0; e < BLK; ++e) x[e] = ld_any(src, p.dt, base + e * sd);
-    const uint8_t sc = calib_e4m3(x, p.fmt, p.calib);
-    const float sv = e4m3_to_f32(sc);
-    uint32_t lo = 0, hi = 0;
-#pragma unroll
-    for (int e = 0; e < BLK; ++e) {
-        const uint32_t nib = nibble_of(x[e], sv, p.fmt);
-        if (e < 8) lo |= nib << (4 * e); else hi |= nib << (4 * (e - 8));
+    const uint8_t sc = calib_e4m3_hw(x, p.fmt, p.calib, a);
+    const float xa = ld_any(src, p.dt, base + a * sd);   // element a (a register index would spill)
+    const uint32_t nib = nibble_of(xa, e4m3_to_f32(sc), p.fmt);
+    const uint32_t other = __shfl_xor_sync(0xffffffffu, nib, 1);
+    if (live && s >= 0) {
+        uint8_t* row = row_at(p.kv, p.g, s, isv ? 1 : 0, h);
+        if ((a & 1) == 0) row[8 * db + a / 2] = (uint8_t)(nib | (other << 4));
+        if (a == 0) row[p.g.D / 2 + db] = sc;
     }
-    uint8_t* row = row_at(p.kv, p.g, s, isv ? 1 : 0, h);
-    if ((reinterpret_cast<uintptr_t>(row) & 7) == 0) {
-        *reinterpret_cast<uint2*>(row + 8 * db) = make_uint2(lo, hi);
-    } else {                                             // rows of D % 128 != 0 are not 8-aligned
-#pragma unroll
-        for (int e = 0; e < 4; ++e) { row[8 * db + e] = (uint8_t)(lo >> (8 * e)); row[8 * db + 4 + e] = (uint8_t)(hi >> (8 * e)); }
-    }
-    row[p.g.D / 2 + db] = sc;
 }
 
-// Per-channel K of blocks completed by this call.  One CTA of D/2 threads per
-// 16 input tokens and head; thread cp owns channels 2cp, 2cp+1.  Rows of the block that
-// are not in this call come from the cache (stored per token by an earlier
-// call) and are dequantised first.
-__global__ void __launch_bounds__(128) store_channel_kernel(const StoreP p) {
+// Per-channel K of blocks completed by this call: one 512-thread CTA per 16
+// input tokens and head.  For each completing token the block's 16 x D values
+// are staged in shared memory first (rows this call brings from the input,
+// the others dequantised from their per-token form in the cache), then every
+// warp takes channel pairs: half-warp u owns channel 2cp+u, lane a evaluates
+// clip alpha_a, then lane e quantises token e.
+__global__ void __launch_bounds__(512) store_channel_kernel(const StoreP p) {
+    extern __shared__ float xs[];                        // [16][D]
     const int h = blockIdx.y;
     const int i_lo = blockIdx.x * PG, i_hi = min(i_lo + PG, p.N);
-    const int D = p.g.D, ND = D / BLK, cp = threadIdx.x;
+    const int D = p.g.D, ND = D / BLK;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, a = lane & 15, u = lane >> 4;
+    const int nwarp = blockDim.x >> 5;
     for (int i = i_lo; i < i_hi; ++i) {
         const int64_t s = p.slots[i];                    // uniform over the CTA
         if (!slot_ok(p, s) || s % PG != PG - 1) continue;
         const int64_t s0 = s - (PG - 1);
-        {
-            float x[2][BLK];
-#pragma unroll 1
-            for (int j = 0; j < PG; ++j) {
-                const int idx = i - (PG - 1) + j;
-                if (idx >= 0 && p.slots[idx] == s0 + j) {
-                    const int64_t base = (int64_t)idx * p.sk_t + (int64_t)h * p.sk_h;
-                    x[0][j] = ld_any(p.k, p.dt, base + (int64_t)(2 * cp) * p.sk_d);
-                    x[1][j] = ld_any(p.k, p.dt, base + (int64_t)(2 * cp + 1) * p.sk_d);
-                } else {
-                    const uint8_t* row = row_at(p.kv, p.g, s0 + j, 0, h);
-                    const uint32_t b = row[cp];
-                    const float sc = e4m3_to_f32(row[D / 2 + (2 * cp) / BLK]);
-                    x[0][j] = __fmul_rn(code_value(b & 0xF, p.fmt), sc);
-                    x[1][j] = __fmul_rn(code_value(b >> 4, p.fmt), sc);
-                }
+        for (int e = threadIdx.x; e < PG * D; e += blockDim.x) {
+            const int j = e / D, c = e % D;
+            const int idx = i - (PG - 1) + j;
+            float val;
+            if (idx >= 0 && p.slots[idx] == s0 + j) {
+                val = ld_any(p.k, p.dt, (int64_t)idx * p.sk_t + (int64_t)h * p.sk_h + (int64_t)c * p.sk_d);
+            } else {
+                const uint8_t* row = row_at(p.kv, p.g, s0 + j, 0, h);
+                val = __fmul_rn(code_value((row[c / 2] >> (4 * (c & 1))) & 0xF, p.fmt),
+                                e4m3_to_f32(row[D / 2 + c / BLK]));
             }
-            uint8_t sc[2];
-            float sv[2];
+            xs[j * D + c] = val;
+        }
+        __syncthreads();                                  // all rows read before any is rewritten
+        for (int cp = warp; cp < D / 2; cp += nwarp) {
+            const int c = 2 * cp + u;
+            float x[BLK];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) { sc[u] = calib_e4m3(x[u], p.fmt, p.calib); sv[u] = e4m3_to_f32(sc[u]); }
-            // every thread has read its rows before any row of the block is rewritten
-            __syncthreads();
-#pragma unroll 1
-            for (int j = 0; j < PG; ++j) {
-                uint8_t* row = row_at(p.kv, p.g, s0 + j, 0, h);
-                row[cp] = (uint8_t)(nibble_of(x[0][j], sv[0], p.fmt) | (nibble_of(x[1][j], sv[1], p.fmt) << 4));
-            }
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int c = 2 * cp + u;
-                row_at(p.kv, p.g, s0 + c / ND, 0, h)[D / 2 + c % ND] = sc[u];
-            }
+            for (int t = 0; t < BLK; ++t) x[t] = xs[t * D + c];
+            const uint8_t sc = calib_e4m3_hw(x, p.fmt, p.calib, a);
+            const uint32_t nib = nibble_of(xs[a * D + c], e4m3_to_f32(sc), p.fmt);
+            const uint32_t hi = __shfl_down_sync(0xffffffffu, nib, 16);
+            if (u == 0) row_at(p.kv, p.g, s0 + a, 0, h)[cp] = (uint8_t)(nib | (hi << 4));
+            if (a == 0) row_at(p.kv, p.g, s0 + c / ND, 0, h)[D / 2 + c % ND] = sc;
         }
         __syncthreads();
     }
@@ -981,11 +999,12 @@ extern "C" int kivi_paged_store(const void* k, const void* v, int in_dtype, int6
     p.N = N; p.g = make_geo(H, D); p.fmt = fmt; p.calib = calib;
     p.slots = slot_mapping; p.kv = kv_cache; p.nb = num_blocks; p.err = err;
     cudaStream_t st = (cudaStream_t)stream;
-    const int64_t total = (int64_t)N * H * 2 * (D / BLK);
-    store_token_kernel<<<(unsigned)((total + 127) / 128), 128, 0, st>>>(p);
+    const int64_t halves = (int64_t)N * H * 2 * (D / BLK);          // one half-warp per block
+    store_token_kernel<<<(unsigned)((halves * 16 + 255) / 256), 256, 0, st>>>(p);
     int e = check_launch();
     if (e) return e;
-    store_channel_kernel<<<dim3((unsigned)((N + PG - 1) / PG), (unsigned)H), D / 2, 0, st>>>(p);
+    store_channel_kernel<<<dim3((unsigned)((N + PG - 1) / PG), (unsigned)H), 512, (size_t)PG * D * sizeof(float),
+                           st>>>(p);
     return check_launch();
 }
 
