@@ -462,6 +462,70 @@ def serving_main(args, rank: int, world: int, local: int) -> None:
         os._exit(0)
 
 
+def paged_main(args, rank: int, world: int, local: int) -> None:
+    """The paged vLLM block layout: B=8 sequences per GPU of --seq tokens in a
+    shuffled block table, INT4 (or --fmt nvfp4) paged decode per step; CUDA
+    events around --steps eager steps; weak scaling over ranks, no collective."""
+    import torch
+    import torch.distributed as dist
+    from int4_kivi import paged
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    S = args.seq
+    nbs = (S + 15) // 16
+    k, v, q = make_inputs(S, seed=31 + rank, device=dev)
+    gp = torch.Generator(device="cpu").manual_seed(5 + rank)
+    bt = (torch.randperm(B * nbs, generator=gp) + 1).to(torch.int32).view(B, nbs).to(dev)
+    kv = torch.zeros(B * nbs + 1, 2, 16, HKV, paged.int4_kivi_kv_cache_full_dim(D), dtype=torch.uint8, device=dev)
+    store = paged.int4_kivi_store if args.fmt == "int4" else paged.nvfp4_kivi_store
+    dec = paged.int4_kivi_paged_decode if args.fmt == "int4" else paged.nvfp4_kivi_paged_decode
+    ar = torch.arange(16, device=dev)
+    for b in range(B):
+        slots = (bt[b].long()[:, None] * 16 + ar[None]).reshape(-1)[:S]
+        store(k[b].permute(1, 0, 2), v[b].permute(1, 0, 2), kv, slots, D)
+    del k, v
+    sl = torch.full((B,), S, dtype=torch.int32, device=dev)
+    out = torch.empty(B, HQ, D, dtype=torch.bfloat16, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        dec(q, kv, bt, sl, out=out)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        dec(q, kv, bt, sl, out=out)
+    e1.record()
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    if rank == 0:
+        peak, kind = _peaks()
+        by = B * HKV * S * 144
+        line = {"metric": f"packed-KV HBM GB/s ({args.fmt.upper()} paged decode, vLLM block layout)",
+                "value": round(world * by / ms / 1e6, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": f"{args.fmt} codes + e4m3 scales, f16 MMA, f32 acc",
+                "data": "synthetic (seeded, config-0 distribution; shuffled block table)",
+                "config": {"workload": f"paged: B={B}/GPU, Hq={HQ}, Hkv={HKV}, D={D}, S={S}, 144 B/token/head",
+                           "parallelism": f"sequence-shard x{world} (no collective)"},
+                "roofline": {"bound": "hbm", "achieved": round(by / ms / 1e6, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(by / ms / 1e6 / peak, 4), "peak_kind": kind,
+                             "timed": "whole step (tile table + decode + merge), CUDA events"},
+                "gpu_launches": 3 * args.steps}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -469,7 +533,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq", type=int, default=65536)
-    ap.add_argument("--workload", default="batch", choices=["batch", "longctx", "serving"],
+    ap.add_argument("--fmt", default="int4", choices=["int4", "nvfp4"], help="paged workload format")
+    ap.add_argument("--workload", default="batch", choices=["batch", "longctx", "serving", "paged"],
                     help="batch: B=8 sequences per GPU (weak scaling, no collective); "
                          "longctx: one 262144-token sequence split across GPUs with an NCCL (m,l,o) merge")
     args = ap.parse_args()
@@ -483,6 +548,8 @@ def main():
         return longctx_main(args, rank, world, local)
     if args.workload == "serving" and args.impl == "ours":
         return serving_main(args, rank, world, local)
+    if args.workload == "paged" and args.impl == "ours":
+        return paged_main(args, rank, world, local)
     if args.impl == "reference":
         if rank != 0:
             return

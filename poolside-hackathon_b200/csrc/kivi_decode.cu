@@ -299,7 +299,8 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
     const int g = lane >> 2, tq = lane & 3;
     const int G = p.G;
     const int src_k = ((2 * warp + (g >> 2)) << 2) | tq;   // lane holding my page's K scales
-    __half* pb = pbuf + warp * 8 * PB_PITCH;
+    const uint32_t pb_s = smem_u32(pbuf + warp * 8 * PB_PITCH);   // P staging [8 heads][PB_PITCH] halves
+    const uint32_t abort_s = smem_u32(&ctl->abort);
 
     uint32_t qB[8][2];
     float acc[8][4];     // [tile: 2*seg + (0:X,1:Y)][c]
@@ -371,19 +372,19 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
         const int s = it % NST;
         if (!mbar_wait_bounded(&ctl->full[s], (it / NST) & 1)) {
             set_err(p.err, KIVI_ERR_TIMEOUT);
-            ctl->abort = 1;
+            sts32s(abort_s, 1u);
         }
-        if (ctl->abort) break;
+        if (lds32s(abort_s)) break;
         uint8_t* st = stages + s * L::BYTES;
         const uint8_t* vs_base = st + L::VS;
         if (FMT == FMT_NVFP4) {
             // my 32 tokens' e4m3 V scales -> fp16 rows [token][8] (per-warp buffer)
             __half* vw = scv + warp * 32 * 8;
-            const uint2 raw = *reinterpret_cast<const uint2*>(st + L::VS + (32 * warp + lane) * 8);
+            const uint2 raw = lds64s(smem_u32(st + L::VS + (32 * warp + lane) * 8));
             __syncwarp();
-            *reinterpret_cast<uint4*>(vw + lane * 8) =
-                make_uint4(e4m3x2_to_h2((uint16_t)raw.x), e4m3x2_to_h2((uint16_t)(raw.x >> 16)),
-                           e4m3x2_to_h2((uint16_t)raw.y), e4m3x2_to_h2((uint16_t)(raw.y >> 16)));
+            sts128s(smem_u32(vw + lane * 8),
+                    make_uint4(e4m3x2_to_h2((uint16_t)raw.x), e4m3x2_to_h2((uint16_t)(raw.x >> 16)),
+                               e4m3x2_to_h2((uint16_t)raw.y), e4m3x2_to_h2((uint16_t)(raw.y >> 16))));
             __syncwarp();
             vs_base = reinterpret_cast<const uint8_t*>(vw) - 32 * warp * 16;
         }
@@ -491,10 +492,10 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
             l1 += (pr[4] + pr[5]) + (pr[6] + pr[7]);
             // stage P as fp16 [head][token] for the PV B-fragments
             __syncwarp();
-            *reinterpret_cast<uint2*>(pb + (2 * tq) * PB_PITCH + 4 * g) =
-                make_uint2(h2_as_u32(__floats2half2_rn(pr[0], pr[1])), h2_as_u32(__floats2half2_rn(pr[2], pr[3])));
-            *reinterpret_cast<uint2*>(pb + (2 * tq + 1) * PB_PITCH + 4 * g) =
-                make_uint2(h2_as_u32(__floats2half2_rn(pr[4], pr[5])), h2_as_u32(__floats2half2_rn(pr[6], pr[7])));
+            sts64s(pb_s + 2 * ((2 * tq) * PB_PITCH + 4 * g),
+                   h2_as_u32(__floats2half2_rn(pr[0], pr[1])), h2_as_u32(__floats2half2_rn(pr[2], pr[3])));
+            sts64s(pb_s + 2 * ((2 * tq + 1) * PB_PITCH + 4 * g),
+                   h2_as_u32(__floats2half2_rn(pr[4], pr[5])), h2_as_u32(__floats2half2_rn(pr[6], pr[7])));
             __syncwarp();
             // ------------------------------- PV -------------------------------
             const uint32_t vc_s = smem_u32(st + L::VC), vs_s = smem_u32(vs_base);
@@ -504,8 +505,8 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
 #pragma unroll
             for (int lam = 0; lam < 2; ++lam) {
                 const int prow = PAIRED ? (g & 3) : g;
-                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pb + prow * PB_PITCH + 16 * lam + 2 * tq);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(pb + prow * PB_PITCH + 16 * lam + 8 + 2 * tq);
+                const uint32_t b0 = lds32s(pb_s + 2 * (prow * PB_PITCH + 16 * lam + 2 * tq));
+                const uint32_t b1 = lds32s(pb_s + 2 * (prow * PB_PITCH + 16 * lam + 8 + 2 * tq));
 #pragma unroll
                 for (int sp = 0; sp < 2; ++sp) {          // segment pairs (2sp, 2sp+1)
                     const uint32_t trow = 32 * warp + 16 * lam + 8 * ((lane >> 3) & 1) + (lane & 7);
@@ -538,7 +539,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->empty[s]);
     }
-    if (cur >= 0 && !ctl->abort) flush(cur);
+    if (cur >= 0 && !lds32s(abort_s)) flush(cur);
     // let the dependent merge kernel start its prologue (programmatic launch)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }

@@ -415,17 +415,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
-// 32-bit shared-window addresses keep the consumer's many smem pointers in one register each
-__device__ __forceinline__ uint2 lds64s(uint32_t a) {
-    uint2 v;
-    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ uint32_t lds8s(uint32_t a) {
-    uint16_t v;
-    asm volatile("ld.shared.u8 %0, [%1];" : "=h"(v) : "r"(a));
-    return v;
-}
+// (32-bit shared-window addresses keep the consumer's many smem pointers in one register each)
 __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
     return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
 }
@@ -518,7 +508,8 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const __grid_c
     // ------------------------------- consumers --------------------------------
     const int h = warp, g = lane >> 2, tq = lane & 3;
     const uint32_t rowp = (uint32_t)p.rowp;
-    __half* pb = pbuf + warp * 8 * PBP;
+    const uint32_t pb = smem_u32(pbuf + warp * 8 * PBP);     // P staging [8 heads][PBP] halves
+    const uint32_t abort_s = smem_u32(&ctl->abort);
     uint32_t qf[2][4][2];
     float acc[8][4];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
@@ -576,9 +567,9 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const __grid_c
         const int s = it % p.nst;
         if (!mbar_wait_bounded(&ctl->full[s], (it / p.nst) & 1)) {
             set_err_flag(p.err, KIVI_ERR_TIMEOUT);
-            ctl->abort = 1;
+            sts32s(abort_s, 1u);
         }
-        if (ctl->abort) break;
+        if (lds32s(abort_s)) break;
         const uint32_t st_s = smem_u32(stages + s * SB);
         const int pg0 = cu.t * TP;
         // All TP blocks of the stage are processed together (TP independent
@@ -677,18 +668,18 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const __grid_c
                 const float p1 = exp2f(x[j][1] - r1), p3 = exp2f(x[j][3] - r1);
                 l0 += p0 + p2;
                 l1 += p1 + p3;
-                pb[(2 * tq) * PBP + 16 * j + ks] = __float2half_rn(p0);
-                pb[(2 * tq + 1) * PBP + 16 * j + ks] = __float2half_rn(p1);
-                pb[(2 * tq) * PBP + 16 * j + ks + 8] = __float2half_rn(p2);
-                pb[(2 * tq + 1) * PBP + 16 * j + ks + 8] = __float2half_rn(p3);
+                sts16s(pb + 2 * ((2 * tq) * PBP + 16 * j + ks), __float2half_rn(p0));
+                sts16s(pb + 2 * ((2 * tq + 1) * PBP + 16 * j + ks), __float2half_rn(p1));
+                sts16s(pb + 2 * ((2 * tq) * PBP + 16 * j + ks + 8), __float2half_rn(p2));
+                sts16s(pb + 2 * ((2 * tq + 1) * PBP + 16 * j + ks + 8), __float2half_rn(p3));
             }
             __syncwarp();
             // ------------------------------- PV -------------------------------
 #pragma unroll
             for (int j = 0; j < TP; ++j) {
                 const uint32_t vpg = st_s + (uint32_t)((j * 32 + 16) * rowp + h * FDD);
-                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pb + g * PBP + 16 * j + 2 * tq);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(pb + g * PBP + 16 * j + 2 * tq + 8);
+                const uint32_t b0 = lds32s(pb + 2 * (g * PBP + 16 * j + 2 * tq));
+                const uint32_t b1 = lds32s(pb + 2 * (g * PBP + 16 * j + 2 * tq + 8));
                 // k-slots (2tq, 2tq+1) = tokens (tq, tq+4); (2tq+8, 2tq+9) = (tq+8, tq+12)
                 const int tA = tq, tB = tq + 4, tC = tq + 8, tD = tq + 12;
                 const uint2 wa = lds64s(vpg + tA * rowp + 8 * g), wb = lds64s(vpg + tB * rowp + 8 * g);
@@ -724,7 +715,7 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const __grid_c
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->empty[s]);
     }
-    if (cur >= 0 && !ctl->abort) flush(cur);
+    if (cur >= 0 && !lds32s(abort_s)) flush(cur);
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
