@@ -34,7 +34,9 @@ BYTES_PER_TOKEN_HEAD = 160          # 64 K codes + 16 K scales + 64 V codes + 16
 METRIC = "packed-KV HBM GB/s (INT4-KIVI fused decode, 64K ctx)"
 # dram__bytes_read.sum + dram__bytes_write.sum of the split-K kernel, measured
 # with ncu on the 16384-token case and scaled by tokens to the 65536-token launch.
-TRAFFIC_PER_LAUNCH = 749.5e6
+TRAFFIC_PER_LAUNCH = 749.7e6
+# same for the paged decode kernel at 16384 tokens (profiles/paged_decode_int4_64k.md)
+PAGED_TRAFFIC_16K = 155.54e6
 
 
 def _peaks():
@@ -519,7 +521,10 @@ def paged_main(args, rank: int, world: int, local: int) -> None:
                            "parallelism": f"sequence-shard x{world} (no collective)"},
                 "roofline": {"bound": "hbm", "achieved": round(by / ms / 1e6, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(by / ms / 1e6 / peak, 4), "peak_kind": kind,
-                             "timed": "whole step (tile table + decode + merge), CUDA events"},
+                             "timed": "whole step (tile table + decode + merge), CUDA events",
+                             "traffic": round(PAGED_TRAFFIC_16K * S / 16384) if args.fmt == "int4" else None,
+                             "traffic_note": "ncu dram read+write of one 16384-token launch scaled by tokens "
+                                             "(profiles/paged_decode_int4_64k.md)"},
                 "gpu_launches": 3 * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
