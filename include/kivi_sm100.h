@@ -134,6 +134,20 @@ int kivi_decode(const void *q, int64_t q_sb, int64_t q_sh,
                 void *out, float *work, int64_t work_floats, int *err,
                 kivi_stream_t stream);
 
+/* Decode over a cache that keeps its partial last page unquantised (the   */
+/* HuggingFace cache layout, int4_kivi/hf_cache.py:107-190): the first      */
+/* (S/16)*16 tokens from the packed pages, the last S % 16 tokens from bf16 */
+/* k_hot AND v_hot (both [B*Hkv, hot_stride, D]); v_packed / v_scale cover  */
+/* only the paged tokens.  Otherwise identical to kivi_decode.              */
+int kivi_decode_bf16_tail(const void *q, int64_t q_sb, int64_t q_sh,
+                          const uint8_t *k_packed, const void *k_scale, int k_np_stride,
+                          const void *k_hot, const void *v_hot, int hot_stride,
+                          const uint8_t *v_packed, const void *v_scale, int v_s_stride,
+                          int B, int Hq, int Hkv, int S, int D, int fmt,
+                          float sm_scale, float g_k, float g_v,
+                          void *out, float *work, int64_t work_floats, int *err,
+                          kivi_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* Variable-length batch decode.  Same as kivi_decode, but batch entry b      */
 /* attends only its first seq_lens[b] tokens (device int32 [B], each in      */

@@ -60,6 +60,9 @@ struct DecodeParams {
     // offsets [B*Hkv + 1] the prologue kernel derives from them
     const int* seq_lens;
     int* tile_off;
+    // optional bf16 V of the tail tokens [BH, hot_stride, D] (caches that keep
+    // the partial page unquantised); nullptr = the tail's V comes from v_packed
+    const __nv_bfloat16* v_hot;
 };
 
 __host__ __device__ inline int64_t tile_start(int64_t c, int64_t W, int N) { return c * W / N; }
@@ -652,6 +655,16 @@ __host__ __device__ inline void head_cta_range(int64_t a0, int64_t a1, int64_t W
     c_hi = (int)(hi < N - 1 ? hi : N - 1);
 }
 
+// V of tail token j (absolute n_full + j) at channel d: bf16 when the caller
+// keeps the partial page unquantised, else dequantised from v_packed.
+template <int FMT>
+__device__ __forceinline__ float tail_v(const DecodeParams& p, int bh, int n_full, int j, int d, int ND) {
+    if (p.v_hot) return __bfloat162float(p.v_hot[((int64_t)bh * p.hot_stride + j) * p.D + d]);
+    const int64_t vr = ((int64_t)bh * p.v_s_stride + n_full + j) * ND + d / BLK;
+    const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
+    return gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int mode, __nv_bfloat16* out,
                                                       float* m_out, float* l_out, float* acc_out) {
@@ -738,11 +751,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         __syncthreads();
         const int d = threadIdx.x;
         float a = (sacc[d] + sacc[DH + d]) + (sacc[2 * DH + d] + sacc[3 * DH + d]);
-        for (int j = 0; j < hot; ++j) {
-            const int64_t vr = ((int64_t)bh * p.v_s_stride + n_full + j) * ND + d / BLK;
-            const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
-            a += w[ns + j] * (gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v));
-        }
+        for (int j = 0; j < hot; ++j) a += w[ns + j] * tail_v<FMT>(p, bh, n_full, j, d, ND);
         if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
         else acc_out[row * D + d] = a;
         if (mode == 1 && threadIdx.x == 0) { m_out[row] = M; l_out[row] = Ls; }
@@ -751,11 +760,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float a = 0.f;
         for (int i = 0; i < ns; ++i) if (w[i] != 0.f) a += p.part_acc[slot(i) * D + d] * w[i];
-        for (int j = 0; j < hot; ++j) {
-            const int64_t vr = ((int64_t)bh * p.v_s_stride + n_full + j) * ND + d / BLK;
-            const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
-            a += w[ns + j] * (gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v));
-        }
+        for (int j = 0; j < hot; ++j) a += w[ns + j] * tail_v<FMT>(p, bh, n_full, j, d, ND);
         if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
         else acc_out[row * D + d] = a;
     }
@@ -879,15 +884,17 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
                 const uint8_t* v_packed, const void* v_scale, int v_s_stride, int B, int Hq, int Hkv,
                 int S, int D, int fmt, float sm_scale, float g_k, float g_v, void* out, float* m_out,
                 float* l_out, float* acc_out, float* work, int64_t work_floats, int* err,
-                kivi_stream_t stream, const int* seq_lens = nullptr) {
+                kivi_stream_t stream, const int* seq_lens = nullptr, const void* v_hot = nullptr) {
     if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || S < 0 || D <= 0 || D % BLK) return KIVI_ERR_ARG;
     if (fmt != FMT_INT4 && fmt != FMT_NVFP4) return KIVI_ERR_ARG;
     const int G = Hq / Hkv, BH = B * Hkv;
     const int n_full = (S / BLK) * BLK, hot = S - n_full;
-    if (k_np_stride < n_full / BLK || v_s_stride < S || (hot > 0 && hot_stride < hot)) return KIVI_ERR_ARG;
+    const int v_tokens = v_hot ? n_full : S;          // tokens v_packed must cover
+    if (k_np_stride < n_full / BLK || v_s_stride < v_tokens || (hot > 0 && hot_stride < hot)) return KIVI_ERR_ARG;
+    if (hot > 0 && v_hot && !k_hot) return KIVI_ERR_ARG;
     if (!q || (!out && mode == 0) || (mode == 1 && (!m_out || !l_out || !acc_out))) return KIVI_ERR_ARG;
     if (n_full > 0 && (!k_packed || !k_scale)) return KIVI_ERR_ARG;
-    if (S > 0 && (!v_packed || !v_scale)) return KIVI_ERR_ARG;
+    if (v_tokens > 0 && (!v_packed || !v_scale)) return KIVI_ERR_ARG;
     if (hot > 0 && !k_hot) return KIVI_ERR_ARG;
     int dev = 0;
     const int sms = num_sms(&dev);
@@ -917,6 +924,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     p.part_m = work; p.part_l = work + pl.slots * G; p.part_acc = work + 2 * pl.slots * G;
     p.err = err;
     p.seq_lens = seq_lens;
+    p.v_hot = reinterpret_cast<const __nv_bfloat16*>(v_hot);
     p.tile_off = seq_lens ? reinterpret_cast<int*>(work + pl.slots * G * (2 + (int64_t)D)) : nullptr;
     cudaStream_t st = (cudaStream_t)stream;
     if (seq_lens && pl.W > 0) {
@@ -1016,6 +1024,18 @@ extern "C" int kivi_decode(const void* q, int64_t q_sb, int64_t q_sh, const uint
     return decode_impl(0, q, q_sb, q_sh, k_packed, k_scale, k_np_stride, k_hot, hot_stride, v_packed, v_scale,
                        v_s_stride, B, Hq, Hkv, S, D, fmt, sm_scale, g_k, g_v, out, nullptr, nullptr, nullptr,
                        work, work_floats, err, stream);
+}
+
+extern "C" int kivi_decode_bf16_tail(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,
+                                     const void* k_scale, int k_np_stride, const void* k_hot, const void* v_hot,
+                                     int hot_stride, const uint8_t* v_packed, const void* v_scale,
+                                     int v_s_stride, int B, int Hq, int Hkv, int S, int D, int fmt,
+                                     float sm_scale, float g_k, float g_v, void* out, float* work,
+                                     int64_t work_floats, int* err, kivi_stream_t stream) {
+    if ((S % BLK) && !v_hot) return KIVI_ERR_ARG;
+    return decode_impl(0, q, q_sb, q_sh, k_packed, k_scale, k_np_stride, k_hot, hot_stride, v_packed, v_scale,
+                       v_s_stride, B, Hq, Hkv, S, D, fmt, sm_scale, g_k, g_v, out, nullptr, nullptr, nullptr,
+                       work, work_floats, err, stream, nullptr, v_hot);
 }
 
 extern "C" int kivi_decode_partial(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,

@@ -43,12 +43,15 @@ def _stacked_geometry(st: dict) -> tuple[int, int, dict]:
 
 def decode_packed(q: Tensor, st: dict, n_qh: int, sm_scale: Optional[float] = None,
                   fmt: Optional[str] = None, g_k: Optional[float] = None, g_v: Optional[float] = None,
-                  out: Optional[Tensor] = None, partial: bool = False):
+                  out: Optional[Tensor] = None, partial: bool = False, v_hot: Optional[Tensor] = None):
     """Core entry: q [B, n_qh, D] bf16 over a stacked packed cache (B*H heads).
 
     Returns bf16 [B, n_qh, D], or with partial=True the merged per-row state
     (m [B*n_qh] in log2 units, l [B*n_qh], acc [B*n_qh, D]) for a cross-GPU
-    log-sum-exp merge."""
+    log-sum-exp merge.  With v_hot (bf16 [B*H, S % 16, D]) the tail tokens'
+    V is taken unquantised like their K (caches that keep the partial page in
+    bf16); v_packed then only has to cover the paged tokens, and the packed
+    tensors may be None when there is no full page yet."""
     B, H, S, D = st["B"], st["H"], st["S"], st["D"]
     fmt = st.get("fmt", "int4") if fmt is None else fmt
     g_k = st.get("g_k", 1.0) if g_k is None else g_k
@@ -61,7 +64,11 @@ def decode_packed(q: Tensor, st: dict, n_qh: int, sm_scale: Optional[float] = No
     q = q.to(torch.bfloat16)
     if q.stride(2) != 1:
         q = q.contiguous()
-    nps, ss, st = _stacked_geometry(st)
+    if st["k_packed"] is None:                 # no full page yet (tail-only, v_hot path)
+        assert v_hot is not None and S < 16, "packed tensors are required once a page is full"
+        nps, ss = 1, 16
+    else:
+        nps, ss, st = _stacked_geometry(st)
     khot = st["k_hot"]
     if khot.shape[1] and khot.stride(2) != 1 or khot.shape[1] and khot.stride(1) != D:
         khot = khot.contiguous()
@@ -84,6 +91,19 @@ def decode_packed(q: Tensor, st: dict, n_qh: int, sm_scale: Optional[float] = No
         return m, l, acc
     if out is None:
         out = torch.empty((B, n_qh, D), dtype=torch.bfloat16, device=dev)
+    if v_hot is not None and hot_stride:
+        assert not partial and st.get("seq_lens") is None, "v_hot is for plain (non-partial, uniform) decode"
+        vh = v_hot.to(torch.bfloat16)
+        if vh.shape != khot.shape or not vh.is_contiguous():
+            vh = vh.contiguous()
+        assert vh.shape == khot.shape, "v_hot must match k_hot [B*H, S % 16, D]"
+        pk = lambda name: N.ptr(st[name]) if st[name] is not None else None
+        rc = L.kivi_decode_bf16_tail(
+            N.ptr(q), q.stride(0), q.stride(1), pk("k_packed"), pk("k_scale"), nps, N.ptr(khot), N.ptr(vh),
+            hot_stride, pk("v_packed"), pk("v_scale"), ss, B, n_qh, H, S, D, N.FMT[fmt], sm_scale, g_k, g_v,
+            N.ptr(out), N.ptr(work), work.numel(), N.ptr(err), N.stream_of(q))
+        N.check(rc, "kivi_decode_bf16_tail")
+        return out
     if st.get("seq_lens") is not None:
         sl = st["seq_lens"]
         assert sl.is_cuda and sl.dtype == torch.int32 and sl.numel() == B

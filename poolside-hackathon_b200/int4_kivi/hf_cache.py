@@ -13,6 +13,16 @@ B200 differences (values returned are identical):
   * the dequantised prefix is kept in a grow-only bf16 buffer and only newly
     frozen pages are dequantised per step, instead of every chunk on every
     step (hf_cache.py:137-154 re-dequantised O(S) bytes per token).
+
+Fused read path (`Int4KiviCache(config, fused_decode=True)` together with
+`enable_fused_decode(model)`): single-token steps of full-attention layers do
+not materialise bf16 K/V at all.  `update` stores the token and returns an
+empty placeholder tagged with its layer; the "int4_kivi" attention function
+then runs the fused decode on the packed pages plus the bf16 partial page
+(K and V both unquantised, as `update` would have returned them).  Prefill
+and sliding-window layers keep the dequantise + SDPA path, with the
+dequantised prefix built per call instead of kept, so the cache holds only
+packed pages and at most 15 bf16 tokens per layer.
 """
 from __future__ import annotations
 
@@ -23,13 +33,16 @@ from transformers.cache_utils import Cache, CacheLayerMixin
 
 from .cache import BLOCK, KIVICache, alloc_packed, append_kivi, dequant_kivi, store_kivi
 
+ATTN_IMPL = "int4_kivi"
+
 
 class _Int4KiviLayer(CacheLayerMixin):
     def __init__(self, k_calib: str = "mse", v_calib: str = "mse", is_sliding: bool = False,
-                 sliding_window: int | None = None):
+                 sliding_window: int | None = None, fused_decode: bool = False):
         super().__init__()
         self.k_calib, self.v_calib = k_calib, v_calib
         self.is_sliding, self.sliding_window = is_sliding, sliding_window
+        self.fused = fused_decode and not is_sliding
         self.store: KIVICache | None = None     # frozen pages (S multiple of 16)
         self.hot_k: Tensor | None = None        # [H, t < 16, D] bf16
         self.hot_v: Tensor | None = None
@@ -112,6 +125,9 @@ class _Int4KiviLayer(CacheLayerMixin):
 
     def _dequant_frozen(self) -> tuple[Tensor, Tensor]:
         S = 0 if self.store is None else self.store.S
+        if self.fused:                      # no persistent bf16 copy in fused mode
+            k_all, v_all = dequant_kivi(self.store)
+            return k_all[:, self._offset:S], v_all[:, self._offset:S]
         if S > self._deq_len:
             k_all, v_all = dequant_kivi(self.store)   # newly frozen pages only are kept below
             H, _, D = k_all.shape
@@ -145,6 +161,11 @@ class _Int4KiviLayer(CacheLayerMixin):
             self.hot_v = torch.cat([self.hot_v, v_new], dim=1)
         self._freeze_pages()
         self._evict_sliding(n_new)
+        if self.fused and n_new == 1:
+            # the "int4_kivi" attention function reads the packed pages itself
+            stub = torch.empty((1, self._H, 0, self._D), dtype=torch.bfloat16, device=k_new.device)
+            stub._kivi_layer = self
+            return stub, stub
         ks, vs = [], []
         if self._frozen_len() > 0:
             fk, fv = self._dequant_frozen()
@@ -158,6 +179,21 @@ class _Int4KiviLayer(CacheLayerMixin):
             if k_full.shape[1] > want:
                 k_full, v_full = k_full[:, -want:], v_full[:, -want:]
         return k_full.unsqueeze(0), v_full.unsqueeze(0)
+
+    def fused_decode(self, query: Tensor, scaling: float | None) -> Tensor:
+        """Attention of one query token per head over everything stored:
+        query [1, Hq, 1, D] -> bf16 [1, Hq, D]."""
+        from .decode import decode_packed
+        Hq, D = query.shape[1], query.shape[3]
+        frozen, t = self._frozen_len(), self._hot_len()
+        c = self.store
+        st = dict(k_packed=c.k_packed if frozen else None, k_scale=c.k_scale if frozen else None,
+                  v_packed=c.v_packed if frozen else None, v_scale=c.v_scale if frozen else None,
+                  k_hot=self.hot_k if t else torch.empty((self._H, 0, D), dtype=torch.bfloat16,
+                                                         device=query.device),
+                  H=self._H, S=frozen + t, D=D, B=1)
+        q = query[:, :, 0].to(torch.bfloat16)
+        return decode_packed(q, st, Hq, sm_scale=scaling, v_hot=self.hot_v if t else None)
 
     # -- memory accounting ----------------------------------------------------
     def nbytes(self) -> int:
@@ -173,7 +209,7 @@ class _Int4KiviLayer(CacheLayerMixin):
         return 2 * (self._stored_len() * getattr(self, "_H", 0) * getattr(self, "_D", 0)) * 2
 
     def reset(self) -> None:
-        self.__init__(self.k_calib, self.v_calib, self.is_sliding, self.sliding_window)
+        self.__init__(self.k_calib, self.v_calib, self.is_sliding, self.sliding_window, self.fused)
 
     def reorder_cache(self, beam_idx) -> None:
         pass
@@ -195,7 +231,7 @@ class Int4KiviCache(Cache):
         model.generate(..., past_key_values=cache)
     """
 
-    def __init__(self, config, k_calib: str = "mse", v_calib: str = "mse"):
+    def __init__(self, config, k_calib: str = "mse", v_calib: str = "mse", fused_decode: bool = False):
         decoder = config.get_text_config(decoder=True)
         sliding_window = getattr(decoder, "sliding_window", None) or getattr(decoder, "attention_chunk_size", None)
         layer_types = getattr(decoder, "layer_types", None)
@@ -203,7 +239,8 @@ class Int4KiviCache(Cache):
             kind = "sliding_attention" if sliding_window is not None else "full_attention"
             layer_types = [kind] * decoder.num_hidden_layers
         layers = [_Int4KiviLayer(k_calib=k_calib, v_calib=v_calib, is_sliding=(lt == "sliding_attention"),
-                                 sliding_window=sliding_window if lt == "sliding_attention" else None)
+                                 sliding_window=sliding_window if lt == "sliding_attention" else None,
+                                 fused_decode=fused_decode)
                   for lt in layer_types]
         super().__init__(layers=layers)
 
@@ -215,3 +252,26 @@ class Int4KiviCache(Cache):
 
     def compression_ratio_vs_bf16(self) -> float:
         return self.bf16_nbytes() / max(self.nbytes(), 1)
+
+
+def kivi_attention_forward(module, query: Tensor, key: Tensor, value: Tensor, attention_mask, dropout: float = 0.0,
+                           scaling: float | None = None, **kwargs):
+    """transformers attention function ("int4_kivi"): placeholders from a fused
+    Int4KiviCache layer go to the fused decode; anything else (prefill,
+    sliding layers, no cache) to the stock SDPA function."""
+    layer = getattr(key, "_kivi_layer", None)
+    if layer is None:
+        from transformers.integrations.sdpa_attention import sdpa_attention_forward
+        return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout,
+                                      scaling=scaling, **kwargs)
+    assert query.shape[0] == 1 and query.shape[2] == 1, "fused decode takes one query token (batch 1)"
+    out = layer.fused_decode(query, scaling)              # [1, Hq, D]
+    return out[:, None].to(query.dtype), None             # [B, q_len, Hq, D]
+
+
+def enable_fused_decode(model) -> None:
+    """Register the "int4_kivi" attention function and switch `model` to it;
+    pair with `Int4KiviCache(model.config, fused_decode=True)`."""
+    from transformers import AttentionInterface
+    AttentionInterface.register(ATTN_IMPL, kivi_attention_forward)
+    model.set_attn_implementation(ATTN_IMPL)

@@ -75,3 +75,91 @@ def test_generate_with_tiny_random_model(cuda_dev):
     assert out.shape == (1, 64)
     assert cache.layers[0].get_seq_length() == 63
     assert cache.compression_ratio_vs_bf16() > 1.5
+
+
+def _ref_attention(q, k, v, scale):
+    """fp32 attention of q [Hq, D] over k, v [H, S, D] (GQA by repeat)."""
+    G = q.shape[0] // k.shape[0]
+    kk = k.float().repeat_interleave(G, 0)
+    vv = v.float().repeat_interleave(G, 0)
+    p = torch.softmax((q.float()[:, None] @ kk.transpose(1, 2))[:, 0] * scale, -1)
+    return (p[:, None] @ vv)[:, 0]
+
+
+def _exact_kv(layer):
+    """fp32 K/V a layer holds: packed pages dequantised exactly (code *
+    fp32(scale), the oracle's dequant; `update` returns them rounded to bf16)
+    followed by the bf16 partial page."""
+    import oracle
+    ks, vs = [], []
+    if layer._frozen_len():
+        c = layer.store
+        d = dict(k_packed=c.k_packed.cpu().numpy(), k_scale=c.k_scale.cpu().numpy(),
+                 v_packed=c.v_packed.cpu().numpy(), v_scale=c.v_scale.cpu().numpy(),
+                 k_hot=c.k_hot.float().cpu().numpy(), H=c.H, S=c.S, D=c.D)
+        k, v = oracle.dequant_int4(d)
+        ks.append(torch.from_numpy(k)); vs.append(torch.from_numpy(v))
+    if layer._hot_len():
+        ks.append(layer.hot_k.float().cpu()); vs.append(layer.hot_v.float().cpu())
+    return torch.cat(ks, 1), torch.cat(vs, 1)
+
+
+def test_fused_decode_matches_dequant_path(cuda_dev):
+    """The fused read path (packed pages + bf16 partial page, no bf16 K/V
+    materialised) equals fp32 attention over the same stored tokens, and the
+    plain layer's `update` returns those tokens (rounded to bf16):
+    |out - ref| <= 2e-3 + |ref| * 2^-8, including steps with no full page yet
+    and steps right after a page freezes."""
+    from int4_kivi.hf_cache import _Int4KiviLayer
+    H, Hq, D = 2, 8, 128
+    k, v, _ = gen_kv(H, 120, D, seed=8)
+    kd, vd = k.to(cuda_dev), v.to(cuda_dev)
+    g = torch.Generator().manual_seed(9)
+    for pre in (5, 37):
+        plain, fused = _Int4KiviLayer(), _Int4KiviLayer(fused_decode=True)
+        plain.update(kd[None, :, :pre], vd[None, :, :pre])
+        fused.update(kd[None, :, :pre], vd[None, :, :pre])
+        for t in range(pre, 100):
+            kk, vv = plain.update(kd[None, :, t:t + 1], vd[None, :, t:t + 1])
+            stub, _ = fused.update(kd[None, :, t:t + 1], vd[None, :, t:t + 1])
+            assert stub.shape[2] == 0 and stub._kivi_layer is fused
+            q = torch.randn(1, Hq, 1, D, generator=g).bfloat16().to(cuda_dev)
+            out = fused.fused_decode(q, D ** -0.5)[0].float().cpu()
+            ek, ev = _exact_kv(fused)
+            assert torch.equal(ek.bfloat16(), kk[0].cpu()) and torch.equal(ev.bfloat16(), vv[0].cpu())
+            ref = _ref_attention(q[0, :, 0].cpu(), ek, ev, D ** -0.5)
+            err = (out - ref).abs()
+            assert bool((err <= 2e-3 + ref.abs() * 2.0 ** -8).all()), (pre, t, err.max().item())
+        assert fused.get_seq_length() == plain.get_seq_length() == 100
+        assert fused._deq_k is None                          # no bf16 copy kept in fused mode
+
+
+def test_fused_generate_tiny_random_model(cuda_dev):
+    """Teacher-forced decode of a random tiny Llama: the fused path's logits
+    track the dequantise + SDPA path's; greedy generate runs end to end."""
+    transformers = pytest.importorskip("transformers")
+    from int4_kivi.hf_cache import Int4KiviCache, enable_fused_decode
+    cfg = transformers.LlamaConfig(vocab_size=128, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                                   num_attention_heads=8, num_key_value_heads=2, head_dim=128,
+                                   max_position_embeddings=512)
+    torch.manual_seed(0)
+    model = transformers.LlamaForCausalLM(cfg).to(cuda_dev, torch.bfloat16).eval()
+    ids = torch.randint(0, 128, (1, 80), device=cuda_dev)
+    with torch.no_grad():
+        c_ref = Int4KiviCache(config=cfg)
+        ref = [model(ids[:, :40], past_key_values=c_ref).logits[:, -1]]
+        for t in range(40, 80):
+            ref.append(model(ids[:, t:t + 1], past_key_values=c_ref).logits[:, -1])
+        enable_fused_decode(model)
+        c_f = Int4KiviCache(config=cfg, fused_decode=True)
+        got = [model(ids[:, :40], past_key_values=c_f).logits[:, -1]]
+        for t in range(40, 80):
+            got.append(model(ids[:, t:t + 1], past_key_values=c_f).logits[:, -1])
+    r, g_ = torch.stack(ref).float(), torch.stack(got).float()
+    assert torch.equal(r[0], g_[0])                           # prefill takes the same path
+    assert (r - g_).abs().max().item() <= 0.02 * r.abs().max().item()
+    assert all(l._deq_k is None for l in c_f.layers)         # no bf16 copy of the prefix kept
+    out = model.generate(ids[:, :40], max_new_tokens=16, do_sample=False,
+                         past_key_values=Int4KiviCache(config=cfg, fused_decode=True))
+    assert out.shape == (1, 56)
+    model.set_attn_implementation("sdpa")
