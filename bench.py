@@ -179,7 +179,7 @@ def time_graph(g, seconds: float = 1.5) -> float:
     return e0.elapsed_time(e1) / n
 
 
-def extra_configs(dev, peak: float) -> dict:
+def extra_configs(dev, peak: float, int4_ms: float | None = None) -> dict:
     """Secondary BASELINE configs on one GPU, each step captured in a CUDA graph:
     c1 (INT4, S=8192) and c2 (NVFP4 at 65536 tokens: a 16-token quant-store
     into the cache followed by decode over the whole cache), then the same
@@ -228,7 +228,35 @@ def extra_configs(dev, peak: float) -> dict:
     del st2, c, g2, kp, ks, vp, vs
     torch.cuda.empty_cache()
     res.update(paged_configs(dev, peak))
+    res.update(bf16_comparator(dev, peak, int4_ms))
     return res
+
+
+def bf16_comparator(dev, peak: float, int4_ms: float | None) -> dict:
+    """The reference's int4-vs-bf16 comparison (scripts/speedup_int4_kivi.py:
+    47-168 times a bf16 split-K decode of the same shapes): here the bf16
+    decode is torch's fused SDPA (native GQA) over a bf16 cache of the
+    headline shapes at 65536 tokens, graph-captured; `int4_speedup` is its
+    step time over the INT4 headline step time."""
+    import torch
+    S = 65536
+    k, v, q = make_inputs(S, seed=13, device=dev)
+    q4 = q[:, :, None]
+    out = torch.empty(B, HQ, 1, D, dtype=torch.bfloat16, device=dev)
+
+    def step():
+        out.copy_(torch.nn.functional.scaled_dot_product_attention(q4, k, v, scale=1.0 / math.sqrt(D),
+                                                                   enable_gqa=True))
+    g = graph_step(step)
+    ms = time_graph(g)
+    by = B * HKV * S * D * 2 * 2
+    r = {"ms_per_step": round(ms, 4), "GB/s": round(by / ms / 1e6, 1), "frac": round(by / ms / 1e6 / peak, 4),
+         "decode_tok_s": round(B / ms * 1e3, 1), "bytes_per_step": by, "kernel": "torch SDPA (bf16, GQA)"}
+    if int4_ms:
+        r["int4_speedup"] = round(ms / int4_ms, 3)
+    del g, k, v
+    torch.cuda.empty_cache()
+    return {"bf16_sdpa_S65536": r}
 
 
 def paged_configs(dev, peak: float) -> dict:
@@ -633,7 +661,7 @@ def main():
         gbs = world * packed_bytes / (ms * 1e-3) / 1e9
         achieved = packed_bytes / (ms * 1e-3) / 1e9
         cpu_gbs, sample, thr, _ = cpu_reference(S, 3, 1, budget_s=15.0)
-        extra = extra_configs(dev, peak) if world == 1 else None
+        extra = extra_configs(dev, peak, ms if S == 65536 else None) if world == 1 else None
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
