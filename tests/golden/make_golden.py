@@ -55,8 +55,11 @@ def pack_codes(codes: torch.Tensor) -> np.ndarray:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("KIVI_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("KIVI_REFERENCE"),
+                    help="checkout of a1exxd0/poolside-hackathon (or set KIVI_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or KIVI_REFERENCE) is required")
     sys.path.insert(0, args.reference)
     sys.path.insert(0, os.path.join(args.reference, "scripts"))
     import kv_quant  # noqa: E402
