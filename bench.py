@@ -338,9 +338,14 @@ def longctx_main(args, rank: int, world: int, local: int) -> None:
     st = dict(k_packed=c.k_packed, k_scale=c.k_scale, k_hot=c.k_hot, v_packed=c.v_packed, v_scale=c.v_scale,
               H=HKV, S=b - a, D=D, B=1)
 
+    merger = None
+    if world > 1 and args.merge != "nccl":
+        from int4_kivi.distributed import PeerMerge, SeqParallelExchange
+        merger = (SeqParallelExchange if args.merge == "fused" else PeerMerge)(HQ, D, dev)
+
     def step():
         if world > 1:
-            return seq_parallel_decode(q, st, HQ)
+            return seq_parallel_decode(q, st, HQ, merger=merger)
         return decode_packed(q, st, HQ)
 
     def barrier():
@@ -376,7 +381,11 @@ def longctx_main(args, rank: int, world: int, local: int) -> None:
                 "scaling": "strong", "vs_baseline": None, "dtype": "int4 codes, f16 MMA, f32 accumulate",
                 "data": "synthetic (seeded, config-0 distribution)",
                 "config": {"workload": "c4: B=1, S=262144, Hq=32, Hkv=8, D=128, sequence split across GPUs",
-                           "parallelism": f"sequence-parallel x{world} + NCCL all_gather of (m,l,acc)"},
+                           "parallelism": f"sequence-parallel x{world}" + (
+                               "" if world == 1 else {"fused": " + merge fused into the decode's combine kernel, "
+                                                                "(m,l,acc) read over NVLink peer memory",
+                                                      "p2p": " + (m,l,acc) publish/merge over NVLink peer memory",
+                                                      "nccl": " + NCCL all_gather of (m,l,acc)"}[args.merge])},
                 "decode_tok_s": round(1 / ms * 1e3, 1),
                 "per_gpu_frac_of_roof": round(by / world / ms / 1e6 / peak, 4)}
         print(json.dumps(line), flush=True)
@@ -384,6 +393,8 @@ def longctx_main(args, rank: int, world: int, local: int) -> None:
     # process-group destroy with a live captured collective can block at exit.
     del gr
     torch.cuda.synchronize()
+    if merger is not None:
+        merger.close()
     if world > 1:
         dist.barrier()
         sys.stdout.flush()
@@ -567,6 +578,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq", type=int, default=65536)
     ap.add_argument("--fmt", default="int4", choices=["int4", "nvfp4"], help="paged workload format")
+    ap.add_argument("--merge", default="fused", choices=["fused", "p2p", "nccl"],
+                    help="longctx: merge the partial states inside the decode's combine kernel over NVLink "
+                         "peer memory, with separate publish/merge launches over peer memory, or by NCCL")
     ap.add_argument("--workload", default="batch", choices=["batch", "longctx", "serving", "paged"],
                     help="batch: B=8 sequences per GPU (weak scaling, no collective); "
                          "longctx: one 262144-token sequence split across GPUs with an NCCL (m,l,o) merge")

@@ -269,6 +269,63 @@ int kivi_paged_decode(const void *q, int64_t q_sb, int64_t q_sh,
                       void *out, float *work, int64_t work_floats, int *err,
                       kivi_stream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* Sequence-parallel decode with the cross-GPU merge fused into the decode's */
+/* own combine kernel (no reference counterpart; replaces decode_partial +  */
+/* all-gather + merge).  Every rank calls it with its KV range of the same  */
+/* B sequences; the combine CTA of each output row publishes the rank-local */
+/* (m, l, acc) of that row into this rank's exchange buffer xbuf, releases  */
+/* the row's epoch to every rank, waits (at most timeout_ns, else *err =    */
+/* KIVI_ERR_TIMEOUT and the row is left unwritten) for every rank's state   */
+/* of the row, reads them through peer_bufs[W] (all ranks' xbuf addresses, */
+/* own included) and writes the merged bf16 row.  xbuf:                     */
+/* kivi_seqpar_buffer_bytes(B*Hq, D, W) bytes from kivi_peer_alloc (zeroed), */
+/* row_epoch: zeroed device uint32 [B*Hq] kept across calls.  Two launches  */
+/* per call, graph-capturable.  Other arguments as kivi_decode.             */
+/* ------------------------------------------------------------------------ */
+int64_t kivi_seqpar_buffer_bytes(int rows, int D, int W);
+int kivi_decode_seqpar(const void *q, int64_t q_sb, int64_t q_sh,
+                       const uint8_t *k_packed, const void *k_scale, int k_np_stride,
+                       const void *k_hot, int hot_stride,
+                       const uint8_t *v_packed, const void *v_scale, int v_s_stride,
+                       int B, int Hq, int Hkv, int S, int D, int fmt,
+                       float sm_scale, float g_k, float g_v,
+                       void *xbuf, const uint64_t *peer_bufs, int W, int rank,
+                       unsigned int *row_epoch, long long timeout_ns,
+                       void *out, float *work, int64_t work_floats, int *err,
+                       kivi_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Cross-GPU merge over NVLink peer memory (sequence-parallel decode).       */
+/*                                                                           */
+/* No reference counterpart (the reference is single-GPU); replaces the      */
+/* all-gather + kivi_lse_merge pair with direct peer reads.  Each rank       */
+/* allocates kivi_peer_buffer_bytes(rows, D, W) bytes with kivi_peer_alloc   */
+/* (zeroed; returns a 64-byte CUDA IPC handle), exchanges the handles over   */
+/* the host, maps the others with kivi_peer_open, and passes the device     */
+/* array of all W ranks' buffer addresses (peer_bufs[W], own one included)  */
+/* and a zeroed device uint32 epoch counter.  Per decode step:              */
+/*   kivi_peer_publish: copy this rank's (m [rows] in log2 units, l [rows],  */
+/*     acc [rows, D]) into its buffer and release the next epoch to every    */
+/*     rank's flag for this rank;                                            */
+/*   kivi_peer_merge: wait until every rank published that epoch (at most    */
+/*     timeout_ns, else *err = KIVI_ERR_TIMEOUT and the rows are left        */
+/*     unwritten), read all W states through the peer pointers and write     */
+/*     bf16 out [rows, D].                                                   */
+/* Both are stream-ordered and graph-capturable; W <= 16, D % 4 == 0.        */
+/* ------------------------------------------------------------------------ */
+int64_t kivi_peer_buffer_bytes(int rows, int D, int W);
+int kivi_peer_alloc(int64_t bytes, void **ptr, void *ipc_handle);   /* handle: 64 bytes out */
+int kivi_peer_open(const void *ipc_handle, void **ptr);
+int kivi_peer_close(void *ptr);                                      /* unmap a peer buffer  */
+int kivi_peer_free(void *ptr);                                       /* free own buffer      */
+int kivi_peer_publish(const float *m, const float *l, const float *acc, int rows, int D,
+                      void *my_buf, const uint64_t *peer_bufs, int W, int rank,
+                      unsigned int *epoch, kivi_stream_t stream);
+int kivi_peer_merge(const uint64_t *peer_bufs, int W, int rows, int D, const unsigned int *epoch,
+                    const void *my_buf, void *out, int *err, long long timeout_ns,
+                    kivi_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,7 +15,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libkivi_sm100.so")
-SOURCES = ["kivi_abi.cu", "kivi_quant.cu", "kivi_decode.cu", "kivi_paged.cu"]
+SOURCES = ["kivi_abi.cu", "kivi_quant.cu", "kivi_decode.cu", "kivi_paged.cu", "kivi_peer.cu"]
 HEADERS = ["kivi_common.cuh", "kivi_internal.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",

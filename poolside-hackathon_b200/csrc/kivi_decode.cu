@@ -63,7 +63,36 @@ struct DecodeParams {
     // optional bf16 V of the tail tokens [BH, hot_stride, D] (caches that keep
     // the partial page unquantised); nullptr = the tail's V comes from v_packed
     const __nv_bfloat16* v_hot;
+    // mode 2 (sequence-parallel exchange): this rank's exchange buffer, the
+    // device array of all ranks' buffers, per-row epoch counters
+    uint8_t* xbuf;
+    const uint64_t* peers;
+    int xW, xrank;                   // ranks in the exchange, this rank
+    unsigned int* row_epoch;
+    long long timeout_ns;
 };
+
+struct SeqPar {
+    uint8_t* xbuf; const uint64_t* peers; int W, rank; unsigned int* row_epoch; long long timeout_ns;
+};
+
+// Exchange buffer of the fused sequence-parallel combine (mode 2):
+//   flags uint32 [W][rows] (flag[j][row] = newest epoch rank j published for
+//   the row), padded to 256 B, then two slots of fp32 m [rows], l [rows],
+//   acc [rows][D]; epoch e of a row uses slot e & 1.
+__host__ __device__ inline int64_t xflag_bytes(int W, int rows) { return ((int64_t)W * rows * 4 + 255) / 256 * 256; }
+__host__ __device__ inline int64_t xslot_floats(int rows, int D) { return (int64_t)rows * (2 + D); }
+__device__ __forceinline__ float* xslot(uint8_t* base, int W, int rows, int D, unsigned int e) {
+    return reinterpret_cast<float*>(base + xflag_bytes(W, rows)) + (e & 1) * xslot_floats(rows, D);
+}
+__device__ __forceinline__ void st_release_sys_u32(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 
 __host__ __device__ inline int64_t tile_start(int64_t c, int64_t W, int N) { return c * W / N; }
 
@@ -727,6 +756,13 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     __syncthreads();
     Ls = (red[4] + red[5]) + (red[6] + red[7]);
     const int64_t row = (int64_t)b * p.Hq + kvh * G + h;
+    const int rows = p.B * p.Hq;
+    unsigned int e = 0;
+    float* xacc = nullptr;                               // mode 2: this row's acc in my slot
+    if (mode == 2) {
+        e = p.row_epoch[row] + 1;
+        xacc = xslot(p.xbuf, p.xW, rows, D, e) + 2 * rows + row * D;
+    }
     if (D == DH && ns >= 16) {
         // many slots (long single sequences): warps split the slots, each lane
         // owns 4 channels (float4 loads), then a shared-memory reduction
@@ -753,18 +789,62 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         float a = (sacc[d] + sacc[DH + d]) + (sacc[2 * DH + d] + sacc[3 * DH + d]);
         for (int j = 0; j < hot; ++j) a += w[ns + j] * tail_v<FMT>(p, bh, n_full, j, d, ND);
         if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
-        else acc_out[row * D + d] = a;
-        if (mode == 1 && threadIdx.x == 0) { m_out[row] = M; l_out[row] = Ls; }
-        return;
-    }
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        float a = 0.f;
-        for (int i = 0; i < ns; ++i) if (w[i] != 0.f) a += p.part_acc[slot(i) * D + d] * w[i];
-        for (int j = 0; j < hot; ++j) a += w[ns + j] * tail_v<FMT>(p, bh, n_full, j, d, ND);
-        if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
-        else acc_out[row * D + d] = a;
+        else if (mode == 1) acc_out[row * D + d] = a;
+        else xacc[d] = a;
+    } else {
+        for (int d = threadIdx.x; d < D; d += blockDim.x) {
+            float a = 0.f;
+            for (int i = 0; i < ns; ++i) if (w[i] != 0.f) a += p.part_acc[slot(i) * D + d] * w[i];
+            for (int j = 0; j < hot; ++j) a += w[ns + j] * tail_v<FMT>(p, bh, n_full, j, d, ND);
+            if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
+            else if (mode == 1) acc_out[row * D + d] = a;
+            else xacc[d] = a;
+        }
     }
     if (mode == 1 && threadIdx.x == 0) { m_out[row] = M; l_out[row] = Ls; }
+    if (mode != 2) return;
+    // ---- sequence-parallel exchange: publish this row, merge every rank's ----
+    float* mine = xslot(p.xbuf, p.xW, rows, D, e);
+    if (threadIdx.x == 0) { mine[row] = M; mine[rows + row] = Ls; }
+    __syncthreads();                                     // the row's state is written (CTA scope) ...
+    if (threadIdx.x < p.xW) {                            // ... and released system-wide to every rank
+        __threadfence_system();
+        st_release_sys_u32(reinterpret_cast<unsigned int*>(p.peers[threadIdx.x]) + (int64_t)p.xrank * rows + row, e);
+    }
+    __shared__ int x_ok;
+    __shared__ float x_w[16];
+    __shared__ float x_l;
+    if (threadIdx.x == 0) {
+        const unsigned int* flags = reinterpret_cast<const unsigned int*>(p.xbuf);
+        int ok = 1;
+        const uint64_t t0 = globaltimer_ns();
+        for (int j = 0; j < p.xW && ok; ++j)
+            while ((int)(ld_acquire_sys_u32(flags + (int64_t)j * rows + row) - e) < 0)
+                if ((long long)(globaltimer_ns() - t0) > p.timeout_ns) { ok = 0; set_err(p.err, KIVI_ERR_TIMEOUT); break; }
+        x_ok = ok;
+        if (ok) {
+            float Mx = -INFINITY;
+            for (int j = 0; j < p.xW; ++j)
+                Mx = fmaxf(Mx, xslot(reinterpret_cast<uint8_t*>(p.peers[j]), p.xW, rows, D, e)[row]);
+            const float Mxr = (Mx == -INFINITY) ? 0.f : Mx;
+            float Lx = 0.f;
+            for (int j = 0; j < p.xW; ++j) {
+                const float* sj = xslot(reinterpret_cast<uint8_t*>(p.peers[j]), p.xW, rows, D, e);
+                x_w[j] = exp2f(sj[row] - Mxr);
+                Lx += sj[rows + row] * x_w[j];
+            }
+            x_l = Lx;
+            p.row_epoch[row] = e;
+        }
+    }
+    __syncthreads();                                     // peers' rows acquired by thread 0
+    if (!x_ok) return;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float a = 0.f;
+        for (int j = 0; j < p.xW; ++j)
+            a += xslot(reinterpret_cast<uint8_t*>(p.peers[j]), p.xW, rows, D, e)[2 * rows + row * D + d] * x_w[j];
+        out[row * D + d] = __float2bfloat16_rn(x_l > 0.f ? a / x_l : 0.f);
+    }
 }
 
 // Merge R records [R, rows], [R, rows, D] -> bf16 [rows, D].
@@ -884,7 +964,8 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
                 const uint8_t* v_packed, const void* v_scale, int v_s_stride, int B, int Hq, int Hkv,
                 int S, int D, int fmt, float sm_scale, float g_k, float g_v, void* out, float* m_out,
                 float* l_out, float* acc_out, float* work, int64_t work_floats, int* err,
-                kivi_stream_t stream, const int* seq_lens = nullptr, const void* v_hot = nullptr) {
+                kivi_stream_t stream, const int* seq_lens = nullptr, const void* v_hot = nullptr,
+                const SeqPar* sp = nullptr) {
     if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || S < 0 || D <= 0 || D % BLK) return KIVI_ERR_ARG;
     if (fmt != FMT_INT4 && fmt != FMT_NVFP4) return KIVI_ERR_ARG;
     const int G = Hq / Hkv, BH = B * Hkv;
@@ -892,7 +973,10 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     const int v_tokens = v_hot ? n_full : S;          // tokens v_packed must cover
     if (k_np_stride < n_full / BLK || v_s_stride < v_tokens || (hot > 0 && hot_stride < hot)) return KIVI_ERR_ARG;
     if (hot > 0 && v_hot && !k_hot) return KIVI_ERR_ARG;
-    if (!q || (!out && mode == 0) || (mode == 1 && (!m_out || !l_out || !acc_out))) return KIVI_ERR_ARG;
+    if (!q || (!out && mode != 1) || (mode == 1 && (!m_out || !l_out || !acc_out))) return KIVI_ERR_ARG;
+    if (mode == 2 && (!sp || !sp->xbuf || !sp->peers || !sp->row_epoch || sp->W <= 0 || sp->W > 16 ||
+                      sp->rank < 0 || sp->rank >= sp->W || sp->timeout_ns <= 0))
+        return KIVI_ERR_ARG;
     if (n_full > 0 && (!k_packed || !k_scale)) return KIVI_ERR_ARG;
     if (v_tokens > 0 && (!v_packed || !v_scale)) return KIVI_ERR_ARG;
     if (hot > 0 && !k_hot) return KIVI_ERR_ARG;
@@ -925,6 +1009,10 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     p.err = err;
     p.seq_lens = seq_lens;
     p.v_hot = reinterpret_cast<const __nv_bfloat16*>(v_hot);
+    if (sp) {
+        p.xbuf = sp->xbuf; p.peers = sp->peers; p.xW = sp->W; p.xrank = sp->rank;
+        p.row_epoch = sp->row_epoch; p.timeout_ns = sp->timeout_ns;
+    }
     p.tile_off = seq_lens ? reinterpret_cast<int*>(work + pl.slots * G * (2 + (int64_t)D)) : nullptr;
     cudaStream_t st = (cudaStream_t)stream;
     if (seq_lens && pl.W > 0) {
@@ -1047,6 +1135,24 @@ extern "C" int kivi_decode_partial(const void* q, int64_t q_sb, int64_t q_sh, co
     return decode_impl(1, q, q_sb, q_sh, k_packed, k_scale, k_np_stride, k_hot, hot_stride, v_packed, v_scale,
                        v_s_stride, B, Hq, Hkv, S, D, fmt, sm_scale, g_k, g_v, nullptr, m_out, l_out, acc_out,
                        work, work_floats, err, stream);
+}
+
+extern "C" int64_t kivi_seqpar_buffer_bytes(int rows, int D, int W) {
+    if (rows <= 0 || D <= 0 || W <= 0 || W > 16) return 0;
+    return xflag_bytes(W, rows) + 2 * xslot_floats(rows, D) * (int64_t)sizeof(float);
+}
+
+extern "C" int kivi_decode_seqpar(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,
+                                  const void* k_scale, int k_np_stride, const void* k_hot, int hot_stride,
+                                  const uint8_t* v_packed, const void* v_scale, int v_s_stride, int B, int Hq,
+                                  int Hkv, int S, int D, int fmt, float sm_scale, float g_k, float g_v, void* xbuf,
+                                  const uint64_t* peer_bufs, int W, int rank, unsigned int* row_epoch,
+                                  long long timeout_ns, void* out, float* work, int64_t work_floats, int* err,
+                                  kivi_stream_t stream) {
+    SeqPar sp{static_cast<uint8_t*>(xbuf), peer_bufs, W, rank, row_epoch, timeout_ns};
+    return decode_impl(2, q, q_sb, q_sh, k_packed, k_scale, k_np_stride, k_hot, hot_stride, v_packed, v_scale,
+                       v_s_stride, B, Hq, Hkv, S, D, fmt, sm_scale, g_k, g_v, out, nullptr, nullptr, nullptr,
+                       work, work_floats, err, stream, nullptr, nullptr, &sp);
 }
 
 extern "C" int kivi_lse_merge(const float* m, const float* l, const float* acc, int R, int rows, int D,

@@ -61,6 +61,18 @@ def lib():
                                              F, P, P, I64, P, P]
             L.kivi_decode_bf16_tail.argtypes = [P, I64, I64, P, P, I, P, P, I, P, P, I, I, I, I, I, I, I, F, F, F,
                                                 P, P, I64, P, P]
+            L.kivi_seqpar_buffer_bytes.restype = I64
+            L.kivi_seqpar_buffer_bytes.argtypes = [I, I, I]
+            L.kivi_decode_seqpar.argtypes = [P, I64, I64, P, P, I, P, I, P, P, I, I, I, I, I, I, I, F, F, F,
+                                             P, P, I, I, P, ctypes.c_longlong, P, P, I64, P, P]
+            L.kivi_peer_buffer_bytes.restype = I64
+            L.kivi_peer_buffer_bytes.argtypes = [I, I, I]
+            L.kivi_peer_alloc.argtypes = [I64, ctypes.POINTER(P), P]
+            L.kivi_peer_open.argtypes = [P, ctypes.POINTER(P)]
+            L.kivi_peer_close.argtypes = [P]
+            L.kivi_peer_free.argtypes = [P]
+            L.kivi_peer_publish.argtypes = [P, P, P, I, I, P, P, I, I, P, P]
+            L.kivi_peer_merge.argtypes = [P, I, I, I, P, P, P, P, ctypes.c_longlong, P]
             L.kivi_paged_full_dim.restype = I
             L.kivi_paged_full_dim.argtypes = [I]
             L.kivi_paged_store.argtypes = [P, P, I, I64, I64, I64, I64, I64, I64, I, I, I, I, I, P, P, I64, P, P]

@@ -43,7 +43,8 @@ def _stacked_geometry(st: dict) -> tuple[int, int, dict]:
 
 def decode_packed(q: Tensor, st: dict, n_qh: int, sm_scale: Optional[float] = None,
                   fmt: Optional[str] = None, g_k: Optional[float] = None, g_v: Optional[float] = None,
-                  out: Optional[Tensor] = None, partial: bool = False, v_hot: Optional[Tensor] = None):
+                  out: Optional[Tensor] = None, partial: bool = False, v_hot: Optional[Tensor] = None,
+                  exchange=None):
     """Core entry: q [B, n_qh, D] bf16 over a stacked packed cache (B*H heads).
 
     Returns bf16 [B, n_qh, D], or with partial=True the merged per-row state
@@ -91,6 +92,16 @@ def decode_packed(q: Tensor, st: dict, n_qh: int, sm_scale: Optional[float] = No
         return m, l, acc
     if out is None:
         out = torch.empty((B, n_qh, D), dtype=torch.bfloat16, device=dev)
+    if exchange is not None:
+        assert not partial and v_hot is None and st.get("seq_lens") is None
+        x = exchange
+        rc = L.kivi_decode_seqpar(
+            N.ptr(q), q.stride(0), q.stride(1), N.ptr(st["k_packed"]), N.ptr(st["k_scale"]), nps,
+            N.ptr(khot) if hot_stride else None, hot_stride, N.ptr(st["v_packed"]), N.ptr(st["v_scale"]), ss,
+            B, n_qh, H, S, D, N.FMT[fmt], sm_scale, g_k, g_v, x.own, N.ptr(x.peers), x.world, x.rank,
+            N.ptr(x.row_epoch), x.timeout_ns, N.ptr(out), N.ptr(work), work.numel(), N.ptr(err), N.stream_of(q))
+        N.check(rc, "kivi_decode_seqpar")
+        return out
     if v_hot is not None and hot_stride:
         assert not partial and st.get("seq_lens") is None, "v_hot is for plain (non-partial, uniform) decode"
         vh = v_hot.to(torch.bfloat16)

@@ -5,12 +5,15 @@ Two regimes (the reference is single-GPU; these are B200-native additions):
     (`shard_sequences` balances sequences by token count);
   * sequence parallel for one long context (>= 128K tokens): the KV sequence
     is split in page-aligned contiguous ranges (`split_tokens`), each rank
-    decodes its range to a partial softmax state (m, l, acc), the states are
-    all-gathered (16.6 KB per rank at 32 heads x 128) and merged locally with
-    the log-sum-exp kernel (`seq_parallel_decode`).
+    decodes its range to a partial softmax state (m, l, acc), and the states
+    (16.6 KB per rank at 32 heads x 128) are merged with log-sum-exp on every
+    rank (`seq_parallel_decode`): either read directly from the peers' memory
+    over NVLink (`PeerMerge`: CUDA IPC buffers + kivi_peer_publish /
+    kivi_peer_merge) or all-gathered with NCCL and merged locally.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Optional, Sequence
 
 import torch
@@ -51,17 +54,121 @@ def merge_partials_torch(m: torch.Tensor, l: torch.Tensor, acc: torch.Tensor) ->
     return (acc * w[..., None]).sum(0) / (l * w).sum(0)[..., None]
 
 
+class _PeerBuffers:
+    """One exchange buffer per rank, allocated by the library (cudaMalloc,
+    zeroed) and mapped into every other rank with CUDA IPC handles that are
+    all-gathered over the host: plain peer mappings, no NVLink multicast
+    objects.  `peers` is the device array of all ranks' buffer addresses."""
+
+    def __init__(self, nbytes: int, device, group=None, timeout_s: float = 2.0):
+        import torch.distributed as dist
+        from . import _native as N
+        self.N = N
+        self.group = group or dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.device = torch.device(device)
+        if nbytes <= 0:
+            raise ValueError(f"unsupported exchange shape for world={self.world}")
+        L = N.lib()
+        with torch.cuda.device(self.device):
+            self.own = ctypes.c_void_p()
+            handle = (ctypes.c_char * 64)()
+            N.check(L.kivi_peer_alloc(nbytes, ctypes.byref(self.own), handle), "kivi_peer_alloc")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=self.group)
+            self.opened = []
+            ptrs = []
+            for j, hj in enumerate(handles):
+                if j == self.rank:
+                    ptrs.append(self.own.value)
+                    continue
+                pj = ctypes.c_void_p()
+                N.check(L.kivi_peer_open((ctypes.c_char * 64).from_buffer_copy(hj), ctypes.byref(pj)),
+                        "kivi_peer_open")
+                self.opened.append(pj)
+                ptrs.append(pj.value)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        self.timeout_ns = int(timeout_s * 1e9)
+        dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after a barrier, so
+        no peer still reads it)."""
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        L = self.N.lib()
+        with torch.cuda.device(self.device):
+            for pj in self.opened:
+                L.kivi_peer_close(pj)
+            self.opened = []
+            if self.own:
+                L.kivi_peer_free(self.own)
+                self.own = ctypes.c_void_p()
+
+
+class PeerMerge(_PeerBuffers):
+    """Merge of per-rank partial decode states (m, l, acc) through NVLink
+    peer memory: kivi_peer_publish + kivi_peer_merge, two stream-ordered,
+    graph-capturable launches after the partial decode."""
+
+    def __init__(self, rows: int, D: int, device, group=None, timeout_s: float = 2.0):
+        import torch.distributed as dist
+        from . import _native as N
+        world = dist.get_world_size(group or dist.group.WORLD)
+        super().__init__(N.lib().kivi_peer_buffer_bytes(rows, D, world), device, group, timeout_s)
+        self.rows, self.D = rows, D
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.out = torch.empty(rows, D, dtype=torch.bfloat16, device=self.device)
+
+    def __call__(self, m: torch.Tensor, l: torch.Tensor, acc: torch.Tensor) -> torch.Tensor:
+        N, L = self.N, self.N.lib()
+        stream = N.stream_of(acc)
+        N.check(L.kivi_peer_publish(N.ptr(m), N.ptr(l), N.ptr(acc), self.rows, self.D, self.own,
+                                    N.ptr(self.peers), self.world, self.rank, N.ptr(self.epoch), stream),
+                "kivi_peer_publish")
+        N.check(L.kivi_peer_merge(N.ptr(self.peers), self.world, self.rows, self.D, N.ptr(self.epoch),
+                                  self.own, N.ptr(self.out), N.ptr(N.err_flag(acc.device)), self.timeout_ns,
+                                  stream),
+                "kivi_peer_merge")
+        return self.out
+
+
+class SeqParallelExchange(_PeerBuffers):
+    """State of the fused sequence-parallel decode (kivi_decode_seqpar): the
+    decode's own combine kernel publishes each output row's rank-local state
+    and merges all ranks' states of that row from their memory, so a step is
+    the split-K kernel plus one combine launch on every rank."""
+
+    def __init__(self, rows: int, D: int, device, group=None, timeout_s: float = 2.0):
+        import torch.distributed as dist
+        from . import _native as N
+        world = dist.get_world_size(group or dist.group.WORLD)
+        super().__init__(N.lib().kivi_seqpar_buffer_bytes(rows, D, world), device, group, timeout_s)
+        self.rows, self.D = rows, D
+        self.row_epoch = torch.zeros(rows, dtype=torch.int32, device=self.device)
+
+
 def seq_parallel_decode(q: torch.Tensor, stacked_shard: dict, n_qh: int, sm_scale: Optional[float] = None,
-                        group=None, fmt: str = "int4") -> torch.Tensor:
-    """Decode q [B, n_qh, D] over this rank's KV shard, all-gather the partial
-    states over `group` (NCCL) and merge them; every rank returns the bf16
-    output [B, n_qh, D]."""
+                        group=None, fmt: str = "int4", merger=None) -> torch.Tensor:
+    """Decode q [B, n_qh, D] over this rank's KV shard and merge the partial
+    states of all ranks; every rank returns the bf16 output [B, n_qh, D].
+    `merger`: a SeqParallelExchange (merge fused into the decode's combine
+    kernel over NVLink peer memory), a PeerMerge (partial decode, then
+    publish + merge over peer memory), or None (NCCL all-gather over `group`
+    and a local merge)."""
     import torch.distributed as dist
 
     from .decode import decode_packed, lse_merge
-    world = dist.get_world_size(group)
+    if isinstance(merger, SeqParallelExchange):
+        return decode_packed(q, stacked_shard, n_qh, sm_scale, fmt=fmt, g_k=stacked_shard.get("g_k", 1.0),
+                             g_v=stacked_shard.get("g_v", 1.0), exchange=merger)
     m, l, acc = decode_packed(q, stacked_shard, n_qh, sm_scale, fmt=fmt,
                               g_k=stacked_shard.get("g_k", 1.0), g_v=stacked_shard.get("g_v", 1.0), partial=True)
+    if merger is not None:
+        return merger(m, l, acc).reshape(q.shape)
+    world = dist.get_world_size(group)
     rows, D = acc.shape
     packed = torch.cat([m[:, None], l[:, None], acc], dim=1)           # [rows, D + 2]
     gathered = torch.empty((world,) + tuple(packed.shape), dtype=packed.dtype, device=packed.device)

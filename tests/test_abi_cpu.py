@@ -92,3 +92,13 @@ def test_paged_python_api_surface():
                  "int4_kivi_kv_cache_full_dim"):
         assert callable(getattr(paged, name))
     assert paged.BLOCK == 16 and paged.QMAX == 7 and paged.int4_kivi_kv_cache_full_dim(128) == 72
+
+
+def test_peer_merge_argument_errors():
+    from int4_kivi import _native as N
+    L = N.lib()
+    assert L.kivi_peer_buffer_bytes(32, 128, 2) == 256 + 2 * 32 * 130 * 4
+    assert L.kivi_peer_buffer_bytes(32, 128, 17) == 0          # at most 16 ranks
+    assert L.kivi_peer_publish(None, None, None, 32, 128, None, None, 2, 0, None, None) == 1
+    assert L.kivi_peer_publish(None, None, None, 32, 128, None, None, 2, 2, None, None) == 1   # rank >= W
+    assert L.kivi_peer_merge(None, 2, 32, 128, None, None, None, None, 0, None) == 1
