@@ -307,12 +307,14 @@ __global__ void __launch_bounds__(128) gather_kernel(const GatherP p) {
 // ---------------------------------------------------------------------------
 // Fused paged decode.
 //
-// Work = flattened (sequence, TP-page tile) list split evenly over a
-// persistent grid.  A CTA has one consumer warp per KV head plus a producer
-// warp; the producer copies whole blocks (K and V of a block are one
-// contiguous 2 * 16 * H * FD byte range) with cp.async.bulk into a ring of
-// stages guarded by mbarriers, so every byte of the cache is read once and in
-// full rows.  Consumer warp h runs, per 16-token block:
+// Work = flattened (sequence, TP-block tile) list split evenly over a
+// persistent grid of one CTA per SM.  A CTA has one consumer warp per KV head
+// plus a producer warp; the producer moves whole blocks (K and V of a block
+// are one contiguous 2 * 16 * H * FD byte range) into a ring of stages guarded
+// by mbarriers, one TMA tensor load per block whose box rows are wider than
+// the cache row, so token rows land at a bank-spreading smem pitch and every
+// byte of the cache is read once, in full rows.  Consumer warp h runs, per
+// 16-token block (TP blocks of a stage interleaved):
 //   QK^T  m16n8k16 with the block's 16 tokens as M, the GQA heads as N; the
 //         A fragments come from 64-bit shared loads of the token rows, the
 //         channel order inside each k-step is permuted to match the nibble
