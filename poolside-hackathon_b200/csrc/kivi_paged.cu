@@ -445,6 +445,23 @@ __device__ __forceinline__ void nib4(uint32_t w, uint32_t (&r)[4]) {
 
 // NW = warps the launch may use (KV heads + the producer warp); it sets the
 // register budget.
+// QK A-operand words.  INT4 needs the magic's (n, n+4) nibble pairing; the
+// e2m1 cvt yields adjacent pairs (c0,c1) (c2,c3) (c4,c5) (c6,c7) directly,
+// and NVFP4 keeps that order (Q and the per-channel scales follow it).
+template <int FMT>
+__device__ __forceinline__ void nib4_qk(uint32_t w, uint32_t (&r)[4]) {
+    if (FMT == FMT_NVFP4) e2m1x8_to_h2x4(w, r[0], r[1], r[2], r[3]);
+    else nib4<FMT>(w, r);
+}
+// NVFP4 PV words: (token A, token B) e2m1 pairs built with one shift and one
+// bit-select per word: even channels 0,2,4,6 -> E[0..3], odd 1,3,5,7 -> O[0..3].
+__device__ __forceinline__ void e2m1_token_pairs(uint32_t wa, uint32_t wb, uint32_t (&E)[4], uint32_t (&O)[4]) {
+    const uint32_t even = (wa & 0x0F0F0F0Fu) | ((wb << 4) & 0xF0F0F0F0u);
+    const uint32_t odd = ((wa >> 4) & 0x0F0F0F0Fu) | (wb & 0xF0F0F0F0u);
+    e2m1x8_to_h2x4(even, E[0], E[1], E[2], E[3]);
+    e2m1x8_to_h2x4(odd, O[0], O[1], O[2], O[3]);
+}
+
 template <int FMT, int NW>
 __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const __grid_constant__ CUtensorMap tm_kv,
                                                                   const DecP p) {
@@ -531,10 +548,19 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const __grid_c
             if (n >= G) continue;
             if (g == 0) { p.part_m[rec + n] = hh ? m1 : m0; p.part_l[rec + n] = hh ? L1 : L0; }
             float* a = p.part_acc + (rec + n) * DD + 16 * g;
-            *reinterpret_cast<float4*>(a) = make_float4(acc[0][hh], acc[1][hh], acc[2][hh], acc[3][hh]);
-            *reinterpret_cast<float4*>(a + 4) = make_float4(acc[4][hh], acc[5][hh], acc[6][hh], acc[7][hh]);
-            *reinterpret_cast<float4*>(a + 8) = make_float4(acc[0][2 + hh], acc[1][2 + hh], acc[2][2 + hh], acc[3][2 + hh]);
-            *reinterpret_cast<float4*>(a + 12) = make_float4(acc[4][2 + hh], acc[5][2 + hh], acc[6][2 + hh], acc[7][2 + hh]);
+            if (FMT == FMT_NVFP4) {   // m-tile e holds channel 16g + {0,2,4,6,1,3,5,7}[e] (+8 for rows g+8)
+#pragma unroll
+                for (int r8 = 0; r8 < 2; ++r8) {
+                    const int c = 2 * r8 + hh;
+                    *reinterpret_cast<float4*>(a + 8 * r8) = make_float4(acc[0][c], acc[4][c], acc[1][c], acc[5][c]);
+                    *reinterpret_cast<float4*>(a + 8 * r8 + 4) = make_float4(acc[2][c], acc[6][c], acc[3][c], acc[7][c]);
+                }
+            } else {                  // m-tile e holds channel 16g + e (+8 for rows g+8)
+                *reinterpret_cast<float4*>(a) = make_float4(acc[0][hh], acc[1][hh], acc[2][hh], acc[3][hh]);
+                *reinterpret_cast<float4*>(a + 4) = make_float4(acc[4][hh], acc[5][hh], acc[6][hh], acc[7][hh]);
+                *reinterpret_cast<float4*>(a + 8) = make_float4(acc[0][2 + hh], acc[1][2 + hh], acc[2][2 + hh], acc[3][2 + hh]);
+                *reinterpret_cast<float4*>(a + 12) = make_float4(acc[4][2 + hh], acc[5][2 + hh], acc[6][2 + hh], acc[7][2 + hh]);
+            }
         }
     };
 
@@ -557,11 +583,15 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const __grid_c
             for (int cc = 0; cc < 2; ++cc)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const int ch = 64 * cc + 16 * tq + 8 * (e >> 1) + 2 * (e & 1);
+                    // k-slots (2tq, 2tq+1 | 2tq+8, 2tq+9) <-> channels (ch, ch+4 | ch+1, ch+5)
+                    // for INT4, (ch, ch+1 | ch+2, ch+3) for NVFP4 (nib4_qk's order)
+                    constexpr bool NV = FMT == FMT_NVFP4;
+                    const int ch = 64 * cc + 16 * tq + 8 * (e >> 1) + (NV ? 4 : 2) * (e & 1);
                     uint32_t b0 = 0, b1 = 0;
                     if (g < G) {
-                        b0 = h2_as_u32(__floats2half2_rn(__bfloat162float(qp[ch]), __bfloat162float(qp[ch + 4])));
-                        b1 = h2_as_u32(__floats2half2_rn(__bfloat162float(qp[ch + 1]), __bfloat162float(qp[ch + 5])));
+                        b0 = h2_as_u32(__floats2half2_rn(__bfloat162float(qp[ch]), __bfloat162float(qp[ch + (NV ? 1 : 4)])));
+                        b1 = h2_as_u32(__floats2half2_rn(__bfloat162float(qp[ch + (NV ? 2 : 1)]),
+                                                         __bfloat162float(qp[ch + (NV ? 3 : 5)])));
                     }
                     qf[cc][e][0] = b0; qf[cc][e][1] = b1;
                 }
@@ -594,13 +624,16 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const __grid_c
                     const uint2 ra = lds64s(kpg + g * rowp + 32 * cc + 8 * tq);
                     const uint2 rb = lds64s(kpg + (g + 8) * rowp + 32 * cc + 8 * tq);
                     uint32_t A0[4], A1[4], B0[4], B1[4];
-                    nib4<FMT>(ra.x, A0); nib4<FMT>(ra.y, A1); nib4<FMT>(rb.x, B0); nib4<FMT>(rb.y, B1);
+                    nib4_qk<FMT>(ra.x, A0); nib4_qk<FMT>(ra.y, A1); nib4_qk<FMT>(rb.x, B0); nib4_qk<FMT>(rb.y, B1);
                     uint32_t S[8], T0 = 0, T1 = 0;
                     if (full) {
 #pragma unroll
                         for (int sw = 0; sw < 2; ++sw) {
                             const uint2 sr = lds64s(kpg + (8 * cc + 2 * tq + sw) * rowp + DD / 2);
-                            const uint32_t x = __byte_perm(sr.x, sr.y, 0x5140), y = __byte_perm(sr.x, sr.y, 0x7362);
+                            // scale pairs in the A words' channel order: (s0,s4) (s1,s5) (s2,s6)
+                            // (s3,s7) for INT4, (s0,s1) (s2,s3) (s4,s5) (s6,s7) for NVFP4
+                            const uint32_t x = FMT == FMT_NVFP4 ? sr.x : __byte_perm(sr.x, sr.y, 0x5140);
+                            const uint32_t y = FMT == FMT_NVFP4 ? sr.y : __byte_perm(sr.x, sr.y, 0x7362);
                             S[4 * sw + 0] = e4m3x2_to_h2((uint16_t)x);
                             S[4 * sw + 1] = e4m3x2_to_h2((uint16_t)(x >> 16));
                             S[4 * sw + 2] = e4m3x2_to_h2((uint16_t)y);
@@ -694,18 +727,25 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const __grid_c
                 }
                 const uint32_t sAB = e4m3_pair(sA, sB), sCD = e4m3_pair(sC, sD);
                 uint32_t X0[4], Y0[4], X1[4], Y1[4], U0[4], V0[4], U1[4], V1[4];
-                nib4<FMT>(__byte_perm(wa.x, wb.x, 0x5410), X0);   // ch 16g+0..3, tokens (tA, tB)
-                nib4<FMT>(__byte_perm(wa.x, wb.x, 0x7632), Y0);   // ch 16g+4..7
-                nib4<FMT>(__byte_perm(wa.y, wb.y, 0x5410), X1);   // ch 16g+8..11
-                nib4<FMT>(__byte_perm(wa.y, wb.y, 0x7632), Y1);   // ch 16g+12..15
-                nib4<FMT>(__byte_perm(wc.x, wd.x, 0x5410), U0);   // same channels, tokens (tC, tD)
-                nib4<FMT>(__byte_perm(wc.x, wd.x, 0x7632), V0);
-                nib4<FMT>(__byte_perm(wc.y, wd.y, 0x5410), U1);
-                nib4<FMT>(__byte_perm(wc.y, wd.y, 0x7632), V1);
+                if (FMT == FMT_NVFP4) {       // X/U: channels 16g+{0,2,4,6}, Y/V: 16g+{1,3,5,7} (+8 in X1..V1)
+                    e2m1_token_pairs(wa.x, wb.x, X0, Y0);
+                    e2m1_token_pairs(wa.y, wb.y, X1, Y1);
+                    e2m1_token_pairs(wc.x, wd.x, U0, V0);
+                    e2m1_token_pairs(wc.y, wd.y, U1, V1);
+                } else {
+                    nib4<FMT>(__byte_perm(wa.x, wb.x, 0x5410), X0);   // ch 16g+0..3, tokens (tA, tB)
+                    nib4<FMT>(__byte_perm(wa.x, wb.x, 0x7632), Y0);   // ch 16g+4..7
+                    nib4<FMT>(__byte_perm(wa.y, wb.y, 0x5410), X1);   // ch 16g+8..11
+                    nib4<FMT>(__byte_perm(wa.y, wb.y, 0x7632), Y1);   // ch 16g+12..15
+                    nib4<FMT>(__byte_perm(wc.x, wd.x, 0x5410), U0);   // same channels, tokens (tC, tD)
+                    nib4<FMT>(__byte_perm(wc.x, wd.x, 0x7632), V0);
+                    nib4<FMT>(__byte_perm(wc.y, wd.y, 0x5410), U1);
+                    nib4<FMT>(__byte_perm(wc.y, wd.y, 0x7632), V1);
+                }
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    const uint32_t a0 = hmul2u(e < 4 ? X0[e & 3] : Y0[e & 3], sAB);   // row g:   ch 16g+e
-                    const uint32_t a1 = hmul2u(e < 4 ? X1[e & 3] : Y1[e & 3], sAB);   // row g+8: ch 16g+8+e
+                    const uint32_t a0 = hmul2u(e < 4 ? X0[e & 3] : Y0[e & 3], sAB);   // row g
+                    const uint32_t a1 = hmul2u(e < 4 ? X1[e & 3] : Y1[e & 3], sAB);   // row g+8
                     const uint32_t a2 = hmul2u(e < 4 ? U0[e & 3] : V0[e & 3], sCD);
                     const uint32_t a3 = hmul2u(e < 4 ? U1[e & 3] : V1[e & 3], sCD);
                     mma_f16(acc[e], a0, a1, a2, a3, b0, b1);
