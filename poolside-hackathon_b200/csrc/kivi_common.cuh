@@ -221,10 +221,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_
         " [%0], [%1, {%3, %4, %5}], [%2];"
         :: "r"(smem_u32(dst)), "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z) : "memory");
 }
-__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
-                 :: "l"(tmap), "r"(x), "r"(y) : "memory");
-}
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
 }
@@ -232,10 +228,6 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
 __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
-                 : "=r"(r0), "=r"(r1) : "r"(addr));
 }
 
 // D = A(16x16 f16, row) * B(16x8 f16, col) + D, fp32 accumulate.

@@ -85,23 +85,6 @@ __device__ __forceinline__ float sq_err(const float x[BLK], float s, int fmt) {
     return sum16(e);
 }
 
-// Pick the e4m3 scale byte of one 16-value block.
-__device__ __forceinline__ uint8_t calib_e4m3(const float x[BLK], int fmt, int calib) {
-    const float qmax = qmax_of(fmt);
-    const float amax = absmax16(x);
-    uint8_t best = f32_to_e4m3(__fdiv_rn(amax, qmax));
-    if (calib == CAL_ABSMAX) return best;
-    float best_err = 1e38f;
-#pragma unroll 1
-    for (int i = 0; i < 16; ++i) {
-        const float a = __double2float_rn(0.5 + i * (0.5 / 15.0));
-        const uint8_t sc = f32_to_e4m3(__fdiv_rn(__fmul_rn(a, amax), qmax));
-        const float err = sq_err(x, e4m3_to_f32(sc), fmt);
-        if (err < best_err) { best_err = err; best = sc; }
-    }
-    return best;
-}
-
 __device__ __forceinline__ uint32_t nibble_of(float x, float s, int fmt) {
     if (s == 0.0f) return 0u;
     const float y = __fdiv_rn(x, s);
@@ -416,8 +399,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
         :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
-// (32-bit shared-window addresses keep the consumer's many smem pointers in one register each)
 __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
     return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
 }
