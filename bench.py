@@ -420,6 +420,7 @@ def serving_main(args, rank: int, world: int, local: int) -> None:
     import torch.distributed as dist
     from int4_kivi import store_kivi
     from int4_kivi.decode import decode_packed
+    from int4_kivi import paged
     from int4_kivi.distributed import shard_sequences
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -444,10 +445,29 @@ def serving_main(args, rank: int, world: int, local: int) -> None:
         Bl = max(len(mine_lens), 1)
         lens = mine_lens or [16]
         S_max = max(lens)
-        per_layer = Bl * HKV * S_max * BYTES_PER_TOKEN_HEAD
+        paged_layout = args.layout == "paged"
+        per_layer = (sum(lens) * HKV * 144) if paged_layout else Bl * HKV * S_max * BYTES_PER_TOKEN_HEAD
         n_caches = L_ if per_layer * L_ <= 40e9 else 1
         caches = []
-        for li in range(n_caches):
+        for li in range(n_caches if paged_layout else 0):
+            # vLLM block layout: exactly ceil(L/16) blocks per sequence behind a block table
+            g = torch.Generator(device=dev).manual_seed(1000 * Bg + li)
+            nbl = [(Lb + 15) // 16 for Lb in lens]
+            bt = torch.zeros(Bl, max(nbl), dtype=torch.int32)
+            cur = 1
+            for b, nb_ in enumerate(nbl):
+                bt[b, :nb_] = torch.arange(cur, cur + nb_, dtype=torch.int32)
+                cur += nb_
+            bt = bt.to(dev)
+            kv = torch.zeros(cur, 2, 16, HKV, paged.int4_kivi_kv_cache_full_dim(D), dtype=torch.uint8, device=dev)
+            ar = torch.arange(16, device=dev)
+            for b, Lb in enumerate(lens):
+                kk = torch.randn(Lb, HKV, D, device=dev, generator=g).bfloat16()
+                vv = torch.randn(Lb, HKV, D, device=dev, generator=g).bfloat16()
+                slots = (bt[b, :nbl[b]].long()[:, None] * 16 + ar[None]).reshape(-1)[:Lb]
+                paged.int4_kivi_store(kk, vv, kv, slots, D)
+            caches.append(dict(kv=kv, bt=bt, sl=torch.tensor(lens, dtype=torch.int32, device=dev)))
+        for li in range(0 if paged_layout else n_caches):
             g = torch.Generator(device=dev).manual_seed(1000 * Bg + li)
             k = torch.randn(Bl * HKV, S_max, D, device=dev, generator=g).bfloat16()
             v = torch.randn(Bl * HKV, S_max, D, device=dev, generator=g).bfloat16()
@@ -472,7 +492,11 @@ def serving_main(args, rank: int, world: int, local: int) -> None:
                 hsd = torch.nn.functional.rms_norm(x, (Hd,))
                 qkv = hsd @ Lw["qkv"]
                 q = qkv[:, :HQ * D].reshape(Bl, HQ, D)
-                decode_packed(q, caches[li % n_caches], HQ, out=att_out)
+                if paged_layout:
+                    c_ = caches[li % n_caches]
+                    paged.int4_kivi_paged_decode(q, c_["kv"], c_["bt"], c_["sl"], out=att_out)
+                else:
+                    decode_packed(q, caches[li % n_caches], HQ, out=att_out)
                 x = x + att_out.reshape(Bl, HQ * D) @ Lw["o"]
                 gu = torch.nn.functional.rms_norm(x, (Hd,)) @ Lw["gu"]
                 x = x + (torch.nn.functional.silu(gu[:, :F_]) * gu[:, F_:]) @ Lw["dn"]
@@ -483,7 +507,7 @@ def serving_main(args, rank: int, world: int, local: int) -> None:
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
-        kv_bytes = sum(lens_all) * HKV * BYTES_PER_TOKEN_HEAD * L_
+        kv_bytes = sum(lens_all) * HKV * (144 if paged_layout else BYTES_PER_TOKEN_HEAD) * L_
         results[Bg] = {"ms_per_step": round(ms, 3), "tok_s": round(Bg / ms * 1e3, 1),
                        "kv_GB_s": round(kv_bytes / ms / 1e6, 1), "caches_per_gpu": n_caches}
         del gr, caches
@@ -494,6 +518,8 @@ def serving_main(args, rank: int, world: int, local: int) -> None:
                 "warmup": 3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "bf16 GEMMs, int4 KV", "data": "synthetic (random-init weights, seeded lengths U[1K,32K])",
                 "config": {"workload": "c3 serving sweep", "hidden": Hd, "ffn": F_, "layers": L_,
+                           "kv_layout": ("paged vLLM blocks, e4m3 scales (144 B/token/head)" if args.layout == "paged"
+                                         else "contiguous KIVI, fp16 scales (160 B/token/head)"),
                            "parallelism": f"sequence-shard x{world}"},
                 "sweep": results}
         print(json.dumps(line), flush=True)
@@ -578,6 +604,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq", type=int, default=65536)
     ap.add_argument("--fmt", default="int4", choices=["int4", "nvfp4"], help="paged workload format")
+    ap.add_argument("--layout", default="contiguous", choices=["contiguous", "paged"],
+                    help="serving: KV cache layout (paged = the vLLM block layout of config 3)")
     ap.add_argument("--merge", default="fused", choices=["fused", "p2p", "nccl"],
                     help="longctx: merge the partial states inside the decode's combine kernel over NVLink "
                          "peer memory, with separate publish/merge launches over peer memory, or by NCCL")
