@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(128) gather_kernel(const GatherP p) {
 constexpr int DD = 128;               // head_dim of the fast path
 constexpr int FDD = 72;               // row bytes per head at D = 128
 #ifndef KIVI_PG_TP
-#define KIVI_PG_TP 4
+#define KIVI_PG_TP 5
 #endif
 #ifndef KIVI_PG_NST
 #define KIVI_PG_NST 6
