@@ -190,3 +190,37 @@ def test_paged_oracle_block_completion_across_calls():
     sc = oracle.paged_calib(np.ascontiguousarray(src.T), "int4", "mse")
     s = np.array([oracle.lib().orc_e4m3_to_f32(int(x)) for x in sc], np.float32)
     assert np.array_equal(kd16[0, 0], np.clip(np.rint(src / s[None]), -7, 7) * s[None])
+
+
+def test_paged_oracle_store_call_boundaries():
+    """Chunked stores: chunks that end on block boundaries give the same bytes
+    as one call; a chunk ending mid-block leaves that block per-token until a
+    later call completes it (then it is requantised per channel from the
+    dequantised rows, so the bytes differ from a one-call store); padding
+    slots (-1) are skipped; an out-of-range slot is reported, the rest stored."""
+    H, D, L = 2, 64, 48
+    rng = np.random.default_rng(7)
+    k = rng.standard_normal((L, H, D)).astype(np.float32)
+    v = rng.standard_normal((L, H, D)).astype(np.float32)
+    slots = np.arange(16, 16 + L, dtype=np.int64)
+    shape = (5, 2, 16, H, oracle.paged_full_dim(D))
+    one = np.zeros(shape, np.uint8)
+    oracle.paged_store(k, v, slots, one)
+    aligned = np.zeros(shape, np.uint8)
+    for a, b in ((0, 16), (16, 48)):
+        oracle.paged_store(k[a:b], v[a:b], slots[a:b], aligned)
+    assert np.array_equal(one, aligned)
+    ragged = np.zeros(shape, np.uint8)
+    for a, b in ((0, 20), (20, 48)):
+        oracle.paged_store(k[a:b], v[a:b], slots[a:b], ragged)
+    assert np.array_equal(one[1], ragged[1])                  # block 1 complete within the first call
+    assert not np.array_equal(one[2, 0], ragged[2, 0])        # block 2's K was requantised on completion
+    assert np.array_equal(one[2, 1], ragged[2, 1])            # V is per token either way
+    padded = np.zeros(shape, np.uint8)
+    sl = slots.copy(); sl[5] = -1
+    oracle.paged_store(k, v, sl, padded)
+    assert not padded[1, 1, 5].any()                          # the padding token's V row is untouched
+    bad = np.zeros(shape, np.uint8)
+    sl = slots.copy(); sl[-1] = 10 ** 6
+    assert oracle.paged_store(k, v, sl, bad) == 1
+    assert np.array_equal(bad[1], one[1])
