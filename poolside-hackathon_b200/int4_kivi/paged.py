@@ -43,6 +43,12 @@ def int4_kivi_kv_cache_full_dim(head_size: int) -> int:
 nvfp4_kivi_kv_cache_full_dim = int4_kivi_kv_cache_full_dim
 
 
+def _same_device(*ts) -> None:
+    devs = {t.device for t in ts if t is not None}
+    if len(devs) > 1:
+        raise ValueError(f"tensors are on different devices: {sorted(map(str, devs))}")
+
+
 def _check_cache(kv_cache: torch.Tensor, head_size: int) -> int:
     if kv_cache.dtype != torch.uint8 or kv_cache.dim() != 5 or kv_cache.shape[1] != 2 or kv_cache.shape[2] != PAGE:
         raise ValueError("kv_cache must be uint8 [num_blocks, 2, 16, H, D/2 + D/16]")
@@ -55,6 +61,9 @@ def _check_cache(kv_cache: torch.Tensor, head_size: int) -> int:
 
 def _store(fmt: str, key, value, kv_cache, slot_mapping, head_size, calib):
     N.require_cuda(key, value, kv_cache, slot_mapping)
+    _same_device(key, value, kv_cache, slot_mapping)
+    if calib not in N.CALIB:
+        raise ValueError(f"unknown calib {calib!r} (expected one of {sorted(N.CALIB)})")
     H = _check_cache(kv_cache, head_size)
     if key.dim() != 3 or key.shape != value.shape or key.shape[1] != H or key.shape[2] != head_size:
         raise ValueError("key/value must be [num_tokens, num_kv_heads, head_size]")
@@ -78,6 +87,7 @@ def _store(fmt: str, key, value, kv_cache, slot_mapping, head_size, calib):
 
 def _gather(fmt, kv_cache, block_table, seq_lens, head_size, num_kv_heads, max_seq):
     N.require_cuda(kv_cache, block_table, seq_lens)
+    _same_device(kv_cache, block_table, seq_lens)
     H = _check_cache(kv_cache, head_size)
     if H != num_kv_heads:
         raise ValueError(f"num_kv_heads {num_kv_heads} != cache heads {H}")
@@ -96,6 +106,7 @@ def _gather(fmt, kv_cache, block_table, seq_lens, head_size, num_kv_heads, max_s
 
 def _decode(fmt, q, kv_cache, block_table, seq_lens, sm_scale, out=None):
     N.require_cuda(q, kv_cache, block_table, seq_lens)
+    _same_device(q, kv_cache, block_table, seq_lens, out)
     if q.dim() != 3 or q.dtype != torch.bfloat16 or q.stride(2) != 1:
         raise ValueError("q must be bf16 [B, num_q_heads, head_size] with a contiguous last dim")
     B, Hq, D = q.shape

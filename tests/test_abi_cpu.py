@@ -102,3 +102,16 @@ def test_peer_merge_argument_errors():
     assert L.kivi_peer_publish(None, None, None, 32, 128, None, None, 2, 0, None, None) == 1
     assert L.kivi_peer_publish(None, None, None, 32, 128, None, None, 2, 2, None, None) == 1   # rank >= W
     assert L.kivi_peer_merge(None, 2, 32, 128, None, None, None, None, 0, None) == 1
+
+
+def test_paged_api_rejects_host_tensors():
+    """The paged functions run on CUDA tensors only (no CPU fallback)."""
+    import torch
+    from int4_kivi import paged
+    kv = torch.zeros(2, 2, 16, 1, 72, dtype=torch.uint8)
+    k = torch.zeros(4, 1, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        paged.int4_kivi_store(k, k, kv, torch.arange(4), 128)
+    with pytest.raises(ValueError):
+        paged.int4_kivi_paged_decode(torch.zeros(1, 2, 128, dtype=torch.bfloat16), kv,
+                                     torch.zeros(1, 1, dtype=torch.int32), torch.ones(1, dtype=torch.int32))
