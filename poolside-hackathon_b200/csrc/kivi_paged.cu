@@ -443,6 +443,20 @@ __device__ __forceinline__ void e2m1_token_pairs(uint32_t wa, uint32_t wb, uint3
     e2m1x8_to_h2x4(odd, O[0], O[1], O[2], O[3]);
 }
 
+// INT4 PV words with the token-pair scale folded in: each nibble pair is moved
+// to bits (4, 20), the fp16 magic gives 1024 + 16 u (u = n ^ 8), and one fma
+// (v * s/16 - 72 s) yields n * s exactly (n * s has <= 8 significant bits,
+// s/16 and 72 s are exact in fp16).  x holds two tokens' 4-nibble halves;
+// r[i] = scaled channel i of both tokens.
+__device__ __forceinline__ void int4_pairs_scaled(uint32_t x, uint32_t s16, uint32_t c72, uint32_t (&r)[4]) {
+    const uint32_t w[4] = {x << 4, x, x >> 4, x >> 8};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t v = lop3_and_xor(w[i], 0x00F000F0u, 0x64806480u);
+        r[i] = h2_as_u32(__hfma2(u32_as_h2(v), u32_as_h2(s16), u32_as_h2(c72)));
+    }
+}
+
 template <int FMT, int NW>
 __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const __grid_constant__ CUtensorMap tm_kv,
                                                                   const DecP p) {
@@ -713,23 +727,29 @@ __global__ void __launch_bounds__(NW * 32, 1) paged_decode_kernel(const __grid_c
                     e2m1_token_pairs(wa.y, wb.y, X1, Y1);
                     e2m1_token_pairs(wc.x, wd.x, U0, V0);
                     e2m1_token_pairs(wc.y, wd.y, U1, V1);
-                } else {
-                    nib4<FMT>(__byte_perm(wa.x, wb.x, 0x5410), X0);   // ch 16g+0..3, tokens (tA, tB)
-                    nib4<FMT>(__byte_perm(wa.x, wb.x, 0x7632), Y0);   // ch 16g+4..7
-                    nib4<FMT>(__byte_perm(wa.y, wb.y, 0x5410), X1);   // ch 16g+8..11
-                    nib4<FMT>(__byte_perm(wa.y, wb.y, 0x7632), Y1);   // ch 16g+12..15
-                    nib4<FMT>(__byte_perm(wc.x, wd.x, 0x5410), U0);   // same channels, tokens (tC, tD)
-                    nib4<FMT>(__byte_perm(wc.x, wd.x, 0x7632), V0);
-                    nib4<FMT>(__byte_perm(wc.y, wd.y, 0x5410), U1);
-                    nib4<FMT>(__byte_perm(wc.y, wd.y, 0x7632), V1);
-                }
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const uint32_t a0 = hmul2u(e < 4 ? X0[e & 3] : Y0[e & 3], sAB);   // row g
-                    const uint32_t a1 = hmul2u(e < 4 ? X1[e & 3] : Y1[e & 3], sAB);   // row g+8
-                    const uint32_t a2 = hmul2u(e < 4 ? U0[e & 3] : V0[e & 3], sCD);
-                    const uint32_t a3 = hmul2u(e < 4 ? U1[e & 3] : V1[e & 3], sCD);
-                    mma_f16(acc[e], a0, a1, a2, a3, b0, b1);
+                    for (int e = 0; e < 8; ++e) {
+                        const uint32_t a0 = hmul2u(e < 4 ? X0[e & 3] : Y0[e & 3], sAB);   // row g
+                        const uint32_t a1 = hmul2u(e < 4 ? X1[e & 3] : Y1[e & 3], sAB);   // row g+8
+                        const uint32_t a2 = hmul2u(e < 4 ? U0[e & 3] : V0[e & 3], sCD);
+                        const uint32_t a3 = hmul2u(e < 4 ? U1[e & 3] : V1[e & 3], sCD);
+                        mma_f16(acc[e], a0, a1, a2, a3, b0, b1);
+                    }
+                } else {                      // X/U: channels 16g+0..3, Y/V: 16g+4..7 (+8 in X1..V1), scaled
+                    const uint32_t s16AB = hmul2u(sAB, 0x2C002C00u), c72AB = hmul2u(sAB, 0xD480D480u);   // s/16, -72 s
+                    const uint32_t s16CD = hmul2u(sCD, 0x2C002C00u), c72CD = hmul2u(sCD, 0xD480D480u);
+                    int4_pairs_scaled(__byte_perm(wa.x, wb.x, 0x5410), s16AB, c72AB, X0);   // tokens (tA, tB)
+                    int4_pairs_scaled(__byte_perm(wa.x, wb.x, 0x7632), s16AB, c72AB, Y0);
+                    int4_pairs_scaled(__byte_perm(wa.y, wb.y, 0x5410), s16AB, c72AB, X1);
+                    int4_pairs_scaled(__byte_perm(wa.y, wb.y, 0x7632), s16AB, c72AB, Y1);
+                    int4_pairs_scaled(__byte_perm(wc.x, wd.x, 0x5410), s16CD, c72CD, U0);   // tokens (tC, tD)
+                    int4_pairs_scaled(__byte_perm(wc.x, wd.x, 0x7632), s16CD, c72CD, V0);
+                    int4_pairs_scaled(__byte_perm(wc.y, wd.y, 0x5410), s16CD, c72CD, U1);
+                    int4_pairs_scaled(__byte_perm(wc.y, wd.y, 0x7632), s16CD, c72CD, V1);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        mma_f16(acc[e], e < 4 ? X0[e & 3] : Y0[e & 3], e < 4 ? X1[e & 3] : Y1[e & 3],
+                                e < 4 ? U0[e & 3] : V0[e & 3], e < 4 ? U1[e & 3] : V1[e & 3], b0, b1);
                 }
             }
         };
