@@ -3,7 +3,7 @@
 //
 // Each rank owns one exchange buffer (same size on every rank), allocated
 // here with cudaMalloc and mapped into the other ranks' address spaces with
-// CUDA IPC handles (plain peer mappings, no multicast objects):
+// CUDA IPC handles (plain point-to-point peer mappings):
 //   [0, 64)      uint32 flag[16]: flag[j] = newest epoch rank j has published
 //                to this rank (written remotely by rank j, read locally)
 //   [256, ...)   two slots of rows x (2 + D) fp32: m [rows], l [rows],

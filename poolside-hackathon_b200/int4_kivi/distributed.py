@@ -57,8 +57,8 @@ def merge_partials_torch(m: torch.Tensor, l: torch.Tensor, acc: torch.Tensor) ->
 class _PeerBuffers:
     """One exchange buffer per rank, allocated by the library (cudaMalloc,
     zeroed) and mapped into every other rank with CUDA IPC handles that are
-    all-gathered over the host: plain peer mappings, no NVLink multicast
-    objects.  `peers` is the device array of all ranks' buffer addresses."""
+    all-gathered over the host: plain point-to-point peer mappings.
+    `peers` is the device array of all ranks' buffer addresses."""
 
     def __init__(self, nbytes: int, device, group=None, timeout_s: float = 2.0):
         import torch.distributed as dist

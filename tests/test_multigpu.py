@@ -4,7 +4,7 @@ all-gather, by reading the peers' memory over NVLink (PeerMerge), or inside
 the decode's combine kernel over NVLink (SeqParallelExchange); the result must
 match the single-GPU decode of the whole sequence.  Skipped when
 fewer than 2 GPUs are visible.  NVLS is off and the peer buffers are plain
-(non-multicast) mappings."""
+point-to-point mappings."""
 import os
 
 import pytest
