@@ -36,7 +36,7 @@ METRIC = "packed-KV HBM GB/s (INT4-KIVI fused decode, 64K ctx)"
 # with ncu on the 16384-token case and scaled by tokens to the 65536-token launch.
 TRAFFIC_PER_LAUNCH = 749.7e6
 # same for the paged decode kernel at 16384 tokens (profiles/paged_decode_int4_64k.md)
-PAGED_TRAFFIC_16K = 154.89e6
+PAGED_TRAFFIC_16K = 155.28e6
 
 
 def _peaks():
