@@ -112,10 +112,20 @@ _err_cache: dict = {}
 _work_cache: dict = {}
 
 
+def device_index(device) -> int:
+    """CUDA ordinal of `device` ("cuda", "cuda:1", torch.device or int); a
+    bare "cuda" means the current device, so every spelling of one GPU
+    shares one error flag and one workspace."""
+    d = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+    if d.type != "cuda":
+        raise ValueError(f"not a CUDA device: {d}")
+    return d.index if d.index is not None else torch.cuda.current_device()
+
+
 def alphas(device, n_alphas: int) -> torch.Tensor:
     """linspace(0.5, 1.0, n) built on the CPU (bit-identical to kv_quant's grid),
     copied once per device."""
-    key = (str(device), n_alphas)
+    key = (device_index(device), n_alphas)
     a = _alpha_cache.get(key)
     if a is None:
         a = torch.linspace(0.5, 1.0, n_alphas, dtype=torch.float32).to(device)
@@ -124,7 +134,7 @@ def alphas(device, n_alphas: int) -> torch.Tensor:
 
 
 def err_flag(device) -> torch.Tensor:
-    key = str(device)
+    key = device_index(device)
     e = _err_cache.get(key)
     if e is None:
         e = torch.zeros(1, dtype=torch.int32, device=device)
@@ -143,7 +153,7 @@ def device_status(device) -> int:
 
 def workspace(device, n_floats: int) -> torch.Tensor:
     """Grow-only scratch buffer for decode partials, one per (device, stream)."""
-    key = (str(device), torch.cuda.current_stream(device).cuda_stream)
+    key = (device_index(device), torch.cuda.current_stream(device).cuda_stream)
     w = _work_cache.get(key)
     if w is None or w.numel() < n_floats:
         w = torch.empty(max(n_floats, 1), dtype=torch.float32, device=device)

@@ -115,3 +115,14 @@ def test_paged_api_rejects_host_tensors():
     with pytest.raises(ValueError):
         paged.int4_kivi_paged_decode(torch.zeros(1, 2, 128, dtype=torch.bfloat16), kv,
                                      torch.zeros(1, 1, dtype=torch.int32), torch.ones(1, dtype=torch.int32))
+
+
+def test_device_index_spellings():
+    """Every spelling of one GPU maps to one ordinal, so the error flag a kernel
+    sets is the one device_status reads (no CUDA context needed for these)."""
+    import torch
+    from int4_kivi import _native as N
+    assert N.device_index("cuda:1") == N.device_index(torch.device("cuda", 1)) == N.device_index(1) == 1
+    assert N.device_index(torch.device("cuda:0")) == 0
+    with pytest.raises(ValueError):
+        N.device_index("cpu")
