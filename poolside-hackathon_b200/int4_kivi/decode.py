@@ -93,8 +93,12 @@ def decode_packed(q: Tensor, st: dict, n_qh: int, sm_scale: Optional[float] = No
     if out is None:
         out = torch.empty((B, n_qh, D), dtype=torch.bfloat16, device=dev)
     if exchange is not None:
-        assert not partial and v_hot is None and st.get("seq_lens") is None
+        if partial or v_hot is not None or st.get("seq_lens") is not None:
+            raise ValueError("exchange takes equal-length, fully packed caches and returns the merged output")
         x = exchange
+        if x.closed or (x.rows, x.D) != (B * n_qh, D) or x.device != dev:
+            raise ValueError(f"exchange buffer is for rows={x.rows}, D={x.D} on {x.device} "
+                             f"(closed={x.closed}); this call needs rows={B * n_qh}, D={D} on {dev}")
         rc = L.kivi_decode_seqpar(
             N.ptr(q), q.stride(0), q.stride(1), N.ptr(st["k_packed"]), N.ptr(st["k_scale"]), nps,
             N.ptr(khot) if hot_stride else None, hot_stride, N.ptr(st["v_packed"]), N.ptr(st["v_scale"]), ss,

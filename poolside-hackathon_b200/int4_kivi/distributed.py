@@ -67,7 +67,7 @@ class _PeerBuffers:
         self.group = group or dist.group.WORLD
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
-        self.device = torch.device(device)
+        self.device = torch.device("cuda", N.device_index(device))
         if nbytes <= 0:
             raise ValueError(f"unsupported exchange shape for world={self.world}")
         L = N.lib()
@@ -75,29 +75,29 @@ class _PeerBuffers:
             self.own = ctypes.c_void_p()
             handle = (ctypes.c_char * 64)()
             N.check(L.kivi_peer_alloc(nbytes, ctypes.byref(self.own), handle), "kivi_peer_alloc")
-            handles = [None] * self.world
-            dist.all_gather_object(handles, bytes(handle), group=self.group)
             self.opened = []
-            ptrs = []
-            for j, hj in enumerate(handles):
-                if j == self.rank:
-                    ptrs.append(self.own.value)
-                    continue
-                pj = ctypes.c_void_p()
-                N.check(L.kivi_peer_open((ctypes.c_char * 64).from_buffer_copy(hj), ctypes.byref(pj)),
-                        "kivi_peer_open")
-                self.opened.append(pj)
-                ptrs.append(pj.value)
+            try:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, bytes(handle), group=self.group)
+                ptrs = []
+                for j, hj in enumerate(handles):
+                    if j == self.rank:
+                        ptrs.append(self.own.value)
+                        continue
+                    pj = ctypes.c_void_p()
+                    N.check(L.kivi_peer_open((ctypes.c_char * 64).from_buffer_copy(hj), ctypes.byref(pj)),
+                            "kivi_peer_open")
+                    self.opened.append(pj)
+                    ptrs.append(pj.value)
+            except BaseException:
+                self._release()          # no peer has read this rank's buffer yet
+                raise
+        self.closed = False
         self.peers = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
         self.timeout_ns = int(timeout_s * 1e9)
         dist.barrier(group=self.group)
 
-    def close(self) -> None:
-        """Unmap the peers' buffers and free this rank's (after a barrier, so
-        no peer still reads it)."""
-        import torch.distributed as dist
-        torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)
+    def _release(self) -> None:
         L = self.N.lib()
         with torch.cuda.device(self.device):
             for pj in self.opened:
@@ -106,6 +106,17 @@ class _PeerBuffers:
             if self.own:
                 L.kivi_peer_free(self.own)
                 self.own = ctypes.c_void_p()
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after a barrier, so
+        no peer still reads it).  Collective; a second call does nothing."""
+        import torch.distributed as dist
+        if self.closed:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._release()
+        self.closed = True
 
 
 class PeerMerge(_PeerBuffers):
@@ -124,6 +135,12 @@ class PeerMerge(_PeerBuffers):
 
     def __call__(self, m: torch.Tensor, l: torch.Tensor, acc: torch.Tensor) -> torch.Tensor:
         N, L = self.N, self.N.lib()
+        if self.closed:
+            raise ValueError("PeerMerge is closed")
+        for name, t, shape in (("m", m, (self.rows,)), ("l", l, (self.rows,)), ("acc", acc, (self.rows, self.D))):
+            if tuple(t.shape) != shape or t.dtype != torch.float32 or not t.is_contiguous() or t.device != self.device:
+                raise ValueError(f"{name} must be contiguous fp32 {list(shape)} on {self.device}, "
+                                 f"got {t.dtype} {list(t.shape)} on {t.device}")
         stream = N.stream_of(acc)
         N.check(L.kivi_peer_publish(N.ptr(m), N.ptr(l), N.ptr(acc), self.rows, self.D, self.own,
                                     N.ptr(self.peers), self.world, self.rank, N.ptr(self.epoch), stream),

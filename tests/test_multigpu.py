@@ -35,7 +35,12 @@ def _rank(rank, world, port, k, v, q, ret, how="nccl"):
         from int4_kivi import _native as N
         assert N.device_status(dev) == 0
         out = out.clone()
+        with pytest.raises(ValueError):                 # shape the buffer was not made for
+            seq_parallel_decode(q[:, :8].to(dev), st, 8, merger=pm)
         pm.close()
+        pm.close()                                      # idempotent
+        with pytest.raises(ValueError):
+            seq_parallel_decode(q.to(dev), st, q.shape[1], merger=pm)
     else:
         out = seq_parallel_decode(q.to(dev), st, q.shape[1])
     ret[rank] = out.cpu()

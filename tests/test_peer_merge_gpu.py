@@ -79,6 +79,8 @@ def _seqpar_case(dev, W):
     x.world, x.rank = W, 0
     x.row_epoch = torch.zeros(32, dtype=torch.int32, device=dev)
     x.timeout_ns = int(2e9) if W == 1 else int(5e7)
+    x.rows, x.D, x.closed = 32, 128, False
+    x.device = torch.device("cuda", N.device_index(dev))
     return q[None, :, 0].to(dev), st, x, xbuf
 
 
