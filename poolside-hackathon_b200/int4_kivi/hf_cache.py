@@ -3,8 +3,11 @@ int4_kivi/hf_cache.py:41-267 contract, on libkivi_sm100 kernels).
 
 Per layer: completed 16-token pages are frozen into INT4 with `store_kivi`
 semantics (K per-channel, V per-token); the partial page stays bf16.  `update`
-returns the full dequantised bf16 K/V `[1, H, S, D]` so the model's own
-attention runs unchanged.  Sliding-window layers keep only the trailing
+returns the full dequantised bf16 K/V `[B, H, S, D]` so the model's own
+attention runs unchanged.  The reference takes batch 1 only; here a batch of
+B sequences (equal lengths, as `generate` keeps them) is stored as B*H
+stacked heads, which every kernel of the library takes as is, so each
+sequence's pages and outputs are the ones it would get alone.  Sliding-window layers keep only the trailing
 window, exactly as DynamicSlidingWindowLayer does.
 
 B200 differences (values returned are identical):
@@ -44,11 +47,11 @@ class _Int4KiviLayer(CacheLayerMixin):
         self.is_sliding, self.sliding_window = is_sliding, sliding_window
         self.fused = fused_decode and not is_sliding
         self.store: KIVICache | None = None     # frozen pages (S multiple of 16)
-        self.hot_k: Tensor | None = None        # [H, t < 16, D] bf16
+        self.hot_k: Tensor | None = None        # [B*H, t < 16, D] bf16 (sequence-major heads)
         self.hot_v: Tensor | None = None
         self.cumulative_length = 0
         self._offset = 0                        # frozen tokens dropped by sliding eviction
-        self._deq_k: Tensor | None = None       # [H, cap, D] bf16 dequantised frozen prefix
+        self._deq_k: Tensor | None = None       # [B*H, cap, D] bf16 dequantised frozen prefix
         self._deq_v: Tensor | None = None
         self._deq_len = 0
 
@@ -148,11 +151,12 @@ class _Int4KiviLayer(CacheLayerMixin):
     def update(self, key_states: Tensor, value_states: Tensor, *args, **kwargs) -> tuple[Tensor, Tensor]:
         if not self.is_initialized:
             self.lazy_initialization(key_states, value_states)
-        assert key_states.shape[0] == 1, "Int4KiviCache supports batch size 1"
-        k_new = key_states[0].to(torch.bfloat16)
-        v_new = value_states[0].to(torch.bfloat16)
-        self._H, self._D = k_new.shape[0], k_new.shape[2]
-        n_new = k_new.shape[1]
+        B, H, n_new, D = key_states.shape
+        if self.hot_k is not None and (B, H, D) != (self._B, self._H, self._D):
+            raise ValueError(f"batch/heads/head_dim changed from {(self._B, self._H, self._D)} to {(B, H, D)}")
+        self._B, self._H, self._D = B, H, D
+        k_new = key_states.to(torch.bfloat16).reshape(B * H, n_new, D)
+        v_new = value_states.to(torch.bfloat16).reshape(B * H, n_new, D)
         self.cumulative_length += n_new
         if self.hot_k is None:
             self.hot_k, self.hot_v = k_new, v_new
@@ -163,9 +167,14 @@ class _Int4KiviLayer(CacheLayerMixin):
         self._evict_sliding(n_new)
         if self.fused and n_new == 1:
             # the "int4_kivi" attention function reads the packed pages itself
-            stub = torch.empty((1, self._H, 0, self._D), dtype=torch.bfloat16, device=k_new.device)
+            stub = torch.empty((B, H, 0, D), dtype=torch.bfloat16, device=k_new.device)
             stub._kivi_layer = self
             return stub, stub
+        return self._dense_kv(n_new)
+
+    def _dense_kv(self, n_new: int) -> tuple[Tensor, Tensor]:
+        """bf16 K/V [B, H, S, D] of everything stored (sliding layers: the
+        window the mask of a call with `n_new` tokens expects)."""
         ks, vs = [], []
         if self._frozen_len() > 0:
             fk, fv = self._dequant_frozen()
@@ -178,20 +187,21 @@ class _Int4KiviLayer(CacheLayerMixin):
             want = self.sliding_window - 1 + n_new
             if k_full.shape[1] > want:
                 k_full, v_full = k_full[:, -want:], v_full[:, -want:]
-        return k_full.unsqueeze(0), v_full.unsqueeze(0)
+        B, H = self._B, self._H
+        return k_full.view(B, H, *k_full.shape[1:]), v_full.view(B, H, *v_full.shape[1:])
 
     def fused_decode(self, query: Tensor, scaling: float | None) -> Tensor:
         """Attention of one query token per head over everything stored:
-        query [1, Hq, 1, D] -> bf16 [1, Hq, D]."""
+        query [B, Hq, 1, D] -> bf16 [B, Hq, D]."""
         from .decode import decode_packed
         Hq, D = query.shape[1], query.shape[3]
         frozen, t = self._frozen_len(), self._hot_len()
         c = self.store
         st = dict(k_packed=c.k_packed if frozen else None, k_scale=c.k_scale if frozen else None,
                   v_packed=c.v_packed if frozen else None, v_scale=c.v_scale if frozen else None,
-                  k_hot=self.hot_k if t else torch.empty((self._H, 0, D), dtype=torch.bfloat16,
+                  k_hot=self.hot_k if t else torch.empty((self._B * self._H, 0, D), dtype=torch.bfloat16,
                                                          device=query.device),
-                  H=self._H, S=frozen + t, D=D, B=1)
+                  H=self._H, S=frozen + t, D=D, B=self._B)
         q = query[:, :, 0].to(torch.bfloat16)
         return decode_packed(q, st, Hq, sm_scale=scaling, v_hot=self.hot_v if t else None)
 
@@ -206,13 +216,15 @@ class _Int4KiviLayer(CacheLayerMixin):
         return total
 
     def bf16_nbytes(self) -> int:
-        return 2 * (self._stored_len() * getattr(self, "_H", 0) * getattr(self, "_D", 0)) * 2
+        heads = getattr(self, "_B", 0) * getattr(self, "_H", 0)
+        return 2 * (self._stored_len() * heads * getattr(self, "_D", 0)) * 2
 
     def reset(self) -> None:
         self.__init__(self.k_calib, self.v_calib, self.is_sliding, self.sliding_window, self.fused)
 
     def reorder_cache(self, beam_idx) -> None:
-        pass
+        if getattr(self, "_B", 1) > 1:
+            raise NotImplementedError("beam reordering is not supported by Int4KiviCache")
 
     def crop(self, max_length: int) -> None:
         raise NotImplementedError("crop is not supported by Int4KiviCache")
@@ -258,20 +270,40 @@ def kivi_attention_forward(module, query: Tensor, key: Tensor, value: Tensor, at
                            scaling: float | None = None, **kwargs):
     """transformers attention function ("int4_kivi"): placeholders from a fused
     Int4KiviCache layer go to the fused decode; anything else (prefill,
-    sliding layers, no cache) to the stock SDPA function."""
+    sliding layers, no cache) to the stock SDPA function.  A mask that hides
+    any stored position (a left-padded batch) also takes SDPA, over the
+    layer's dequantised K/V, since the fused decode attends to every token."""
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
     layer = getattr(key, "_kivi_layer", None)
+    if layer is not None and not _attends_all(attention_mask):
+        key, value = layer._dense_kv(1)
+        layer = None
     if layer is None:
-        from transformers.integrations.sdpa_attention import sdpa_attention_forward
         return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout,
                                       scaling=scaling, **kwargs)
-    assert query.shape[0] == 1 and query.shape[2] == 1, "fused decode takes one query token (batch 1)"
-    out = layer.fused_decode(query, scaling)              # [1, Hq, D]
+    if query.shape[2] != 1:
+        raise ValueError("fused decode takes one query token per sequence")
+    out = layer.fused_decode(query, scaling)              # [B, Hq, D]
     return out[:, None].to(query.dtype), None             # [B, q_len, Hq, D]
+
+
+def _attends_all(mask) -> bool:
+    """True when `mask` (None, bool where True attends, or additive float)
+    hides no key position."""
+    if mask is None:
+        return True
+    if mask.dtype == torch.bool:
+        return bool(mask.all())
+    return bool((mask == 0).all())
 
 
 def enable_fused_decode(model) -> None:
     """Register the "int4_kivi" attention function and switch `model` to it;
-    pair with `Int4KiviCache(model.config, fused_decode=True)`."""
+    pair with `Int4KiviCache(model.config, fused_decode=True)`.  The name also
+    gets SDPA's mask builder: without one, transformers passes no mask at all
+    to an unknown attention name, which would drop a batch's padding."""
     from transformers import AttentionInterface
+    from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
     AttentionInterface.register(ATTN_IMPL, kivi_attention_forward)
+    AttentionMaskInterface.register(ATTN_IMPL, sdpa_mask)
     model.set_attn_implementation(ATTN_IMPL)

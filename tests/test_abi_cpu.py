@@ -126,3 +126,19 @@ def test_device_index_spellings():
     assert N.device_index(torch.device("cuda:0")) == 0
     with pytest.raises(ValueError):
         N.device_index("cpu")
+
+
+def test_fused_attention_mask_check():
+    """The fused hf decode runs only when the mask hides no key position
+    (a left-padded batch goes to SDPA over the dequantised K/V)."""
+    import torch
+    from int4_kivi.hf_cache import _attends_all
+    assert _attends_all(None)
+    m = torch.ones(2, 1, 1, 9, dtype=torch.bool)
+    assert _attends_all(m)
+    m[1, 0, 0, 0] = False
+    assert not _attends_all(m)
+    f = torch.zeros(2, 1, 1, 9)
+    assert _attends_all(f)
+    f[0, 0, 0, 3] = torch.finfo(torch.float32).min
+    assert not _attends_all(f)

@@ -163,3 +163,76 @@ def test_fused_generate_tiny_random_model(cuda_dev):
                          past_key_values=Int4KiviCache(config=cfg, fused_decode=True))
     assert out.shape == (1, 56)
     model.set_attn_implementation("sdpa")
+
+
+def test_batched_layer_equals_single_sequences(cuda_dev):
+    """B = 2 sequences stored as stacked heads: `update` returns exactly what
+    two batch-1 layers return, and the fused decode of each row equals fp32
+    attention over that row's stored tokens."""
+    from int4_kivi.hf_cache import _Int4KiviLayer
+    H, Hq, D, B = 2, 8, 128, 2
+    k, v, _ = gen_kv(B * H, 90, D, seed=21)
+    kd, vd = k.view(B, H, 90, D).to(cuda_dev), v.view(B, H, 90, D).to(cuda_dev)
+    g = torch.Generator().manual_seed(22)
+    batched, fused = _Int4KiviLayer(), _Int4KiviLayer(fused_decode=True)
+    single = [_Int4KiviLayer() for _ in range(B)]
+    pos = 0
+    for n in (21, 1, 1, 10, 1, 40, 1):
+        kk, vv = batched.update(kd[:, :, pos:pos + n], vd[:, :, pos:pos + n])
+        fused.update(kd[:, :, pos:pos + n], vd[:, :, pos:pos + n])
+        for b in range(B):
+            sk, sv = single[b].update(kd[b:b + 1, :, pos:pos + n], vd[b:b + 1, :, pos:pos + n])
+            assert torch.equal(kk[b:b + 1], sk) and torch.equal(vv[b:b + 1], sv)
+        pos += n
+        assert kk.shape == (B, H, pos, D) and batched.get_seq_length() == pos
+        if n == 1:
+            q = torch.randn(B, Hq, 1, D, generator=g).bfloat16().to(cuda_dev)
+            out = fused.fused_decode(q, D ** -0.5).float().cpu()
+            ek, ev = _exact_kv(fused)                       # [B*H, pos, D], sequence-major
+            for b in range(B):
+                ref = _ref_attention(q[b, :, 0].cpu(), ek[b * H:(b + 1) * H], ev[b * H:(b + 1) * H], D ** -0.5)
+                err = (out[b] - ref).abs()
+                assert bool((err <= 2e-3 + ref.abs() * 2.0 ** -8).all()), (pos, b, err.max().item())
+    with pytest.raises(ValueError):
+        batched.update(kd[:1, :, :1], vd[:1, :, :1])        # batch size may not change
+
+
+def test_batched_generate_tiny_random_model(cuda_dev):
+    """Batch 2 through a random tiny Llama: teacher-forced logits of the
+    batch track each sequence run alone; fused and dequantise paths agree;
+    a left-padded batch takes SDPA in the fused cache too (same tokens as the
+    dequantise path, bit for bit)."""
+    transformers = pytest.importorskip("transformers")
+    from int4_kivi.hf_cache import Int4KiviCache, enable_fused_decode
+    cfg = transformers.LlamaConfig(vocab_size=128, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                                   num_attention_heads=8, num_key_value_heads=2, head_dim=128,
+                                   max_position_embeddings=512)
+    torch.manual_seed(0)
+    model = transformers.LlamaForCausalLM(cfg).to(cuda_dev, torch.bfloat16).eval()
+    ids = torch.randint(0, 128, (2, 70), device=cuda_dev)
+
+    def forced(x, **kw):
+        c = Int4KiviCache(config=cfg, **kw)
+        lg = [model(x[:, :40], past_key_values=c).logits[:, -1]]
+        for t in range(40, 70):
+            lg.append(model(x[:, t:t + 1], past_key_values=c).logits[:, -1])
+        return torch.stack(lg, 1).float()                    # [B, 31, vocab]
+
+    with torch.no_grad():
+        both = forced(ids)
+        alone = torch.cat([forced(ids[b:b + 1]) for b in range(2)])
+        enable_fused_decode(model)
+        fused = forced(ids, fused_decode=True)
+    scale = both.abs().max().item()
+    assert (both - alone).abs().max().item() <= 0.02 * scale
+    assert (both - fused).abs().max().item() <= 0.02 * scale
+    pad = torch.ones(2, 40, dtype=torch.long, device=cuda_dev)
+    pad[1, :5] = 0                                           # left-padded second row
+    x = ids[:, :40].clone()
+    x[1, :5] = 0
+    out_f = model.generate(x, attention_mask=pad, max_new_tokens=12, do_sample=False,
+                           past_key_values=Int4KiviCache(config=cfg, fused_decode=True))
+    model.set_attn_implementation("sdpa")
+    out_d = model.generate(x, attention_mask=pad, max_new_tokens=12, do_sample=False,
+                           past_key_values=Int4KiviCache(config=cfg))
+    assert out_f.shape == (2, 52) and torch.equal(out_f, out_d)
