@@ -51,10 +51,10 @@ int kivi_last_cuda_error(void);         /* cudaError_t of the last KIVI_ERR_CUDA
 /* ------------------------------------------------------------------------ */
 /* Quantize-and-store.                                                       */
 /*                                                                           */
-/* Replaces int4_kivi/triton_kernels.py:162-203 (k_store_kernel),            */
-/* :241-279 (v_store_kernel) and their launches in int4_kivi/cache.py:90-141.*/
+/* Replaces int4_kivi/triton_kernels.py:137-178 (k_store_kernel),            */
+/* :216-254 (v_store_kernel) and their launches in int4_kivi/cache.py:90-141.*/
 /*                                                                           */
-/* Input K: 16-bit [H, S_k, D], V: [H, S_v, D] (dtype `in_dtype`), strided.  */
+/* Input K: [H, S_k, D], V: [H, S_v, D] of `in_dtype` (bf16, fp16, fp32).  */
 /* (S_k and S_v differ on append: K pages vs new V tokens, one launch.)      */
 /* K: the first (S_k/16)*16 tokens, per channel over 16-token pages, are     */
 /*    written to k_packed[h, d, kpage0 + p, 0:8] (row stride k_np_stride     */
@@ -77,8 +77,8 @@ int kivi_store(const void *k, const void *v, int in_dtype,
 
 /* ------------------------------------------------------------------------ */
 /* Dequantize to bf16 [H, S, D] (out strides in elements).                   */
-/* Replaces int4_kivi/triton_kernels.py:206-235 (k_dequant_kernel),          */
-/* :282-311 (v_dequant_kernel) and int4_kivi/cache.py:165-201.               */
+/* Replaces int4_kivi/triton_kernels.py:181-210 (k_dequant_kernel),          */
+/* :257-286 (v_dequant_kernel) and int4_kivi/cache.py:165-201.               */
 /* K writes tokens [0, (S/16)*16) only (the bf16 hot tail is the caller's);  */
 /* V writes every token.  value = code * fp32(scale) (NVFP4: * g).           */
 /* ------------------------------------------------------------------------ */
@@ -101,6 +101,19 @@ int kivi_roundtrip(const void *x, void *y, int dtype, int H, int S, int D,
 int kivi_calibrate(const float *blocks, int64_t n, int fmt, int calib,
                    const float *alphas, int n_alphas, float *scales,
                    kivi_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Legacy page-level dequant.  Replaces kv_quant.py:70-76                    */
+/* (QuantizedPage.dequantize: `q.to(fp16) * scale`, then `.to(bfloat16)`)     */
+/* and the unpacked int8 codes of kv_quant.py:37-38 (quantize_block).        */
+/* packed u8 [rows, row_stride, D/16, 8] and fp16 scale [rows, row_stride,   */
+/* D/16] as written by kivi_store's V path (per-token 16-channel blocks).    */
+/* out  : bf16 [rows, tokens, D] = bf16(fp16(code * scale)), or NULL.        */
+/* codes: int8 [rows, tokens, D], or NULL.  out / codes 16-byte aligned.     */
+/* ------------------------------------------------------------------------ */
+int kivi_page_dequant(const uint8_t *packed, const void *scale, int rows, int tokens,
+                      int row_stride, int D, void *out, int8_t *codes,
+                      kivi_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Fused split-K flash-decode over a packed cache.                           */
@@ -185,8 +198,8 @@ int kivi_decode_partial(const void *q, int64_t q_sb, int64_t q_sh,
 /* ------------------------------------------------------------------------ */
 /* kivi_decode without a caller workspace: no counterpart in the reference.  */
 /* For callers that cannot allocate device memory at decode time (a serving  */
-/* engine with its own fixed memory pool, a stream capture, an FFI host      */
-/* without a CUDA allocator).  Same arguments and result as kivi_decode,     */
+/* engine that hands out all device memory from its own fixed pool, an FFI   */
+/* host without a CUDA allocator).  Same arguments and result as kivi_decode,*/
 /* minus `work`; the split-K partials go to a library-owned device array of  */
 /* KIVI_NOALLOC_SCRATCH_FLOATS floats (8 MiB, held on every GPU that loads   */
 /* the library until exit).  Problems whose kivi_decode_workspace_floats()   */
@@ -195,7 +208,9 @@ int kivi_decode_partial(const void *q, int64_t q_sb, int64_t q_sh,
 /* make that first call before any stream capture.  All calls share the one  */
 /* array: calls that overlap on the GPU (different streams, or different     */
 /* host threads on the same device) race and must be serialised by the      */
-/* caller.  Nothing is allocated or freed.                                   */
+/* caller.  Nothing is allocated or freed.  The looked-up address is kept    */
+/* for the life of the process: after a cudaDeviceReset the library must be  */
+/* reloaded before this entry point is used again on that device.           */
 /* ------------------------------------------------------------------------ */
 #define KIVI_NOALLOC_SCRATCH_FLOATS (1 << 21)
 
@@ -268,6 +283,17 @@ int kivi_paged_decode(const void *q, int64_t q_sb, int64_t q_sh,
                       int B, int Hq, int Hkv, int D, int fmt, float sm_scale,
                       void *out, float *work, int64_t work_floats, int *err,
                       kivi_stream_t stream);
+
+/* Same decode with the normalised output kept in fp32 [B, Hq, D] (the value */
+/* kivi_paged_decode rounds to bf16): the fork's paged decode has no such    */
+/* output; it exists for callers (and parity checks) that want the state     */
+/* before the bf16 cast.                                                     */
+int kivi_paged_decode_f32(const void *q, int64_t q_sb, int64_t q_sh,
+                          const uint8_t *kv_cache, int64_t num_blocks,
+                          const int *block_table, int64_t bt_stride, const int *seq_lens,
+                          int B, int Hq, int Hkv, int D, int fmt, float sm_scale,
+                          float *out, float *work, int64_t work_floats, int *err,
+                          kivi_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Sequence-parallel decode with the cross-GPU merge fused into the decode's */

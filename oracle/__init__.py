@@ -283,3 +283,44 @@ def paged_decode(q, kv: np.ndarray, block_table, seq_lens, sm_scale: float, fmt:
     ms = max(int(sl.max()) if sl.size else 0, 1)
     k, v = paged_gather(kv, block_table, sl, H, D, fmt, ms)
     return decode_attention(qf, k, v, sm_scale, seq_lens=sl)
+
+
+# ----------------------- legacy page-level API -----------------------
+def page_quantize(x, calib: str = "mse", n_alphas: int = 32) -> tuple[np.ndarray, np.ndarray]:
+    """kv_quant.quantize_page for one tensor x [H, T, D] (kv_quant.py:37-38,
+    71-84): per-token 16-channel blocks, fp32 scale from the calibration,
+    codes = clamp(rint(x / s), -7, 7) with an fp32 division, scales stored
+    as fp16.  Returns (int8 codes [H, T, D], fp16 scales [H, T, D/16])."""
+    xf = _f32(x)
+    H, T, D = xf.shape
+    xb = xf.reshape(H, T, D // BLOCK, BLOCK)
+    s = calibrate(xb, "int4", calib, n_alphas)                   # [H, T, ND, 1] fp32
+    codes = np.clip(np.rint(xb / s), -7, 7).astype(np.int8).reshape(H, T, D)
+    return codes, s[..., 0].astype(np.float16)
+
+
+def page_dequant(codes: np.ndarray, scale16: np.ndarray):
+    """QuantizedPage.dequantize (kv_quant.py:62-67): fp16(code * fp16 scale),
+    then bf16; returned as a torch bf16 tensor [H, T, D]."""
+    import torch
+    H, T, D = codes.shape
+    sf = np.repeat(scale16.astype(np.float16), BLOCK, axis=-1).reshape(H, T, D)
+    prod = codes.astype(np.float16) * sf                          # rounded once to fp16
+    return torch.from_numpy(prod.astype(np.float32)).to(torch.bfloat16)
+
+
+def page_error(x, page_size: int = 16, n_alphas: int = 32) -> tuple[float, float]:
+    """kv_quant.measure_page_error (kv_quant.py:170-191): mean over complete
+    pages of each page's mean squared error, absmax and MSE calibration."""
+    xf = _f32(x)
+    H, S, D = xf.shape
+    P = S // page_size
+    res = []
+    for calib in ("absmax", "mse"):
+        errs = []
+        for i in range(P):
+            pg = xf[:, i * page_size:(i + 1) * page_size]
+            d = pg - roundtrip_f32(pg, "int4", "headdim", calib, n_alphas)
+            errs.append(float(np.mean(d.astype(np.float64) ** 2)))
+        res.append(sum(errs) / max(len(errs), 1))
+    return res[0], res[1]

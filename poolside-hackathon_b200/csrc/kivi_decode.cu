@@ -10,7 +10,7 @@
 //   * work = flattened (head, 128-token tile) list split evenly over a
 //     persistent grid (stream-K style), so every SM gets the same bytes;
 //   * warp 4 issues TMA tile loads (K codes/scales, V codes/scales) into a
-//     4-stage ring guarded by mbarriers; warps 0-3 each own 32 tokens of a
+//     3-stage ring guarded by mbarriers; warps 0-3 each own 32 tokens of a
 //     tile;
 //   * packed nibbles go smem -> registers with ldmatrix.trans, which pairs
 //     two channels (K) or two tokens (V) per 32-bit word; a LOP3 fp16 magic
@@ -32,13 +32,8 @@ namespace kivi {
 constexpr int TILE = 128;        // tokens per pipeline stage (8 pages)
 constexpr int NWARP_C = 4;       // consumer warps, 32 tokens each
 constexpr int NTHREADS = (NWARP_C + 1) * 32;
-#ifndef KIVI_NST
-#define KIVI_NST 3
-#endif
-#ifndef KIVI_CTAS
-#define KIVI_CTAS 3
-#endif
-constexpr int NST = KIVI_NST;    // pipeline depth
+constexpr int NST = 3;           // pipeline depth
+constexpr int CTAS_PER_SM = 3;   // resident CTAs the register budget is sized for
 constexpr int DH = 128;          // head_dim of the fast path
 constexpr int PB_PITCH = 40;     // halves per head row in the P staging buffer
 
@@ -269,7 +264,7 @@ __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
 // Fast path kernel.
 // ---------------------------------------------------------------------------
 template <int FMT, bool PAIRED>
-__global__ void __launch_bounds__(NTHREADS, KIVI_CTAS)
+__global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
 decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_constant__ CUtensorMap tm_ks,
                    const __grid_constant__ CUtensorMap tm_vc, const __grid_constant__ CUtensorMap tm_vs,
                    const DecodeParams p) {
@@ -1168,9 +1163,8 @@ extern "C" int kivi_lse_merge(const float* m, const float* l, const float* acc, 
 // Allocation-free decode.
 //
 // Some callers cannot call cudaMalloc at decode time: a serving engine that
-// hands out all device memory from its own pre-sized pool, code running
-// under a CUDA stream capture, or an FFI host (Go, Java) that owns no CUDA
-// allocator.  For them the split-K partials live in one fixed, library-owned
+// hands out all device memory from its own pre-sized pool, or an FFI host
+// (Go, Java) that owns no CUDA allocator.  For them the split-K partials live in one fixed, library-owned
 // device array instead of a caller-supplied workspace.  Its size is fixed at
 // KIVI_NOALLOC_SCRATCH_FLOATS fp32 values (8 MiB) and every GPU that loads the
 // library keeps it until the process exits.

@@ -311,14 +311,8 @@ __global__ void __launch_bounds__(128) gather_kernel(const GatherP p) {
 // ---------------------------------------------------------------------------
 constexpr int DD = 128;               // head_dim of the fast path
 constexpr int FDD = 72;               // row bytes per head at D = 128
-#ifndef KIVI_PG_TP
-#define KIVI_PG_TP 5
-#endif
-#ifndef KIVI_PG_NST
-#define KIVI_PG_NST 6
-#endif
-constexpr int TP = KIVI_PG_TP;        // blocks per pipeline stage
-constexpr int PNST = KIVI_PG_NST;     // most pipeline stages (the launch picks what fits)
+constexpr int TP = 5;                 // blocks per pipeline stage
+constexpr int PNST = 6;               // most pipeline stages (the launch picks what fits)
 constexpr int PBP = 16 * TP + 8;     // halves per head row of the P staging buffer
 constexpr int MAX_H = 16;             // KV heads (consumer warps) of the fast path
 
@@ -335,7 +329,8 @@ struct DecP {
     float* part_m; float* part_l; float* part_acc;
     int* tile_off;                    // [B + 1]
     int* err;
-    __nv_bfloat16* out;
+    __nv_bfloat16* out;               // bf16 [B, Hq, D], or null
+    float* out_f32;                   // fp32 [B, Hq, D] (normalised, before the bf16 cast), or null
 };
 
 __device__ __forceinline__ int seq_len_of(const DecP& p, int b) {
@@ -832,7 +827,9 @@ __global__ void __launch_bounds__(128) paged_merge_kernel(const DecP p) {
     const int d = threadIdx.x;
     const float a = (sacc[d] + sacc[D + d]) + (sacc[2 * D + d] + sacc[3 * D + d]);
     const int64_t row = (int64_t)b * p.Hq + h * G + n;
-    p.out[row * D + d] = __float2bfloat16_rn(ns > 0 && Ls > 0.f ? a / Ls : 0.f);
+    const float o = ns > 0 && Ls > 0.f ? a / Ls : 0.f;
+    if (p.out) p.out[row * D + d] = __float2bfloat16_rn(o);
+    if (p.out_f32) p.out_f32[row * D + d] = o;
 }
 
 // Any head_dim (multiple of 16, <= 256), group <= 16: one CTA per (sequence,
@@ -908,7 +905,10 @@ __global__ void __launch_bounds__(128) paged_decode_generic_kernel(const DecP p)
             Ls += sm_l[w2][n] * e;
             a += sm_acc[(w2 * G + n) * D + d] * e;
         }
-        p.out[((int64_t)b * p.Hq + h * G + n) * D + d] = __float2bfloat16_rn(Ls > 0.f ? a / Ls : 0.f);
+        const float o = Ls > 0.f ? a / Ls : 0.f;
+        const int64_t oi = ((int64_t)b * p.Hq + h * G + n) * D + d;
+        if (p.out) p.out[oi] = __float2bfloat16_rn(o);
+        if (p.out_f32) p.out_f32[oi] = o;
     }
 }
 
@@ -945,10 +945,7 @@ EncodeFn paged_encode_fn() {
 // 24 or 8 words apart mod 32 (rows g..g+3 then cover distinct banks).  The
 // padded pitch needs the TMA path (rows of whole 16-byte multiples, even H);
 // odd H keeps the natural pitch.
-#ifndef KIVI_PG_PAD
-#define KIVI_PG_PAD 1
-#endif
-bool paged_tma_ok(int H) { return KIVI_PG_PAD && (H * FDD) % 16 == 0; }
+bool paged_tma_ok(int H) { return (H * FDD) % 16 == 0; }
 int paged_rowp(int H) {
     const int rb = H * FDD;
     if (!paged_tma_ok(H)) return rb;
@@ -1066,14 +1063,15 @@ extern "C" int64_t kivi_paged_decode_workspace_floats(int B, int Hq, int Hkv, in
     return paged_plan(B, Hkv, Hq / Hkv, bt_stride, D, sms, PAGED_MAX_OCC).floats;
 }
 
-extern "C" int kivi_paged_decode(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* kv_cache,
-                                 int64_t num_blocks, const int* block_table, int64_t bt_stride,
-                                 const int* seq_lens, int B, int Hq, int Hkv, int D, int fmt, float sm_scale,
-                                 void* out, float* work, int64_t work_floats, int* err, kivi_stream_t stream) {
+namespace {
+int paged_decode_impl(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* kv_cache, int64_t num_blocks,
+                      const int* block_table, int64_t bt_stride, const int* seq_lens, int B, int Hq, int Hkv,
+                      int D, int fmt, float sm_scale, void* out, float* out_f32, float* work,
+                      int64_t work_floats, int* err, kivi_stream_t stream) {
     if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || D <= 0 || D % 16 || D > 256 || !fmt_ok(fmt) || bt_stride < 0)
         return KIVI_ERR_ARG;
     if (B == 0) return KIVI_OK;
-    if (!q || !kv_cache || !block_table || !seq_lens || !out || num_blocks <= 0) return KIVI_ERR_ARG;
+    if (!q || !kv_cache || !block_table || !seq_lens || (!out && !out_f32) || num_blocks <= 0) return KIVI_ERR_ARG;
     const int G = Hq / Hkv;
     int dev = 0;
     const int sms = cur_device_sms(&dev);
@@ -1084,7 +1082,7 @@ extern "C" int kivi_paged_decode(const void* q, int64_t q_sb, int64_t q_sh, cons
     p.bt = block_table; p.bt_stride = bt_stride; p.seq_lens = seq_lens;
     p.B = B; p.Hq = Hq; p.G = G;
     p.scale2 = sm_scale * 1.4426950408889634f;
-    p.err = err; p.out = reinterpret_cast<__nv_bfloat16*>(out);
+    p.err = err; p.out = reinterpret_cast<__nv_bfloat16*>(out); p.out_f32 = out_f32;
     cudaStream_t st = (cudaStream_t)stream;
     const bool fast = D == DD && Hkv <= MAX_H && G <= 8 && (uintptr_t)kv_cache % 16 == 0 &&
                       (uintptr_t)q % 4 == 0 && q_sh % 2 == 0 && q_sb % 2 == 0;
@@ -1158,4 +1156,24 @@ extern "C" int kivi_paged_decode(const void* q, int64_t q_sb, int64_t q_sh, cons
     cudaError_t le = cudaLaunchKernelEx(&cfg, paged_merge_kernel, p);
     if (le != cudaSuccess) return record_cuda_error(le);
     return check_launch();
+}
+}  // namespace
+
+extern "C" int kivi_paged_decode(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* kv_cache,
+                                 int64_t num_blocks, const int* block_table, int64_t bt_stride,
+                                 const int* seq_lens, int B, int Hq, int Hkv, int D, int fmt, float sm_scale,
+                                 void* out, float* work, int64_t work_floats, int* err, kivi_stream_t stream) {
+    if (!out) return KIVI_ERR_ARG;
+    return paged_decode_impl(q, q_sb, q_sh, kv_cache, num_blocks, block_table, bt_stride, seq_lens, B, Hq, Hkv, D,
+                             fmt, sm_scale, out, nullptr, work, work_floats, err, stream);
+}
+
+extern "C" int kivi_paged_decode_f32(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* kv_cache,
+                                     int64_t num_blocks, const int* block_table, int64_t bt_stride,
+                                     const int* seq_lens, int B, int Hq, int Hkv, int D, int fmt, float sm_scale,
+                                     float* out, float* work, int64_t work_floats, int* err,
+                                     kivi_stream_t stream) {
+    if (!out) return KIVI_ERR_ARG;
+    return paged_decode_impl(q, q_sb, q_sh, kv_cache, num_blocks, block_table, bt_stride, seq_lens, B, Hq, Hkv, D,
+                             fmt, sm_scale, nullptr, out, work, work_floats, err, stream);
 }

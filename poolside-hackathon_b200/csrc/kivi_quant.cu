@@ -65,42 +65,90 @@ __device__ __forceinline__ void quant_pack(const float x[BLK], int calib, const 
     packed = make_uint2(lo, hi);
 }
 
-// grid-stride over K blocks (h, p, d) then V blocks (h, t, db).
+// K blocks (per channel, 16-token pages) go through shared memory so that
+// both sides are coalesced: a CTA loads PPC pages x D channels of one head
+// with 16-byte row loads, each thread quantises (channel, page) blocks read
+// column-wise from the tile, and the packed results are written back grouped
+// by channel, where consecutive pages are contiguous in k_packed / k_scale.
+// V blocks (16 channels of one token) are contiguous in the input and in the
+// output, so V CTAs take one block per thread directly.
+// Grid: [0, nk_ctas) K chunks (head-major), then V CTAs (grid-stride).
 template <typename T, int FMT>
-__global__ void __launch_bounds__(256) store_kernel(StoreArgs a) {
+__global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_chunks, int nk_ctas) {
+    extern __shared__ __align__(16) uint8_t st_smem[];
     const T* k = reinterpret_cast<const T*>(a.k);
     const T* v = reinterpret_cast<const T*>(a.v);
-    const int NP = a.S_k / BLK, ND = a.D / BLK;
-    const int64_t nk = (int64_t)a.H * NP * a.D;
+    const int D = a.D, ND = D / BLK, tid = threadIdx.x;
+    if ((int)blockIdx.x < nk_ctas) {
+        const int NP = a.S_k / BLK;
+        const int h = blockIdx.x / n_chunks, p0 = (blockIdx.x % n_chunks) * ppc;
+        const int np_here = min(ppc, NP - p0), ntok = np_here * BLK;
+        T* tile = reinterpret_cast<T*>(st_smem);                                   // [ntok][D]
+        uint2* sc = reinterpret_cast<uint2*>(st_smem + (size_t)ppc * BLK * D * sizeof(T));   // [ppc][D+1]
+        uint16_t* ss = reinterpret_cast<uint16_t*>(sc + (size_t)ppc * (D + 1));               // [ppc][D+2]
+        const T* src = k + h * a.sk_h + (int64_t)p0 * BLK * a.sk_s;
+        const int vpr = D * (int)sizeof(T) / 16;                                   // 16-byte vectors per row
+        if (a.sk_d == 1 && (a.sk_s * (int64_t)sizeof(T)) % 16 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+            uint4* t4 = reinterpret_cast<uint4*>(tile);
+            for (int i = tid; i < ntok * vpr; i += 256) {
+                const int r = i / vpr, c = i - r * vpr;
+                t4[i] = __ldg(reinterpret_cast<const uint4*>(src + r * a.sk_s) + c);
+            }
+        } else {
+            for (int i = tid; i < ntok * D; i += 256) {
+                const int r = i / D, d = i - r * D;
+                tile[i] = src[r * a.sk_s + d * a.sk_d];
+            }
+        }
+        __syncthreads();
+        for (int b = tid; b < np_here * D; b += 256) {
+            const int p = b / D, c = b - p * D;
+            float x[BLK];
+#pragma unroll
+            for (int j = 0; j < BLK; ++j) x[j] = to_f32<T>(tile[(p * BLK + j) * D + c]);
+            uint2 pk;
+            uint16_t sb;
+            quant_pack<FMT>(x, a.calib_k, a.alphas, a.n_alphas, a.g_k, pk, sb);
+            sc[p * (D + 1) + c] = pk;
+            ss[p * (D + 2) + c] = sb;
+        }
+        __syncthreads();
+        for (int b = tid; b < np_here * D; b += 256) {
+            const int c = b / np_here, p = b - c * np_here;
+            const int64_t row = ((int64_t)h * D + c) * a.k_np_stride + a.kpage0 + p0 + p;
+            reinterpret_cast<uint2*>(a.k_packed)[row] = sc[p * (D + 1) + c];
+            if (FMT == FMT_NVFP4) reinterpret_cast<uint8_t*>(a.k_scale)[row] = (uint8_t)ss[p * (D + 2) + c];
+            else reinterpret_cast<uint16_t*>(a.k_scale)[row] = ss[p * (D + 2) + c];
+        }
+        return;
+    }
     const int64_t nv = (int64_t)a.H * a.S_v * ND;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nk + nv;
-         i += (int64_t)gridDim.x * blockDim.x) {
+    const int nv_ctas = gridDim.x - nk_ctas;
+    for (int64_t j = (int64_t)(blockIdx.x - nk_ctas) * 256 + tid; j < nv; j += (int64_t)nv_ctas * 256) {
+        const int db = (int)(j % ND);
+        const int64_t r = j / ND;
+        const int t = (int)(r % a.S_v), h = (int)(r / a.S_v);
         float x[BLK];
         uint2 pk;
         uint16_t sb;
-        if (i < nk) {
-            const int d = (int)(i % a.D);
-            const int64_t r = i / a.D;
-            const int p = (int)(r % NP), h = (int)(r / NP);
-            load_strided16<T>(k + h * a.sk_h + (int64_t)p * BLK * a.sk_s + d * a.sk_d, a.sk_s, x);
-            quant_pack<FMT>(x, a.calib_k, a.alphas, a.n_alphas, a.g_k, pk, sb);
-            const int64_t row = ((int64_t)h * a.D + d) * a.k_np_stride + a.kpage0 + p;
-            reinterpret_cast<uint2*>(a.k_packed)[row] = pk;
-            if (FMT == FMT_NVFP4) reinterpret_cast<uint8_t*>(a.k_scale)[row] = (uint8_t)sb;
-            else reinterpret_cast<uint16_t*>(a.k_scale)[row] = sb;
-        } else {
-            const int64_t j = i - nk;
-            const int db = (int)(j % ND);
-            const int64_t r = j / ND;
-            const int t = (int)(r % a.S_v), h = (int)(r / a.S_v);
-            load_contig16<T>(v + h * a.sv_h + t * a.sv_s + (int64_t)db * BLK * a.sv_d, a.sv_d, x);
-            quant_pack<FMT>(x, a.calib_v, a.alphas, a.n_alphas, a.g_v, pk, sb);
-            const int64_t row = ((int64_t)h * a.v_s_stride + a.vtok0 + t) * ND + db;
-            reinterpret_cast<uint2*>(a.v_packed)[row] = pk;
-            if (FMT == FMT_NVFP4) reinterpret_cast<uint8_t*>(a.v_scale)[row] = (uint8_t)sb;
-            else reinterpret_cast<uint16_t*>(a.v_scale)[row] = sb;
-        }
+        load_contig16<T>(v + h * a.sv_h + t * a.sv_s + (int64_t)db * BLK * a.sv_d, a.sv_d, x);
+        quant_pack<FMT>(x, a.calib_v, a.alphas, a.n_alphas, a.g_v, pk, sb);
+        const int64_t row = ((int64_t)h * a.v_s_stride + a.vtok0 + t) * ND + db;
+        reinterpret_cast<uint2*>(a.v_packed)[row] = pk;
+        if (FMT == FMT_NVFP4) reinterpret_cast<uint8_t*>(a.v_scale)[row] = (uint8_t)sb;
+        else reinterpret_cast<uint16_t*>(a.v_scale)[row] = sb;
     }
+}
+
+// Pages per K chunk: the input tile stays within 64 KB of shared memory.
+template <typename T>
+static int store_ppc(int D) {
+    const int p = 65536 / (BLK * D * (int)sizeof(T));
+    return p < 1 ? 1 : (p > 16 ? 16 : p);
+}
+template <typename T>
+static size_t store_smem(int D, int ppc) {
+    return (size_t)ppc * BLK * D * sizeof(T) + (size_t)ppc * (D + 1) * 8 + (size_t)ppc * (D + 2) * 2;
 }
 
 __device__ __forceinline__ float nib_value(uint32_t nib, int fmt) {
@@ -154,6 +202,45 @@ __global__ void __launch_bounds__(256) dequant_kernel(DequantArgs a) {
                 o[c * a.so_d] = __float2bfloat16_rn(__fmul_rn(nib_value(nib, FMT), s));
             }
         }
+    }
+}
+
+// Legacy page-level dequant (kv_quant.py:70-76, QuantizedPage.dequantize):
+// per-token 16-channel INT4 blocks, value = bf16(fp16(code * fp16 scale)),
+// the fp16 product rounded once and then narrowed to bf16 like the
+// reference's `q.to(fp16) * scale` followed by `.to(bfloat16)`.  Optionally
+// also writes the unpacked int8 codes.  One thread per block.
+__global__ void __launch_bounds__(256) page_dequant_kernel(const uint8_t* __restrict__ packed,
+                                                           const __half* __restrict__ scale, int rows,
+                                                           int tokens, int row_stride, int ND,
+                                                           __nv_bfloat16* __restrict__ out,
+                                                           int8_t* __restrict__ codes) {
+    const int64_t n = (int64_t)rows * tokens * ND;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int db = (int)(i % ND);
+        const int64_t rt = i / ND;
+        const int t = (int)(rt % tokens), r = (int)(rt / tokens);
+        const int64_t src = ((int64_t)r * row_stride + t) * ND + db;
+        const uint2 pk = reinterpret_cast<const uint2*>(packed)[src];
+        const __half s = scale[src];
+        uint32_t ob[8];
+        uint32_t cb[4];
+#pragma unroll
+        for (int j = 0; j < BLK; ++j) {
+            const int c = sx4((int)(((j < 8 ? pk.x : pk.y) >> (4 * (j & 7))) & 0xF));
+            const __half prod = __hmul(__int2half_rn(c), s);
+            const uint32_t bits = __bfloat16_as_ushort(__float2bfloat16_rn(__half2float(prod)));
+            if (j & 1) ob[j >> 1] |= bits << 16; else ob[j >> 1] = bits;
+            const uint32_t cbyte = (uint32_t)(c & 0xFF) << (8 * (j & 3));
+            if (j & 3) cb[j >> 2] |= cbyte; else cb[j >> 2] = cbyte;
+        }
+        const int64_t o = i * BLK;                     // [rows, tokens, ND, 16] == [rows, tokens, D]
+        if (out) {
+            uint4* o4 = reinterpret_cast<uint4*>(out + o);
+            o4[0] = make_uint4(ob[0], ob[1], ob[2], ob[3]);
+            o4[1] = make_uint4(ob[4], ob[5], ob[6], ob[7]);
+        }
+        if (codes) *reinterpret_cast<uint4*>(codes + o) = make_uint4(cb[0], cb[1], cb[2], cb[3]);
     }
 }
 
@@ -220,6 +307,37 @@ static int grid_for(int64_t n) {
 
 using namespace kivi;
 
+namespace {
+template <typename T, int FMT>
+int launch_store(const StoreArgs& a, cudaStream_t st) {
+    const int NP = a.S_k / BLK, ND = a.D / BLK;
+    const int ppc = store_ppc<T>(a.D);
+    const int n_chunks = (NP + ppc - 1) / ppc;
+    const int64_t nk_ctas64 = (int64_t)a.H * n_chunks;
+    const int64_t nv = (int64_t)a.H * a.S_v * ND;
+    int64_t nv_ctas = (nv + 255) / 256;
+    if (nv_ctas > 148LL * 16) nv_ctas = 148LL * 16;
+    if (nk_ctas64 + nv_ctas > 0x7fffffffLL) return KIVI_ERR_UNSUPPORTED;
+    const size_t smem = nk_ctas64 > 0 ? store_smem<T>(a.D, ppc) : 0;
+    if (smem > 48 * 1024) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        static int set_bytes[64];                  // largest size configured, per device
+        if (dev >= 0 && dev < 64 && set_bytes[dev] < (int)smem) {
+            e = cudaFuncSetAttribute(store_kernel<T, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return record_cuda_error(e);
+            set_bytes[dev] = (int)smem;
+        } else if (dev < 0 || dev >= 64) {
+            e = cudaFuncSetAttribute(store_kernel<T, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return record_cuda_error(e);
+        }
+    }
+    store_kernel<T, FMT><<<(int)(nk_ctas64 + nv_ctas), 256, smem, st>>>(a, ppc, n_chunks, (int)nk_ctas64);
+    return check_launch();
+}
+}  // namespace
+
 extern "C" int kivi_store(const void* k, const void* v, int in_dtype, int64_t sk_h, int64_t sk_s,
                           int64_t sk_d, int64_t sv_h, int64_t sv_s, int64_t sv_d, int H, int S_k,
                           int S_v, int D, int fmt, int calib_k, int calib_v, const float* alphas,
@@ -230,7 +348,7 @@ extern "C" int kivi_store(const void* k, const void* v, int in_dtype, int64_t sk
     if (fmt != FMT_INT4 && fmt != FMT_NVFP4) return KIVI_ERR_ARG;
     if ((unsigned)calib_k > 1 || (unsigned)calib_v > 1) return KIVI_ERR_ARG;
     if ((calib_k == CAL_MSE || calib_v == CAL_MSE) && (!alphas || n_alphas <= 0)) return KIVI_ERR_ARG;
-    if (in_dtype != KIVI_DT_BF16 && in_dtype != KIVI_DT_F16) return KIVI_ERR_ARG;
+    if (in_dtype != KIVI_DT_BF16 && in_dtype != KIVI_DT_F16 && in_dtype != KIVI_DT_F32) return KIVI_ERR_ARG;
     if (fmt == FMT_NVFP4 && !(g_k > 0.0f && g_v > 0.0f)) return KIVI_ERR_ARG;
     const int NP = S_k / BLK;
     if (NP > 0 && (kpage0 < 0 || k_np_stride < kpage0 + NP)) return KIVI_ERR_ARG;
@@ -244,15 +362,14 @@ extern "C" int kivi_store(const void* k, const void* v, int in_dtype, int64_t sk
                 n_alphas, g_k, g_v, k_packed, k_scale, kpage0, k_np_stride, v_packed, v_scale,
                 vtok0, v_s_stride};
     cudaStream_t st = (cudaStream_t)stream;
-    const int g = grid_for(n);
-    if (in_dtype == KIVI_DT_BF16) {
-        if (fmt == FMT_INT4) store_kernel<__nv_bfloat16, FMT_INT4><<<g, 256, 0, st>>>(a);
-        else store_kernel<__nv_bfloat16, FMT_NVFP4><<<g, 256, 0, st>>>(a);
-    } else {
-        if (fmt == FMT_INT4) store_kernel<__half, FMT_INT4><<<g, 256, 0, st>>>(a);
-        else store_kernel<__half, FMT_NVFP4><<<g, 256, 0, st>>>(a);
+    switch (in_dtype) {
+        case KIVI_DT_BF16: return fmt == FMT_INT4 ? launch_store<__nv_bfloat16, FMT_INT4>(a, st)
+                                                  : launch_store<__nv_bfloat16, FMT_NVFP4>(a, st);
+        case KIVI_DT_F16: return fmt == FMT_INT4 ? launch_store<__half, FMT_INT4>(a, st)
+                                                 : launch_store<__half, FMT_NVFP4>(a, st);
+        default: return fmt == FMT_INT4 ? launch_store<float, FMT_INT4>(a, st)
+                                        : launch_store<float, FMT_NVFP4>(a, st);
     }
-    return check_launch();
 }
 
 extern "C" int kivi_dequant(const uint8_t* k_packed, const void* k_scale, int k_np_stride,
@@ -303,5 +420,19 @@ extern "C" int kivi_calibrate(const float* blocks, int64_t n, int fmt, int calib
     if (n == 0) return KIVI_OK;
     calibrate_kernel<<<grid_for(n), 256, 0, (cudaStream_t)stream>>>(blocks, n, fmt, calib, alphas,
                                                                     n_alphas, scales);
+    return check_launch();
+}
+
+extern "C" int kivi_page_dequant(const uint8_t* packed, const void* scale, int rows, int tokens, int row_stride,
+                                 int D, void* out, int8_t* codes, kivi_stream_t stream) {
+    if (rows < 0 || tokens < 0 || D <= 0 || D % BLK || row_stride < tokens) return KIVI_ERR_ARG;
+    const int64_t n = (int64_t)rows * tokens * (D / BLK);
+    if (n == 0) return KIVI_OK;
+    if (!packed || !scale || (!out && !codes)) return KIVI_ERR_ARG;
+    if ((uintptr_t)packed % 8 || (uintptr_t)scale % 2 || (uintptr_t)out % 16 || (uintptr_t)codes % 16)
+        return KIVI_ERR_ALIGN;
+    page_dequant_kernel<<<grid_for(n), 256, 0, (cudaStream_t)stream>>>(
+        packed, reinterpret_cast<const __half*>(scale), rows, tokens, row_stride, D / BLK,
+        reinterpret_cast<__nv_bfloat16*>(out), codes);
     return check_launch();
 }

@@ -26,7 +26,15 @@ _lock = threading.Lock()
 
 
 class KiviError(RuntimeError):
-    """A nonzero status returned by libkivi_sm100."""
+    """A nonzero status returned by libkivi_sm100 (or raised by a kernel
+    through the device error flag); `status` is the kivi_status code."""
+
+    def __init__(self, msg: str, status: int = 0):
+        super().__init__(msg)
+        self.status = status
+
+
+KIVI_ERR_TIMEOUT = 5
 
 
 def lib():
@@ -50,6 +58,7 @@ def lib():
             L.kivi_dequant.argtypes = [P, P, I, P, P, I, I, I, I, I, F, F, P, P, I64, I64, I64, P]
             L.kivi_roundtrip.argtypes = [P, P, I, I, I, I, I, I, I, P, I, P]
             L.kivi_calibrate.argtypes = [P, I64, I, I, P, I, P, P]
+            L.kivi_page_dequant.argtypes = [P, P, I, I, I, I, P, P, P]
             L.kivi_decode_workspace_floats.restype = I64
             L.kivi_decode_workspace_floats.argtypes = [I, I, I, I, I]
             L.kivi_decode.argtypes = [P, I64, I64, P, P, I, P, I, P, P, I, I, I, I, I, I, I, F, F, F,
@@ -80,6 +89,7 @@ def lib():
             L.kivi_paged_decode_workspace_floats.restype = I64
             L.kivi_paged_decode_workspace_floats.argtypes = [I, I, I, I64, I]
             L.kivi_paged_decode.argtypes = [P, I64, I64, P, I64, P, I64, P, I, I, I, I, I, F, P, P, I64, P, P]
+            L.kivi_paged_decode_f32.argtypes = [P, I64, I64, P, I64, P, I64, P, I, I, I, I, I, F, P, P, I64, P, P]
             _lib = L
     return _lib
 
@@ -89,7 +99,7 @@ def check(status: int, what: str) -> None:
         L = lib()
         msg = L.kivi_status_string(status).decode()
         extra = f" (cudaError {L.kivi_last_cuda_error()})" if status == 4 else ""
-        raise KiviError(f"{what}: {msg}{extra}")
+        raise KiviError(f"{what}: {msg}{extra}", status)
 
 
 def ptr(t):
@@ -149,6 +159,48 @@ def device_status(device) -> int:
     if v:
         e.zero_()
     return v
+
+
+def raise_device_status(device, what: str = "kernel") -> None:
+    """Synchronise the current stream and raise KiviError if a kernel set the
+    device error flag (a bounded wait that ran out); the flag is cleared."""
+    torch.cuda.current_stream(device).synchronize()
+    v = device_status(device)
+    if v:
+        raise KiviError(f"{what}: {lib().kivi_status_string(v).decode()}", v)
+
+
+_poll: dict = {}
+
+
+def poll_errors(device) -> None:
+    """Sync-free error check for per-step callers: copies the device error
+    flag into pinned host memory behind the work already queued on the
+    current stream, and raises KiviError for a flag whose copy (from an
+    earlier poll) has completed; a raised flag is cleared.  An error is thus
+    reported at most one poll after the step whose kernel set it has
+    finished, without ever blocking the host."""
+    if torch.cuda.is_current_stream_capturing():
+        return
+    key = device_index(device)
+    e = err_flag(device)
+    st = _poll.get(key)
+    if st is None:
+        st = {"host": torch.zeros(1, dtype=torch.int32).pin_memory(), "event": None}
+        _poll[key] = st
+    ev = st["event"]
+    if ev is not None and ev.query():
+        v = int(st["host"][0])
+        if v:
+            st["host"][0] = 0
+            st["event"] = None
+            e.zero_()
+            raise KiviError(f"device error flag: {lib().kivi_status_string(v).decode()}", v)
+    if ev is None or ev.query():
+        st["host"].copy_(e, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(device))
+        st["event"] = ev
 
 
 def workspace(device, n_floats: int) -> torch.Tensor:

@@ -44,7 +44,7 @@ def _stacked_geometry(st: dict) -> tuple[int, int, dict]:
 def decode_packed(q: Tensor, st: dict, n_qh: int, sm_scale: Optional[float] = None,
                   fmt: Optional[str] = None, g_k: Optional[float] = None, g_v: Optional[float] = None,
                   out: Optional[Tensor] = None, partial: bool = False, v_hot: Optional[Tensor] = None,
-                  exchange=None):
+                  exchange=None, check: bool = False):
     """Core entry: q [B, n_qh, D] bf16 over a stacked packed cache (B*H heads).
 
     Returns bf16 [B, n_qh, D], or with partial=True the merged per-row state
@@ -52,7 +52,18 @@ def decode_packed(q: Tensor, st: dict, n_qh: int, sm_scale: Optional[float] = No
     log-sum-exp merge.  With v_hot (bf16 [B*H, S % 16, D]) the tail tokens'
     V is taken unquantised like their K (caches that keep the partial page in
     bf16); v_packed then only has to cover the paged tokens, and the packed
-    tensors may be None when there is no full page yet."""
+    tensors may be None when there is no full page yet.
+
+    check=True synchronises after the launch and raises KiviError(status=5)
+    if a bounded device wait ran out (the sync-free alternative for per-step
+    callers is int4_kivi._native.poll_errors)."""
+    res = _decode_packed(q, st, n_qh, sm_scale, fmt, g_k, g_v, out, partial, v_hot, exchange)
+    if check:
+        N.raise_device_status(q.device, "decode")
+    return res
+
+
+def _decode_packed(q, st, n_qh, sm_scale, fmt, g_k, g_v, out, partial, v_hot, exchange):
     B, H, S, D = st["B"], st["H"], st["S"], st["D"]
     fmt = st.get("fmt", "int4") if fmt is None else fmt
     g_k = st.get("g_k", 1.0) if g_k is None else g_k

@@ -2,7 +2,8 @@
 
 Two regimes (the reference is single-GPU; these are B200-native additions):
   * sequence / kv-head sharding: independent decode per rank, no collective
-    (`shard_sequences` balances sequences by token count);
+    (`shard_sequences` balances sequences by token count, `shard_heads` deals
+    out kv-head groups, `plan_shards` combines the two for small batches);
   * sequence parallel for one long context (>= 128K tokens): the KV sequence
     is split in page-aligned contiguous ranges (`split_tokens`), each rank
     decodes its range to a partial softmax state (m, l, acc), and the states
@@ -45,6 +46,45 @@ def shard_sequences(lengths: Sequence[int], world: int) -> list[list[int]]:
     return out
 
 
+def shard_heads(Hkv: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous kv-head range [h0, h1) of `rank` when the kv heads of every
+    sequence are dealt out over `world` ranks (KV-head-group sharding).  Each
+    rank decodes its kv heads and the GQA query heads that read them
+    (q heads [h0*G, h1*G)), which needs no communication for the attention op:
+    the reference's GQA kernel is one program per (sequence, kv head, split),
+    int4_kivi/decode.py:466-472, so kv heads are independent.  With more
+    ranks than heads the surplus ranks get an empty range."""
+    if Hkv <= 0 or world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad shard request Hkv={Hkv} world={world} rank={rank}")
+    return Hkv * rank // world, Hkv * (rank + 1) // world
+
+
+def plan_shards(lengths: Sequence[int], Hkv: int, world: int) -> list[list[tuple[int, int, int]]]:
+    """Units of decode work per rank as (sequence, h0, h1) triples, sharding by
+    sequence and, when there are fewer sequences than ranks, by kv-head group
+    too: every sequence's kv heads are split into f equal groups, f the
+    smallest power of two (dividing Hkv) with len(lengths) * f >= world, and
+    the (sequence, group) units are assigned longest-first to the least
+    loaded rank (load = tokens x heads = packed bytes).  No unit needs data
+    from another rank."""
+    B = len(lengths)
+    f = 1
+    while B * f < world and f * 2 <= Hkv and Hkv % (f * 2) == 0:
+        f *= 2
+    hg = Hkv // f
+    units = [(b, j * hg, (j + 1) * hg) for b in range(B) for j in range(f)]
+    units.sort(key=lambda u: (-lengths[u[0]], u[0], u[1]))
+    loads = [0] * world
+    out: list[list[tuple[int, int, int]]] = [[] for _ in range(world)]
+    for u in units:
+        r = min(range(world), key=lambda j: (loads[j], j))
+        out[r].append(u)
+        loads[r] += lengths[u[0]] * (u[2] - u[1])
+    for o in out:
+        o.sort()
+    return out
+
+
 def merge_partials_torch(m: torch.Tensor, l: torch.Tensor, acc: torch.Tensor) -> torch.Tensor:
     """Reference math of the merge (m in log2 units) for host-side checks:
     m/l [R, rows], acc [R, rows, D] -> fp32 [rows, D]."""
@@ -74,12 +114,18 @@ class _PeerBuffers:
         with torch.cuda.device(self.device):
             self.own = ctypes.c_void_p()
             handle = (ctypes.c_char * 64)()
-            N.check(L.kivi_peer_alloc(nbytes, ctypes.byref(self.own), handle), "kivi_peer_alloc")
             self.opened = []
+            failure = None
             try:
-                handles = [None] * self.world
-                dist.all_gather_object(handles, bytes(handle), group=self.group)
-                ptrs = []
+                N.check(L.kivi_peer_alloc(nbytes, ctypes.byref(self.own), handle), "kivi_peer_alloc")
+            except Exception as ex:      # still take part in the gathers below
+                failure = ex
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle) if failure is None else None, group=self.group)
+            ptrs = []
+            try:
+                if failure is not None or any(h is None for h in handles):
+                    raise failure or RuntimeError("a peer could not allocate its exchange buffer")
                 for j, hj in enumerate(handles):
                     if j == self.rank:
                         ptrs.append(self.own.value)
@@ -89,9 +135,19 @@ class _PeerBuffers:
                             "kivi_peer_open")
                     self.opened.append(pj)
                     ptrs.append(pj.value)
-            except BaseException:
-                self._release()          # no peer has read this rank's buffer yet
-                raise
+            except Exception as ex:      # reported to every rank below
+                failure = ex
+            # Every rank learns whether every open succeeded, so all of them
+            # release their buffers and raise together; no rank is left
+            # waiting in a later barrier for one that gave up.  Nothing has
+            # read any exchange buffer yet: kernels run only after __init__.
+            oks = [None] * self.world
+            dist.all_gather_object(oks, failure is None, group=self.group)
+            if not all(oks):
+                self._release()
+                if failure is not None:
+                    raise failure
+                raise RuntimeError(f"kivi_peer_open failed on rank(s) {[j for j, o in enumerate(oks) if not o]}")
         self.closed = False
         self.peers = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
         self.timeout_ns = int(timeout_s * 1e9)

@@ -256,6 +256,14 @@ class Int4KiviCache(Cache):
                   for lt in layer_types]
         super().__init__(layers=layers)
 
+    def update(self, key_states: Tensor, value_states: Tensor, layer_idx: int, *args, **kwargs):
+        if layer_idx == 0 and key_states.is_cuda:
+            # once per forward step: raise a device error flag set by an
+            # earlier step's kernels (sync-free, see _native.poll_errors)
+            from . import _native
+            _native.poll_errors(key_states.device)
+        return super().update(key_states, value_states, layer_idx, *args, **kwargs)
+
     def nbytes(self) -> int:
         return sum(l.nbytes() for l in self.layers)
 
@@ -287,14 +295,21 @@ def kivi_attention_forward(module, query: Tensor, key: Tensor, value: Tensor, at
     return out[:, None].to(query.dtype), None             # [B, q_len, Hq, D]
 
 
+_mask_memo: list = [None, -1, True]   # [mask tensor of the last check, its version, its result]
+
+
 def _attends_all(mask) -> bool:
     """True when `mask` (None, bool where True attends, or additive float)
-    hides no key position."""
+    hides no key position.  Every layer of one forward step gets the same
+    mask tensor, so the answer (which needs a device-to-host read) is
+    computed once per step and reused for the other layers."""
     if mask is None:
         return True
-    if mask.dtype == torch.bool:
-        return bool(mask.all())
-    return bool((mask == 0).all())
+    if _mask_memo[0] is mask and _mask_memo[1] == mask._version:
+        return _mask_memo[2]
+    ok = bool(mask.all()) if mask.dtype == torch.bool else bool((mask == 0).all())
+    _mask_memo[:] = [mask, mask._version, ok]
+    return ok
 
 
 def enable_fused_decode(model) -> None:

@@ -123,10 +123,13 @@ def _decode(fmt, q, kv_cache, block_table, seq_lens, sm_scale, out=None):
         sm_scale = 1.0 / math.sqrt(D)
     if out is None:
         out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=q.device)
+    if out.shape != (B, Hq, D) or out.dtype not in (torch.bfloat16, torch.float32) or not out.is_contiguous():
+        raise ValueError(f"out must be contiguous bf16 or fp32 [{B}, {Hq}, {D}]")
     L = N.lib()
     need = L.kivi_paged_decode_workspace_floats(B, Hq, H, bt.shape[1], D)
     work = N.workspace(q.device, need)
-    N.check(L.kivi_paged_decode(N.ptr(q), q.stride(0), q.stride(1), N.ptr(kv_cache), kv_cache.shape[0], N.ptr(bt),
+    entry = L.kivi_paged_decode if out.dtype == torch.bfloat16 else L.kivi_paged_decode_f32
+    N.check(entry(N.ptr(q), q.stride(0), q.stride(1), N.ptr(kv_cache), kv_cache.shape[0], N.ptr(bt),
                                 bt.shape[1], N.ptr(sl), B, Hq, H, D, N.FMT[fmt], float(sm_scale), N.ptr(out),
                                 N.ptr(work), work.numel(), N.ptr(N.err_flag(q.device)), N.stream_of(q)),
             f"{fmt}_kivi_paged_decode")
@@ -145,7 +148,8 @@ def int4_kivi_gather_dequant(kv_cache, block_table, seq_lens, head_size, num_kv_
 
 
 def int4_kivi_paged_decode(q, kv_cache, block_table, seq_lens, sm_scale=None, out=None):
-    """One decode token per sequence: q bf16 [B, Hq, D] -> bf16 [B, Hq, D]."""
+    """One decode token per sequence: q bf16 [B, Hq, D] -> bf16 [B, Hq, D]
+    (or, given an fp32 `out`, the normalised output before the bf16 cast)."""
     return _decode("int4", q, kv_cache, block_table, seq_lens, sm_scale, out)
 
 

@@ -158,8 +158,53 @@ def sweep_tensor(x: Tensor, n_alphas: int = 32) -> dict:
 
 
 # ------------------------- legacy page-level cache API -------------------------
+# The reference's first cache design (kv_quant.py:37-169): per-token 16-channel
+# blocks for both K and V, int8 codes, fp16 scales, pages of `page_size`
+# tokens plus an unquantised hot tail.  Here every quantisation is one
+# kivi_store launch (its per-token path, the same blocks and calibration) and
+# every dequantisation one kivi_page_dequant launch; a layer keeps its pages in
+# two capacity-backed device buffers instead of a list of per-page tensors.
+
+
+def _store_tokens(x: Tensor, use_mse: bool, n_alphas: int, packed: Tensor, scale: Tensor, tok0: int) -> None:
+    """Quantise rows x [R, T, D] (per token, 16-channel blocks) into packed
+    [R, cap, D/16, 8] / scale fp16 [R, cap, D/16] at token tok0."""
+    R, T, D = x.shape
+    if T == 0:
+        return
+    if x.dtype not in N.DTYPE:
+        x = x.float()
+    calib = N.CALIB["mse" if use_mse else "absmax"]
+    al = N.alphas(x.device, n_alphas)
+    sv = x.stride()
+    N.check(N.lib().kivi_store(None, N.ptr(x), N.DTYPE[x.dtype], 0, 0, 0, sv[0], sv[1], sv[2], R, 0, T, D,
+                               N.FMT["int4"], calib, calib, N.ptr(al), n_alphas, 1.0, 1.0, None, None, 0, 0,
+                               N.ptr(packed), N.ptr(scale), tok0, packed.shape[1], N.stream_of(x)),
+            "kivi_store")
+
+
+def _page_dequant(packed: Tensor, scale: Tensor, tokens: int, values: bool = True, codes: bool = False):
+    """bf16 values and/or int8 codes [R, tokens, D] of the first `tokens`
+    tokens of packed [R, cap, D/16, 8] / scale [R, cap, D/16]."""
+    R, cap, ND, _ = packed.shape
+    D = ND * BLOCK
+    out = torch.empty(R, tokens, D, dtype=torch.bfloat16, device=packed.device) if values else None
+    cod = torch.empty(R, tokens, D, dtype=torch.int8, device=packed.device) if codes else None
+    N.check(N.lib().kivi_page_dequant(N.ptr(packed), N.ptr(scale), R, tokens, cap, D, N.ptr(out), N.ptr(cod),
+                                      N.stream_of(packed)), "kivi_page_dequant")
+    return out, cod
+
+
+def _pack_codes(c: Tensor) -> Tensor:
+    """int8 codes [..., D] -> packed nibbles [..., D/16, 8] (element 2j low)."""
+    u = c.to(torch.uint8) & 0xF
+    return (u[..., 0::2] | (u[..., 1::2] << 4)).reshape(*c.shape[:-1], c.shape[-1] // BLOCK, BLOCK // 2)
+
+
 @dataclasses.dataclass
 class QuantizedPage:
+    """One quantised page (kv_quant.py:45-68): int8 codes [H, T, D] and fp16
+    scales [H, T, D/16] for K and V, and the page's first token position."""
     k_int4: Tensor
     v_int4: Tensor
     k_scale: Tensor
@@ -167,74 +212,136 @@ class QuantizedPage:
     start_pos: int
 
     def dequantize(self) -> tuple[Tensor, Tensor]:
-        def _deq(q: Tensor, scale: Tensor) -> Tensor:
-            sf = scale.unsqueeze(-1).expand(*scale.shape, BLOCK).reshape(*q.shape)
-            return dequantize_block(q, sf).to(torch.bfloat16)
-        return _deq(self.k_int4, self.k_scale), _deq(self.v_int4, self.v_scale)
+        """bf16 K, V [H, T, D]: bf16(fp16(code * scale)), one kernel launch."""
+        H, T, D = self.k_int4.shape
+        dev = _device_of(self.k_int4)
+        codes = torch.cat([self.k_int4, self.v_int4]).to(dev)
+        packed = _pack_codes(codes).contiguous()
+        sc = torch.cat([self.k_scale, self.v_scale]).to(dev, torch.float16).contiguous()
+        out, _ = _page_dequant(packed, sc, T)
+        out = out.to(self.k_int4.device)
+        return out[:H], out[H:]
 
     def mem_bytes(self) -> int:
-        return 2 * (self.k_int4.numel() // 2 + self.k_scale.numel() * 2)
+        """Bytes at 4-bit codes plus fp16 scales, K and V."""
+        codes = self.k_int4.numel() // 2
+        scales = self.k_scale.numel() * 2
+        return 2 * (codes + scales)
 
     def bf16_bytes(self) -> int:
-        return self.k_int4.numel() * 2 * 2
+        """Bytes of the same K and V in bf16."""
+        return 2 * 2 * self.k_int4.numel()
 
 
 def quantize_page(k: Tensor, v: Tensor, start_pos: int, use_mse: bool = True, n_alphas: int = 32) -> QuantizedPage:
-    """One page k, v [n_heads, page_tokens, head_dim] (kv_quant.py:72-84)."""
-    n_heads, page_tokens, head_dim = k.shape
-    kf = k.float().reshape(n_heads, page_tokens, head_dim // BLOCK, BLOCK)
-    vf = v.float().reshape(n_heads, page_tokens, head_dim // BLOCK, BLOCK)
-    calib = "mse" if use_mse else "absmax"
-    ks = _calibrate(kf, 7.0, _q_int4, calib, n_alphas)
-    vs = _calibrate(vf, 7.0, _q_int4, calib, n_alphas)
-    k_q = quantize_block(kf, ks).reshape(n_heads, page_tokens, head_dim)
-    v_q = quantize_block(vf, vs).reshape(n_heads, page_tokens, head_dim)
-    return QuantizedPage(k_q, v_q, ks.squeeze(-1).to(torch.float16), vs.squeeze(-1).to(torch.float16), start_pos)
+    """Quantise one page k, v [n_heads, page_tokens, head_dim] (kv_quant.py:71-84):
+    per-token 16-channel blocks, absmax or MSE scale, codes from the fp32 scale,
+    scales stored as fp16.  K and V go through one store launch."""
+    H, T, D = k.shape
+    dev = _device_of(k)
+    x = torch.cat([k, v]).to(dev)
+    packed = torch.empty(2 * H, T, D // BLOCK, BLOCK // 2, dtype=torch.uint8, device=dev)
+    scale = torch.empty(2 * H, T, D // BLOCK, dtype=torch.float16, device=dev)
+    _store_tokens(x, use_mse, n_alphas, packed, scale, 0)
+    _, codes = _page_dequant(packed, scale, T, values=False, codes=True)
+    codes, scale = codes.to(k.device), scale.to(k.device)
+    return QuantizedPage(codes[:H], codes[H:], scale[:H], scale[H:], start_pos)
 
 
 class QuantizedKVLayer:
+    """Pages of one layer (kv_quant.py:87-131).  Complete pages are quantised
+    straight into capacity-backed device buffers [2, H, cap, D/16, 8] (K rows
+    0..H-1, V rows H..2H-1), one store launch per append; the tokens of the
+    unfinished page stay in `hot_k` / `hot_v` as given."""
+
     def __init__(self, page_size: int = PAGE, use_mse: bool = True, n_alphas: int = 32) -> None:
         self.page_size = page_size
         self.use_mse = use_mse
         self.n_alphas = n_alphas
-        self.pages: list[QuantizedPage] = []
+        self.n_pages = 0
+        self._packed: Optional[Tensor] = None
+        self._scale: Optional[Tensor] = None
         self.hot_k: Optional[Tensor] = None
         self.hot_v: Optional[Tensor] = None
 
+    def _reserve(self, H: int, tokens: int, D: int, device) -> None:
+        cap = self._packed.shape[1] if self._packed is not None else 0
+        if tokens <= cap:
+            return
+        new_cap = max(tokens, 2 * cap, 4 * self.page_size)
+        packed = torch.empty(2 * H, new_cap, D // BLOCK, BLOCK // 2, dtype=torch.uint8, device=device)
+        scale = torch.empty(2 * H, new_cap, D // BLOCK, dtype=torch.float16, device=device)
+        if cap:
+            packed[:, :cap].copy_(self._packed)
+            scale[:, :cap].copy_(self._scale)
+        self._packed, self._scale = packed, scale
+
     def append(self, k: Tensor, v: Tensor) -> None:
-        self.hot_k = torch.cat([self.hot_k, k], dim=1) if self.hot_k is not None else k
-        self.hot_v = torch.cat([self.hot_v, v], dim=1) if self.hot_v is not None else v
-        while self.hot_k.shape[1] >= self.page_size:
-            start = len(self.pages) * self.page_size
-            self.pages.append(quantize_page(self.hot_k[:, :self.page_size], self.hot_v[:, :self.page_size],
-                                            start, self.use_mse, self.n_alphas))
-            self.hot_k = self.hot_k[:, self.page_size:]
-            self.hot_v = self.hot_v[:, self.page_size:]
+        """k, v: [n_kv_heads, new_tokens, head_dim]."""
+        self.hot_k = k if self.hot_k is None else torch.cat([self.hot_k, k], dim=1)
+        self.hot_v = v if self.hot_v is None else torch.cat([self.hot_v, v], dim=1)
+        n_new = self.hot_k.shape[1] // self.page_size * self.page_size
+        if n_new == 0:
+            return
+        H, _, D = self.hot_k.shape
+        dev = _device_of(self.hot_k)
+        t0 = self.n_pages * self.page_size
+        self._reserve(H, t0 + n_new, D, dev)
+        x = torch.cat([self.hot_k[:, :n_new], self.hot_v[:, :n_new]]).to(dev)
+        _store_tokens(x, self.use_mse, self.n_alphas, self._packed, self._scale, t0)
+        self.n_pages += n_new // self.page_size
+        self.hot_k = self.hot_k[:, n_new:]
+        self.hot_v = self.hot_v[:, n_new:]
+
+    @property
+    def pages(self) -> list[QuantizedPage]:
+        """The stored pages as QuantizedPage records (materialised on access)."""
+        if not self.n_pages:
+            return []
+        H = self._packed.shape[0] // 2
+        _, codes = _page_dequant(self._packed, self._scale, self.n_pages * self.page_size, values=False,
+                                 codes=True)
+        P = self.page_size
+        return [QuantizedPage(codes[:H, i * P:(i + 1) * P], codes[H:, i * P:(i + 1) * P],
+                              self._scale[:H, i * P:(i + 1) * P], self._scale[H:, i * P:(i + 1) * P], i * P)
+                for i in range(self.n_pages)]
 
     def get_kv(self) -> tuple[Tensor, Tensor]:
-        if not self.pages:
+        """bf16 K, V [n_kv_heads, seq_len, head_dim]: dequantised pages, then the hot tail."""
+        if not self.n_pages:
             if self.hot_k is None:
                 raise ValueError("Cache is empty")
             return self.hot_k.bfloat16(), self.hot_v.bfloat16()
-        parts_k, parts_v = zip(*(p.dequantize() for p in self.pages))
-        k = torch.cat(list(parts_k), dim=1)
-        v = torch.cat(list(parts_v), dim=1)
-        if self.hot_k is not None and self.hot_k.shape[1] > 0:
-            k = torch.cat([k, self.hot_k.bfloat16()], dim=1)
-            v = torch.cat([v, self.hot_v.bfloat16()], dim=1)
+        H = self._packed.shape[0] // 2
+        out, _ = _page_dequant(self._packed, self._scale, self.n_pages * self.page_size)
+        k, v = out[:H], out[H:]
+        if self.hot_k is not None and self.hot_k.shape[1]:
+            k = torch.cat([k, self.hot_k.to(k.device, torch.bfloat16)], dim=1)
+            v = torch.cat([v, self.hot_v.to(v.device, torch.bfloat16)], dim=1)
         return k, v
 
     def seq_len(self) -> int:
-        hot = self.hot_k.shape[1] if self.hot_k is not None else 0
-        return len(self.pages) * self.page_size + hot
+        return self.n_pages * self.page_size + (self.hot_k.shape[1] if self.hot_k is not None else 0)
+
+    def _page_elems(self) -> int:
+        return self._packed.shape[0] // 2 * self.n_pages * self.page_size * self._packed.shape[2] * BLOCK \
+            if self.n_pages else 0
 
     def mem_bytes(self) -> int:
-        hot_cost = self.hot_k.numel() * 2 * 2 if self.hot_k is not None else 0
-        return sum(p.mem_bytes() for p in self.pages) + hot_cost
+        """4-bit codes + fp16 scales of the pages (K and V) plus the hot tail at 2 B per element."""
+        e = self._page_elems()
+        hot = 2 * 2 * self.hot_k.numel() if self.hot_k is not None else 0
+        return 2 * (e // 2 + (e // BLOCK) * 2) + hot
+
+    def bf16_bytes(self) -> int:
+        """The same tokens (pages and hot tail, K and V) at bf16."""
+        hot = self.hot_k.numel() if self.hot_k is not None else 0
+        return 2 * 2 * (self._page_elems() + hot)
 
 
 class QuantizedKVCache:
-    """Per-layer paged cache with the reference's `update`/`get_kv` contract."""
+    """Per-layer paged cache with the reference's `update` / `get_kv` contract
+    (kv_quant.py:134-167; batch 1, k/v [1, n_kv_heads, new_tokens, head_dim])."""
 
     def __init__(self, page_size: int = PAGE, use_mse: bool = True, n_alphas: int = 32) -> None:
         self.page_size = page_size
@@ -243,43 +350,42 @@ class QuantizedKVCache:
         self.layers: list[QuantizedKVLayer] = []
 
     def _ensure(self, layer_idx: int) -> None:
-        while len(self.layers) <= layer_idx:
-            self.layers.append(QuantizedKVLayer(self.page_size, self.use_mse, self.n_alphas))
+        self.layers.extend(QuantizedKVLayer(self.page_size, self.use_mse, self.n_alphas)
+                           for _ in range(layer_idx + 1 - len(self.layers)))
 
     def update(self, layer_idx: int, k: Tensor, v: Tensor) -> None:
         self._ensure(layer_idx)
         self.layers[layer_idx].append(k.squeeze(0), v.squeeze(0))
 
     def get_kv(self, layer_idx: int) -> tuple[Tensor, Tensor]:
+        """bf16 [1, n_kv_heads, seq_len, head_dim] K and V of one layer."""
         k, v = self.layers[layer_idx].get_kv()
-        return k.unsqueeze(0), v.unsqueeze(0)
+        return k[None], v[None]
 
     def mem_bytes(self) -> int:
-        return sum(l.mem_bytes() for l in self.layers)
+        return sum(layer.mem_bytes() for layer in self.layers)
 
     def bf16_bytes(self) -> int:
-        total = 0
-        for layer in self.layers:
-            total += sum(p.bf16_bytes() for p in layer.pages)
-            if layer.hot_k is not None:
-                total += layer.hot_k.numel() * 2 * 2
-        return total
+        return sum(layer.bf16_bytes() for layer in self.layers)
 
     def compression_ratio(self) -> float:
         return self.bf16_bytes() / max(self.mem_bytes(), 1)
 
 
 def measure_page_error(k: Tensor, page_size: int = PAGE, n_alphas: int = 32) -> dict:
-    """Absmax vs MSE-optimal reconstruction error over complete pages (kv_quant.py:147-169)."""
-    n_heads, seq_len, head_dim = k.shape
-    abs_errs, opt_errs = [], []
-    for i in range(seq_len // page_size):
-        page = k[:, i * page_size:(i + 1) * page_size].float()
-        pg = page.reshape(n_heads, page_size, head_dim // BLOCK, BLOCK)
-        for calib, errs in (("absmax", abs_errs), ("mse", opt_errs)):
-            s = _calibrate(pg, 7.0, _q_int4, calib, n_alphas)
-            errs.append(((pg - dequantize_block(quantize_block(pg, s), s)) ** 2).mean().item())
-    absmax_mse = float(sum(abs_errs) / max(len(abs_errs), 1))
-    optimal_mse = float(sum(opt_errs) / max(len(opt_errs), 1))
-    return {"absmax_mse": absmax_mse, "optimal_mse": optimal_mse,
-            "reduction_pct": 100.0 * (absmax_mse - optimal_mse) / max(absmax_mse, 1e-12)}
+    """Absmax vs MSE-optimal reconstruction error over complete pages
+    (kv_quant.py:170-191): the mean over pages of each page's mean squared
+    error, with fp32 scales.  Each calibration is one kivi_roundtrip launch
+    (per-token 16-channel blocks) over all complete pages at once."""
+    H, S, D = k.shape
+    P = S // page_size
+    if P == 0:
+        return {"absmax_mse": 0.0, "optimal_mse": 0.0, "reduction_pct": 0.0}
+    x = k[:, :P * page_size].float()
+    res = {}
+    for calib in ("absmax", "mse"):
+        d = (x - roundtrip(x, "int4", "headdim", calib, n_alphas)).pow(2)
+        per_page = d.reshape(H, P, page_size * D).transpose(0, 1).reshape(P, -1).mean(dim=1)
+        res[calib] = float(per_page.double().mean().item())
+    a, o = res["absmax"], res["mse"]
+    return {"absmax_mse": a, "optimal_mse": o, "reduction_pct": 100.0 * (a - o) / max(a, 1e-12)}

@@ -49,3 +49,43 @@ def cuda_dev():
     if not torch.cuda.is_available():
         pytest.skip("needs CUDA")
     return torch.device("cuda:0")
+
+
+# ---------------------------------------------------------------------------
+# The decode bar, one definition for every decode path (contiguous, varlen,
+# paged, the fused hf read path, multi-GPU), against the oracle's
+# double-precision attention on the same dequantised values:
+#   * fp32 state (the normalised output before the bf16 cast):
+#       max-abs <= 2e-3 and relative RMS <= 1e-3;
+#   * bf16 output: relative RMS <= 1e-3 against the oracle rounded to bf16,
+#       and elementwise |out - ref| <= 2e-3 + |ref| * 2^-8 (the fp32 bar plus
+#       one bf16 rounding step of the value).
+# ---------------------------------------------------------------------------
+FP32_MAX_ABS, REL_RMS = 2e-3, 1e-3
+
+
+def _f64(x):
+    import torch
+    if isinstance(x, torch.Tensor):
+        return x.detach().cpu().double().numpy()
+    return np.asarray(x, dtype=np.float64)
+
+
+def check_decode_fp32(got, ref, what=""):
+    g, r = _f64(got), _f64(ref)
+    err = np.abs(g - r).max() if g.size else 0.0
+    rel = np.sqrt(((g - r) ** 2).sum() / max((r ** 2).sum(), 1e-300))
+    assert err <= FP32_MAX_ABS and rel <= REL_RMS, f"{what} fp32 max-abs {err:.3e} rel-rms {rel:.3e}"
+    return err, rel
+
+
+def check_decode_bf16(got, ref, what=""):
+    import torch
+    g, r = _f64(got), _f64(ref)
+    rb = torch.from_numpy(r).to(torch.bfloat16).double().numpy()
+    err = np.abs(g - r)
+    ok = err <= 2e-3 + np.abs(r) * 2.0 ** -8
+    assert bool(ok.all()), f"{what} bf16 max-abs {err.max():.3e} ({int((~ok).sum())} elements over the bound)"
+    rel = np.sqrt(((g - rb) ** 2).sum() / max((r ** 2).sum(), 1e-300))
+    assert rel <= REL_RMS, f"{what} bf16 rel-rms {rel:.3e} vs the bf16-rounded oracle"
+    return float(err.max()) if err.size else 0.0, rel

@@ -15,6 +15,10 @@ Everything here is computed by the reference's OWN Python code on CPU:
   * the paged cache's e4m3 MSE calibration `fp8` / `mse_scale` / `rt`
     (scripts/diag_kernel_perchannel.py:30-53), taken from the script's source
     text (its module-level vLLM import and GPU code are not executed)
+  * the legacy page-level API quantize_page / QuantizedPage /
+    QuantizedKVCache / measure_page_error                       (kv_quant.py:37-191)
+  * the reference test's heavy-tailed K (randn**3) through `_ref_codes`
+    and roundtrip                                                (tests/test_int4_kivi.py:43-56)
 
 The only code of ours is the nibble packer (element 2j -> low nibble of byte j,
 int4_kivi/triton_kernels.py:21-24) and the input generator.
@@ -187,6 +191,68 @@ def main():
         "chan_deq": ns["rt"](chan, s_ch).numpy(),
     }
     np.savez_compressed(os.path.join(HERE, "paged_calib.npz"), **paged)
+
+    # ---------------- 6. legacy page-level API (kv_quant.py:37-191) ---------
+    leg = {}
+    k, v, _ = gen_kv(2, 48, 64, seed=21)
+    leg["k"], leg["v"] = bits16(k), bits16(v)
+    for use_mse in (False, True):
+        tag = "mse" if use_mse else "absmax"
+        pg = kv_quant.quantize_page(k[:, :16], v[:, :16], 0, use_mse=use_mse)
+        leg[f"page_{tag}_k_int4"] = pg.k_int4.numpy()
+        leg[f"page_{tag}_v_int4"] = pg.v_int4.numpy()
+        leg[f"page_{tag}_k_scale"] = bits16(pg.k_scale)
+        leg[f"page_{tag}_v_scale"] = bits16(pg.v_scale)
+        kd, vd = pg.dequantize()
+        leg[f"page_{tag}_k_deq"], leg[f"page_{tag}_v_deq"] = bits16(kd), bits16(vd)
+        leg[f"page_{tag}_mem"] = np.array([pg.mem_bytes(), pg.bf16_bytes()])
+    # fp32 input page (the calibration sees the full fp32 values)
+    xf = torch.randn(2, 16, 64, generator=torch.Generator().manual_seed(4)) * 3
+    leg["f32_k"], leg["f32_v"] = xf.numpy(), (xf * 0.5).numpy()
+    pg = kv_quant.quantize_page(xf, xf * 0.5, 0, use_mse=True, n_alphas=7)
+    leg["f32_k_int4"], leg["f32_k_scale"] = pg.k_int4.numpy(), bits16(pg.k_scale)
+    leg["f32_v_int4"], leg["f32_v_scale"] = pg.v_int4.numpy(), bits16(pg.v_scale)
+    # a two-layer cache fed in ragged appends (5, 20, 1, 13, 9 tokens = 48)
+    cache = kv_quant.QuantizedKVCache()
+    t = 0
+    for n in (5, 20, 1, 13, 9):
+        for layer in (0, 1):
+            sc = 1.0 if layer == 0 else 0.25
+            cache.update(layer, (k[None, :, t:t + n] * sc).bfloat16(), (v[None, :, t:t + n] * sc).bfloat16())
+        t += n
+        kk, vv = cache.get_kv(1)
+        leg[f"cache_t{t}_k"], leg[f"cache_t{t}_v"] = bits16(kk), bits16(vv)
+        leg[f"cache_t{t}_mem"] = np.array([cache.mem_bytes(), cache.bf16_bytes()])
+        leg[f"cache_t{t}_ratio"] = np.array([cache.compression_ratio()])
+        leg[f"cache_t{t}_len"] = np.array([cache.layers[1].seq_len()])
+    kk, vv = cache.get_kv(0)
+    leg["cache_l0_k"], leg["cache_l0_v"] = bits16(kk), bits16(vv)
+    xe = (torch.randn(4, 80, 128, generator=torch.Generator().manual_seed(6)) *
+          torch.exp(torch.empty(1, 1, 128).uniform_(-1.0, 2.0, generator=torch.Generator().manual_seed(7))))
+    leg["err_x"] = xe.numpy()
+    e = kv_quant.measure_page_error(xe)
+    leg["err"] = np.array([e["absmax_mse"], e["optimal_mse"], e["reduction_pct"]])
+    np.savez_compressed(os.path.join(HERE, "legacy_page.npz"), **leg)
+
+    # ------- 7. heavy-tailed K (randn**3, tests/test_int4_kivi.py:51-56) -------
+    # the reference test's input distribution, drawn here on the CPU generator;
+    # codes and scales from the reference test's recipe (`_ref_codes`)
+    ht = {}
+    g = torch.Generator().manual_seed(0)
+    k = (torch.randn(2, 72, 128, generator=g) ** 3).to(torch.bfloat16)
+    v = torch.randn(2, 72, 128, generator=g).to(torch.bfloat16)
+    ht["k"], ht["v"] = bits16(k), bits16(v)
+    for calib in ("absmax", "mse"):
+        kb = _to_blocks(k[:, :64], "channel").float()
+        ks = _calibrate(kb, qmax, qfn, calib)
+        vb = _to_blocks(v, "headdim").float()
+        vs = _calibrate(vb, qmax, qfn, calib)
+        ht[f"{calib}_k_packed"] = pack_codes(qfn(kb / ks))
+        ht[f"{calib}_k_scale"] = bits16(ks[..., 0].to(torch.float16))
+        ht[f"{calib}_v_packed"] = pack_codes(qfn(vb / vs))
+        ht[f"{calib}_v_scale"] = bits16(vs[..., 0].to(torch.float16))
+        ht[f"{calib}_k_rt"] = bits16(kv_quant.roundtrip(k, "int4", "channel", calib))
+    np.savez_compressed(os.path.join(HERE, "heavy_tail.npz"), **ht)
     print("golden fixtures written to", HERE)
 
 

@@ -1,12 +1,11 @@
 """GPU parity tests: libkivi_sm100 (through the package API and its C ABI)
 against the CPU oracle on identical seeded inputs.
 
-Bars (written per test):
+Bars:
   * codes, scales, dequantised K/V, roundtrip outputs: bit-exact;
-  * decode attention, fp32 state (partial path): max-abs <= 2e-3 and
-    relative RMS <= 1e-3 vs the oracle's double-precision attention;
-  * decode attention, bf16 output: |out - ref| <= 2e-3 + |ref| * 2^-8 (one bf16
-    rounding step on top of the fp32 bar).
+  * decode attention: the one decode bar of conftest.py (fp32 state max-abs
+    <= 2e-3 and relative RMS <= 1e-3; bf16 output relative RMS <= 1e-3 vs the
+    bf16-rounded oracle and |out - ref| <= 2e-3 + |ref| * 2^-8).
 Mirrors the reference's tests/test_int4_kivi.py cases (code parity S in
 {256, 512, 2048} x {absmax, mse}, dequant vs roundtrip, hot page S=40, memory
 ratio) with the tolerance tightened to exact.
@@ -18,7 +17,7 @@ import pytest
 import torch
 
 import oracle
-from conftest import gen_kv
+from conftest import check_decode_bf16, check_decode_fp32, gen_kv
 
 pytestmark = pytest.mark.gpu
 
@@ -153,15 +152,8 @@ def _store(fmt, k, v, dev, calib="mse", g=1.0):
     return store_nvfp4_kivi(k.to(dev), v.to(dev), calib, calib, g_k=g, g_v=g)
 
 
-def _check_fp32(got, ref):
-    err = (got - ref).abs().max().item()
-    rel = ((got - ref).norm() / ref.norm()).item()
-    assert err <= 2e-3 and rel <= 1e-3, f"max-abs {err:.3e} rel-rms {rel:.3e}"
-
-
-def _check_bf16(got, ref):
-    err = (got.float() - ref).abs()
-    assert bool((err <= 2e-3 + ref.abs() * 2.0 ** -8).all()), f"max-abs {err.max().item():.3e}"
+_check_fp32 = check_decode_fp32
+_check_bf16 = check_decode_bf16
 
 
 @pytest.mark.parametrize("fmt", ["int4", "nvfp4"])

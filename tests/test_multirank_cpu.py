@@ -10,7 +10,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from int4_kivi.distributed import merge_partials_torch, shard_sequences, split_tokens
+from int4_kivi.distributed import merge_partials_torch, plan_shards, shard_heads, shard_sequences, split_tokens
 
 
 def test_split_tokens_page_aligned():
@@ -67,3 +67,58 @@ def test_gloo_sequence_parallel_merge():
     ref = torch.softmax((q.double() @ k.double().T) / math.sqrt(D), -1) @ v.double()
     for r in range(2):
         assert (ret[r].double() - ref).abs().max().item() < 1e-5
+
+
+def test_shard_heads_cover_all_heads():
+    for Hkv in (1, 4, 8, 16):
+        for W in (1, 2, 4, 8, 16):
+            rs = [shard_heads(Hkv, W, r) for r in range(W)]
+            assert rs[0][0] == 0 and rs[-1][1] == Hkv
+            assert all(b == c for (_, b), (c, _) in zip(rs, rs[1:]))
+            assert max(b - a for a, b in rs) - min(b - a for a, b in rs) <= 1
+    with pytest.raises(ValueError):
+        shard_heads(8, 2, 2)
+
+
+def test_plan_shards_uses_every_rank():
+    """Batches smaller than the world split kv heads so every rank has work;
+    every (sequence, head) is decoded exactly once."""
+    rng = np.random.default_rng(1)
+    for B in (1, 2, 3, 4, 8, 64):
+        lens = rng.integers(1024, 32769, size=B).tolist()
+        for W in (1, 2, 4, 8):
+            plan = plan_shards(lens, 8, W)
+            cover = sorted((b, h) for units in plan for (b, h0, h1) in units for h in range(h0, h1))
+            assert cover == [(b, h) for b in range(B) for h in range(8)]
+            if B * 8 >= W:
+                assert all(plan), (B, W, plan)
+
+
+def _heads_worker(rank, world, port, q, k, v, ret):
+    """Attention of this rank's kv-head range only (no collective on the data
+    path); the host gathers the pieces only to check them."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    Hkv, G = k.shape[0], q.shape[0] // k.shape[0]
+    h0, h1 = shard_heads(Hkv, world, rank)
+    outs = []
+    for h in range(h0, h1):
+        for j in range(G):
+            s = (q[h * G + j].double() @ k[h].double().T) / math.sqrt(q.shape[1])
+            outs.append(torch.softmax(s, -1) @ v[h].double())
+    ret[rank] = (h0, h1, torch.stack(outs))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_gloo_kv_head_sharding():
+    torch.manual_seed(1)
+    Hkv, G, T, D = 8, 4, 300, 64
+    q, k, v = torch.randn(Hkv * G, D), torch.randn(Hkv, T, D), torch.randn(Hkv, T, D)
+    ret = mp.Manager().dict()
+    mp.spawn(_heads_worker, args=(2, 29400 + os.getpid() % 90, q, k, v, ret), nprocs=2, join=True)
+    assert [ret[r][:2] for r in range(2)] == [(0, 4), (4, 8)]
+    out = torch.cat([ret[r][2] for r in range(2)])
+    ref = torch.stack([torch.softmax((q[i].double() @ k[i // G].double().T) / math.sqrt(D), -1) @ v[i // G].double()
+                       for i in range(Hkv * G)])
+    assert (out - ref).abs().max().item() < 1e-12

@@ -224,3 +224,43 @@ def test_paged_oracle_store_call_boundaries():
     sl = slots.copy(); sl[-1] = 10 ** 6
     assert oracle.paged_store(k, v, sl, bad) == 1
     assert np.array_equal(bad[1], one[1])
+
+
+# ---------------- legacy page API (kv_quant.py:37-191) ----------------
+@pytest.mark.parametrize("calib", CALIBS)
+def test_legacy_page_oracle(calib):
+    g = load_golden("legacy_page.npz")
+    k, v = bf16_from_bits(g["k"])[:, :16], bf16_from_bits(g["v"])[:, :16]
+    for name, x in (("k", k), ("v", v)):
+        codes, sc = oracle.page_quantize(x, calib)
+        assert np.array_equal(codes, g[f"page_{calib}_{name}_int4"])
+        assert np.array_equal(sc.view(np.uint16), g[f"page_{calib}_{name}_scale"])
+        assert torch.equal(oracle.page_dequant(codes, sc), bf16_from_bits(g[f"page_{calib}_{name}_deq"]))
+
+
+def test_legacy_page_oracle_fp32_input():
+    g = load_golden("legacy_page.npz")
+    for name in ("k", "v"):
+        codes, sc = oracle.page_quantize(g[f"f32_{name}"], "mse", n_alphas=7)
+        assert np.array_equal(codes, g[f"f32_{name}_int4"])
+        assert np.array_equal(sc.view(np.uint16), g[f"f32_{name}_scale"])
+
+
+def test_legacy_page_error_oracle():
+    g = load_golden("legacy_page.npz")
+    a, o = oracle.page_error(g["err_x"])
+    np.testing.assert_allclose([a, o], g["err"][:2], rtol=1e-6)
+
+
+# ------------- heavy-tailed K of the reference test (randn**3) -------------
+@pytest.mark.parametrize("calib", CALIBS)
+def test_heavy_tail_store_oracle(calib):
+    g = load_golden("heavy_tail.npz")
+    k, v = bf16_from_bits(g["k"]), bf16_from_bits(g["v"])
+    c = oracle.store_int4(k, v, calib, calib)
+    assert np.array_equal(c["k_packed"], g[f"{calib}_k_packed"])
+    assert np.array_equal(c["k_scale"].view(np.uint16), g[f"{calib}_k_scale"])
+    assert np.array_equal(c["v_packed"], g[f"{calib}_v_packed"])
+    assert np.array_equal(c["v_scale"].view(np.uint16), g[f"{calib}_v_scale"])
+    rt = torch.from_numpy(oracle.roundtrip_f32(k, "int4", "channel", calib)).to(torch.bfloat16)
+    assert torch.equal(rt, bf16_from_bits(g[f"{calib}_k_rt"]))

@@ -6,10 +6,9 @@ and scattered decode-style stores), scripts/validate_paged_decode.py:108-116
 (decode: exact block, partial tail, short, tiny, mixed batch, long, long
 mixed; Hq = 48, Hkv = 8, D = 128, block 0 left unused) and
 scripts/validate_nvfp4_kivi.py:126-160 (NVFP4 decode at 512 / 500 / 33).
-Store and gather are compared byte for byte; decode (bf16 output) against the
-oracle's double-precision attention over the same cache:
-|out - ref| <= 2e-3 + |ref| * 2^-8 and relative RMS <= 1e-3 against the
-bf16-rounded reference.
+Store and gather are compared byte for byte; decode against the oracle's
+double-precision attention over the same cache with the decode bar of
+conftest.py, on the bf16 output and on the fp32 state (kivi_paged_decode_f32).
 """
 import math
 
@@ -18,6 +17,7 @@ import pytest
 import torch
 
 import oracle
+from conftest import check_decode_bf16, check_decode_fp32
 
 pytestmark = pytest.mark.gpu
 
@@ -141,15 +141,12 @@ def test_paged_gather_bit_exact(cuda_dev, fmt):
 
 
 def _check_decode(out, want):
-    """bf16 output: |out - ref| <= 2e-3 + |ref| * 2^-8 (one bf16 rounding on top
-    of the 2e-3 fp32 bar), and relative RMS <= 1e-3 against the reference
-    rounded to bf16 (the output rounding alone is ~1.1e-3 relative RMS)."""
-    o, w = out.float().cpu().numpy(), want
-    err = np.abs(o - w)
-    assert bool((err <= 2e-3 + np.abs(w) * 2.0 ** -8).all()), err.max()
-    wb = torch.from_numpy(w).bfloat16().float().numpy()
-    rel = np.sqrt(((o - wb) ** 2).mean() / max((w ** 2).mean(), 1e-30))
-    assert rel <= 1e-3, rel
+    """The decode bar of conftest.py, on the bf16 output (or, for an fp32
+    `out`, on the normalised state before the bf16 cast)."""
+    if out.dtype == torch.float32:
+        check_decode_fp32(out, want)
+    else:
+        check_decode_bf16(out, want)
 
 
 DECODE_CASES = {
@@ -175,11 +172,15 @@ def test_paged_decode_vs_oracle(cuda_dev, fmt, case, Hq):
     q = torch.randn(len(seq_lens), Hq, D, generator=g).bfloat16()
     sm = 1.0 / math.sqrt(D)
     dec = paged.int4_kivi_paged_decode if fmt == "int4" else paged.nvfp4_kivi_paged_decode
-    out = dec(q.to(cuda_dev), kv_gpu, torch.from_numpy(bt).to(cuda_dev),
-              torch.tensor(seq_lens, dtype=torch.int32, device=cuda_dev), sm)
+    btd, sld = torch.from_numpy(bt).to(cuda_dev), torch.tensor(seq_lens, dtype=torch.int32, device=cuda_dev)
+    out = dec(q.to(cuda_dev), kv_gpu, btd, sld, sm)
+    out32 = dec(q.to(cuda_dev), kv_gpu, btd, sld, sm,
+                out=torch.empty(len(seq_lens), Hq, D, dtype=torch.float32, device=cuda_dev))
     torch.cuda.synchronize()
     want = oracle.paged_decode(q.float(), kv_cpu, bt, seq_lens, sm, fmt)
     _check_decode(out, want)
+    _check_decode(out32, want)
+    assert torch.equal(out, out32.bfloat16())
 
 
 @pytest.mark.parametrize("H,Hq,Dh", ((16, 32, 128), (2, 6, 64), (4, 4, 256)))
@@ -190,11 +191,14 @@ def test_paged_decode_other_shapes(cuda_dev, H, Hq, Dh):
     kv_gpu, kv_cpu, bt = _build(seq_lens, H, "int4", 3, cuda_dev, Dh=Dh)
     g = torch.Generator().manual_seed(4)
     q = torch.randn(len(seq_lens), Hq, Dh, generator=g).bfloat16()
-    out = paged.int4_kivi_paged_decode(q.to(cuda_dev), kv_gpu, torch.from_numpy(bt).to(cuda_dev),
-                                       torch.tensor(seq_lens, dtype=torch.int32, device=cuda_dev))
+    btd, sld = torch.from_numpy(bt).to(cuda_dev), torch.tensor(seq_lens, dtype=torch.int32, device=cuda_dev)
+    out = paged.int4_kivi_paged_decode(q.to(cuda_dev), kv_gpu, btd, sld)
+    out32 = paged.int4_kivi_paged_decode(q.to(cuda_dev), kv_gpu, btd, sld,
+                                         out=torch.empty(3, Hq, Dh, dtype=torch.float32, device=cuda_dev))
     torch.cuda.synchronize()
     want = oracle.paged_decode(q.float(), kv_cpu, bt, seq_lens, 1.0 / math.sqrt(Dh), "int4")
     _check_decode(out, want)
+    _check_decode(out32, want)
 
 
 def test_paged_decode_empty_sequence_and_graph(cuda_dev):

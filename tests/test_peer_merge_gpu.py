@@ -91,13 +91,11 @@ def test_fused_seqpar_single_rank_equals_decode(cuda_dev):
     from int4_kivi import _native as N
     from int4_kivi.decode import decode_packed
     q, st, x, _ = _seqpar_case(cuda_dev, 1)
-    want = decode_packed(q, st, 32).float()
+    want = decode_packed(q, st, 32)
     for it in range(3):
-        got = decode_packed(q, st, 32, exchange=x).float()
+        got = decode_packed(q, st, 32, exchange=x)
         torch.cuda.synchronize()
-        d = (got - want).abs()
-        n = int(torch.count_nonzero(d))
-        assert bool((d <= 2e-3 + want.abs() * 2.0 ** -8).all()), (it, n, float(d.max()))
+        assert torch.equal(got, want), (it, int(torch.count_nonzero(got != want)))
     assert N.device_status(cuda_dev) == 0
     assert int(x.row_epoch.min().item()) == 3 == int(x.row_epoch.max().item())
 
@@ -114,3 +112,27 @@ def test_fused_seqpar_wait_times_out(cuda_dev):
     torch.cuda.synchronize()
     assert N.device_status(cuda_dev) == 5
     assert torch.count_nonzero(out).item() == 0
+
+
+def test_timeout_raises_through_python_api(cuda_dev):
+    """The same silent second rank, seen from the Python API: decode_packed
+    (check=True) raises KiviError with status KIVI_ERR_TIMEOUT, and the
+    sync-free per-step poll raises it once the step has finished."""
+    from int4_kivi import _native as N
+    from int4_kivi.decode import decode_packed
+    q, st, x, _ = _seqpar_case(cuda_dev, 2)
+    N.device_status(cuda_dev)
+    with pytest.raises(N.KiviError) as ei:
+        decode_packed(q, st, 32, exchange=x, check=True)
+    assert ei.value.status == N.KIVI_ERR_TIMEOUT
+    assert N.device_status(cuda_dev) == 0                # raised and cleared
+    decode_packed(q, st, 32, exchange=x)                 # fails on the device again
+    N.poll_errors(cuda_dev)                              # queues the flag copy, returns at once
+    torch.cuda.synchronize()
+    with pytest.raises(N.KiviError) as ei:
+        N.poll_errors(cuda_dev)
+    assert ei.value.status == N.KIVI_ERR_TIMEOUT
+    N.poll_errors(cuda_dev)                              # cleared: nothing more to report
+    torch.cuda.synchronize()
+    N.poll_errors(cuda_dev)
+    assert N.device_status(cuda_dev) == 0

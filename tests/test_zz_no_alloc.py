@@ -1,8 +1,8 @@
 """kivi_decode_noalloc: the allocation-free decode entry point.
 
 Callers that cannot allocate device memory while decoding (an engine that
-owns all device memory through its own pool, code inside a stream capture, an
-FFI host with no CUDA allocator) call this variant; it keeps the split-K
+owns all device memory through its own pool, an FFI host with no CUDA
+allocator) call this variant; it keeps the split-K
 partials in a fixed library-owned device array instead of a workspace.
 This file is collected last on purpose, so a run that stops at the first
 failure has already run every other test.  It passes alone in a fresh process
