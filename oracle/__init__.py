@@ -68,6 +68,7 @@ def lib():
         L.orc_e4m3_to_f32.argtypes = [ctypes.c_uint8]
         L.orc_e4m3_to_f32.restype = F
         L.orc_num_threads.restype = I
+        L.orc_set_num_threads.argtypes = [I]
         L.orc_paged_calib.argtypes = [P, I, I]
         L.orc_paged_calib.restype = ctypes.c_uint8
         L.orc_paged_store.argtypes = [P, P, I, I, I, I, I, P, P, Lg]
@@ -108,6 +109,12 @@ def alphas(n_alphas: int = 32) -> np.ndarray:
 
 def num_threads() -> int:
     return lib().orc_num_threads()
+
+
+def set_num_threads(n: int) -> None:
+    """OpenMP threads of the oracle's loops (e.g. all host cores under a
+    launcher that exported OMP_NUM_THREADS=1)."""
+    lib().orc_set_num_threads(int(n))
 
 
 def calibrate(blocks, fmt: str, calib: str, n_alphas: int = 32) -> np.ndarray:

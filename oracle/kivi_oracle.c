@@ -461,6 +461,15 @@ int orc_num_threads(void) {
 #endif
 }
 
+/* Thread count of the OpenMP loops (a launcher may have set OMP_NUM_THREADS=1). */
+void orc_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 /* ------------------------------------------------------------------------- */
 /* Paged cache (the vLLM-fork layout named by WRITEUP.md:82-95,117-124 and     */
 /* used at scripts/validate_paged_decode.py:32-64,                             */

@@ -52,7 +52,7 @@ __device__ __forceinline__ float mean16(const float e[BLK]) {
     float s = __fadd_rn(e[0], e[8]);
 #pragma unroll
     for (int j = 1; j < 8; ++j) s = __fadd_rn(s, __fadd_rn(e[j], e[j + 8]));
-    return __fdiv_rn(s, 16.0f);
+    return __fmul_rn(s, 0.0625f);      // == s / 16 exactly (a power-of-two scaling, one rounding)
 }
 
 __device__ __forceinline__ float absmax16(const float x[BLK]) {
@@ -62,12 +62,38 @@ __device__ __forceinline__ float absmax16(const float x[BLK]) {
     return fmaxf(m, 1e-9f);   // .clamp_min(1e-9)
 }
 
+// A stand-in for the correctly rounded quotient x / s that every grid
+// (rint + clamp, the e2m1 bucketing) maps to the same point, given r = 1/s
+// rounded to nearest.  y = x * r is within ~2^-22 |y| of the true quotient,
+// so it rounds to the same grid point as the IEEE quotient unless it lies
+// that close to a rounding boundary (a half-integer, or an e2m1 bound); only
+// then is the exact division done.  Valid for every x and every normal,
+// nonzero s (the scales here are >= 1e-9 / 7 or e4m3 values).
+__device__ __forceinline__ float quot_for_grid(float x, float s, float r, int fmt) {
+    const float y = __fmul_rn(x, r);
+    const float a = fabsf(y);
+    const float tol = 1e-5f * fmaxf(1.0f, a);
+    bool near;
+    if (fmt == FMT_NVFP4) {
+        const float bnd = a < 1.0f ? (a < 0.5f ? 0.25f : 0.75f)
+                                   : (a < 2.125f ? (a < 1.5f ? 1.25f : 1.75f) : (a < 3.0f ? 2.5f : (a < 4.25f ? 3.5f : 5.0f)));
+        near = fabsf(a - bnd) < tol;
+    } else {
+        near = fabsf(fabsf(y - rintf(y)) - 0.5f) < tol;
+    }
+    return near ? __fdiv_rn(x, s) : y;
+}
+__device__ __forceinline__ float q_grid_div(float x, float s, float r, int fmt) {
+    return q_grid(quot_for_grid(x, s, r, fmt), fmt);
+}
+
 // Reconstruction error of one block under scale s (the kv_quant MSE term).
 __device__ __forceinline__ float block_err(const float x[BLK], float s, int fmt) {
     float e[BLK];
+    const float r = __frcp_rn(s);
 #pragma unroll
     for (int i = 0; i < BLK; ++i) {
-        float q = (s == 0.0f) ? 0.0f : q_grid(__fdiv_rn(x[i], s), fmt);
+        float q = (s == 0.0f) ? 0.0f : q_grid_div(x[i], s, r, fmt);
         float d = __fsub_rn(x[i], __fmul_rn(q, s));
         e[i] = __fmul_rn(d, d);
     }

@@ -203,7 +203,9 @@ __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
 }
 
 // One m16n8k16 step for two M-tiles given the k-half words wA, wB and their
-// scale pairs.  INT4 splits each scale into head/tail parts (two exact MMAs).
+// scale pairs.  INT4 splits each scale into an 8-bit head and a 3-bit tail
+// (two MMAs), so every code x scale product is exact in fp16; used for K,
+// and for V when the GQA group is too large for the paired form.
 template <int FMT, bool SPLIT>
 __device__ __forceinline__ void mma_pair(float (&c0)[4], float (&c1)[4], uint32_t wA, uint32_t wB,
                                          uint32_t sA, uint32_t sB, uint32_t b0, uint32_t b1) {
@@ -555,7 +557,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                             mma_raw<FMT>(acc[2 * sg], acc[2 * sg + 1], hs ? w2 : w0, hs ? w3 : w1,
                                     hmul2u(b0, sa), hmul2u(b1, sb));
                         } else {
-                            mma_pair<FMT, false>(acc[2 * sg], acc[2 * sg + 1], hs ? w2 : w0, hs ? w3 : w1, sa, sb, b0, b1);
+                            mma_pair<FMT, true>(acc[2 * sg], acc[2 * sg + 1], hs ? w2 : w0, hs ? w3 : w1, sa, sb, b0, b1);
                         }
                     }
                 }

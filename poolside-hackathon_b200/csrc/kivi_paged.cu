@@ -76,9 +76,10 @@ __device__ __forceinline__ float grid_code(float y, int fmt) {
 // Squared reconstruction error of a block under the e4m3-rounded scale s.
 __device__ __forceinline__ float sq_err(const float x[BLK], float s, int fmt) {
     float e[BLK];
+    const float r = __frcp_rn(s);
 #pragma unroll
     for (int i = 0; i < BLK; ++i) {
-        const float q = (s == 0.0f) ? 0.0f : grid_code(__fdiv_rn(x[i], s), fmt);
+        const float q = (s == 0.0f) ? 0.0f : grid_code(quot_for_grid(x[i], s, r, fmt), fmt);
         const float d = __fsub_rn(x[i], __fmul_rn(q, s));
         e[i] = __fmul_rn(d, d);
     }
@@ -87,7 +88,7 @@ __device__ __forceinline__ float sq_err(const float x[BLK], float s, int fmt) {
 
 __device__ __forceinline__ uint32_t nibble_of(float x, float s, int fmt) {
     if (s == 0.0f) return 0u;
-    const float y = __fdiv_rn(x, s);
+    const float y = quot_for_grid(x, s, __frcp_rn(s), fmt);
     if (fmt == FMT_NVFP4) return (uint32_t)e2m1_index(fabsf(y)) | (y < 0.0f ? 8u : 0u);
     return (uint32_t)(int)grid_code(y, fmt) & 0xFu;
 }

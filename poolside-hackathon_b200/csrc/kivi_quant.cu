@@ -42,11 +42,12 @@ __device__ __forceinline__ void quant_pack(const float x[BLK], int calib, const 
     if (FMT == FMT_NVFP4) {
         uint8_t sc;
         float sd = nvfp4_calibrate16(x, calib, alphas, n_alphas, g, &sc);
+        const float r = __frcp_rn(sd);
 #pragma unroll
         for (int i = 0; i < BLK; ++i) {
             uint32_t nib = 0;
             if (sd != 0.0f) {
-                float y = __fdiv_rn(x[i], sd);
+                float y = quot_for_grid(x[i], sd, r, FMT_NVFP4);
                 nib = (uint32_t)e2m1_index(fabsf(y)) | (y < 0.0f ? 8u : 0u);
             }
             if (i < 8) lo |= nib << (4 * i); else hi |= nib << (4 * (i - 8));
@@ -54,9 +55,10 @@ __device__ __forceinline__ void quant_pack(const float x[BLK], int calib, const 
         sbits = sc;
     } else {
         float s = calibrate16(x, FMT, calib, alphas, n_alphas);
+        const float r = __frcp_rn(s);
 #pragma unroll
         for (int i = 0; i < BLK; ++i) {
-            int c = (int)q_grid(__fdiv_rn(x[i], s), FMT);
+            int c = (int)q_grid_div(x[i], s, r, FMT);
             uint32_t nib = (uint32_t)c & 0xF;
             if (i < 8) lo |= nib << (4 * i); else hi |= nib << (4 * (i - 8));
         }
@@ -65,11 +67,12 @@ __device__ __forceinline__ void quant_pack(const float x[BLK], int calib, const 
     packed = make_uint2(lo, hi);
 }
 
-// K blocks (per channel, 16-token pages) go through shared memory so that
-// both sides are coalesced: a CTA loads PPC pages x D channels of one head
-// with 16-byte row loads, each thread quantises (channel, page) blocks read
-// column-wise from the tile, and the packed results are written back grouped
-// by channel, where consecutive pages are contiguous in k_packed / k_scale.
+// K blocks (per channel, 16-token pages): a CTA owns PPC pages x D channels
+// of one head.  Threads take consecutive channels, so each of a block's 16
+// token loads is a contiguous row segment across the warp; the packed
+// results go through shared memory and are written back grouped by channel,
+// where consecutive pages are contiguous in k_packed / k_scale (a direct
+// write would put neighbouring lanes k_np_stride pages apart).
 // V blocks (16 channels of one token) are contiguous in the input and in the
 // output, so V CTAs take one block per thread directly.
 // Grid: [0, nk_ctas) K chunks (head-major), then V CTAs (grid-stride).
@@ -82,30 +85,14 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
     if ((int)blockIdx.x < nk_ctas) {
         const int NP = a.S_k / BLK;
         const int h = blockIdx.x / n_chunks, p0 = (blockIdx.x % n_chunks) * ppc;
-        const int np_here = min(ppc, NP - p0), ntok = np_here * BLK;
-        T* tile = reinterpret_cast<T*>(st_smem);                                   // [ntok][D]
-        uint2* sc = reinterpret_cast<uint2*>(st_smem + (size_t)ppc * BLK * D * sizeof(T));   // [ppc][D+1]
-        uint16_t* ss = reinterpret_cast<uint16_t*>(sc + (size_t)ppc * (D + 1));               // [ppc][D+2]
+        const int np_here = min(ppc, NP - p0);
+        uint2* sc = reinterpret_cast<uint2*>(st_smem);                              // [ppc][D+1]
+        uint16_t* ss = reinterpret_cast<uint16_t*>(sc + (size_t)ppc * (D + 1));     // [ppc][D+2]
         const T* src = k + h * a.sk_h + (int64_t)p0 * BLK * a.sk_s;
-        const int vpr = D * (int)sizeof(T) / 16;                                   // 16-byte vectors per row
-        if (a.sk_d == 1 && (a.sk_s * (int64_t)sizeof(T)) % 16 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-            uint4* t4 = reinterpret_cast<uint4*>(tile);
-            for (int i = tid; i < ntok * vpr; i += 256) {
-                const int r = i / vpr, c = i - r * vpr;
-                t4[i] = __ldg(reinterpret_cast<const uint4*>(src + r * a.sk_s) + c);
-            }
-        } else {
-            for (int i = tid; i < ntok * D; i += 256) {
-                const int r = i / D, d = i - r * D;
-                tile[i] = src[r * a.sk_s + d * a.sk_d];
-            }
-        }
-        __syncthreads();
         for (int b = tid; b < np_here * D; b += 256) {
             const int p = b / D, c = b - p * D;
             float x[BLK];
-#pragma unroll
-            for (int j = 0; j < BLK; ++j) x[j] = to_f32<T>(tile[(p * BLK + j) * D + c]);
+            load_strided16<T>(src + (int64_t)p * BLK * a.sk_s + c * a.sk_d, a.sk_s, x);
             uint2 pk;
             uint16_t sb;
             quant_pack<FMT>(x, a.calib_k, a.alphas, a.n_alphas, a.g_k, pk, sb);
@@ -140,15 +127,16 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
     }
 }
 
-// Pages per K chunk: the input tile stays within 64 KB of shared memory.
+// Pages per K chunk: 16 (a 32-byte run of fp16 scales per channel), fewer
+// for wide heads so the staged output stays within 40 KB of shared memory.
 template <typename T>
 static int store_ppc(int D) {
-    const int p = 65536 / (BLK * D * (int)sizeof(T));
+    const int p = 40960 / (D * 10 + 18);
     return p < 1 ? 1 : (p > 16 ? 16 : p);
 }
 template <typename T>
 static size_t store_smem(int D, int ppc) {
-    return (size_t)ppc * BLK * D * sizeof(T) + (size_t)ppc * (D + 1) * 8 + (size_t)ppc * (D + 2) * 2;
+    return (size_t)ppc * (D + 1) * 8 + (size_t)ppc * (D + 2) * 2;
 }
 
 __device__ __forceinline__ float nib_value(uint32_t nib, int fmt) {
@@ -280,9 +268,10 @@ __global__ void __launch_bounds__(256) roundtrip_kernel(RoundtripArgs a) {
             load_strided16<T>(x + base, D, v);
         }
         const float s = calibrate16(v, a.fmt, a.calib, a.alphas, a.n_alphas);
+        const float r = __frcp_rn(s);
 #pragma unroll
         for (int j = 0; j < BLK; ++j)
-            y[base + j * stride] = from_f32<T>(__fmul_rn(q_grid(__fdiv_rn(v[j], s), a.fmt), s));
+            y[base + j * stride] = from_f32<T>(__fmul_rn(q_grid_div(v[j], s, r, a.fmt), s));
     }
 }
 
