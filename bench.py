@@ -127,6 +127,7 @@ def _load_reference_kv_quant():
         return None
     spec = importlib.util.spec_from_file_location("reference_kv_quant", path)
     mod = importlib.util.module_from_spec(spec)
+    sys.modules["reference_kv_quant"] = mod          # its dataclasses look their module up
     spec.loader.exec_module(mod)
     return mod
 

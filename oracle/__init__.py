@@ -50,7 +50,9 @@ def build(force: bool = False) -> str:
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB_PATH):
+        src = os.path.join(_HERE, "kivi_oracle.c")
+        if not os.path.exists(_LIB_PATH) or (os.path.exists(src) and
+                                             os.path.getmtime(_LIB_PATH) < os.path.getmtime(src)):
             build()
         L = ctypes.CDLL(_LIB_PATH)
         P, I, F, Lg = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_long

@@ -300,7 +300,10 @@ namespace {
 template <typename T, int FMT>
 int launch_store(const StoreArgs& a, cudaStream_t st) {
     const int NP = a.S_k / BLK, ND = a.D / BLK;
-    const int ppc = store_ppc<T>(a.D);
+    // fewer pages per CTA when the K work is small, so short stores (and the
+    // ALU-heavy MSE search) still fill every SM
+    int ppc = store_ppc<T>(a.D);
+    while (ppc > 1 && (int64_t)a.H * ((NP + ppc - 1) / ppc) < 8LL * 148) ppc >>= 1;
     const int n_chunks = (NP + ppc - 1) / ppc;
     const int64_t nk_ctas64 = (int64_t)a.H * n_chunks;
     const int64_t nv = (int64_t)a.H * a.S_v * ND;

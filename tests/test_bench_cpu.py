@@ -1,6 +1,7 @@
 """The benchmark's CPU reference arm (the driver runs `bench.py --impl
 reference`): it must print one JSON line with the contract's keys, time the
-CPU restatement on this host's cores, and need no GPU."""
+reference's CPU path on all of this host's cores, and need no GPU.  Run the
+way torchrun runs it too (OMP_NUM_THREADS=1 exported)."""
 import json
 import os
 import subprocess
@@ -10,7 +11,7 @@ from conftest import ROOT
 
 
 def test_reference_arm_prints_contract_line():
-    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
     r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
                         "--warmup", "1"], capture_output=True, text=True, timeout=600, env=env, cwd=ROOT)
     assert r.returncode == 0, r.stderr[-2000:]
@@ -21,6 +22,9 @@ def test_reference_arm_prints_contract_line():
                 "scaling", "vs_baseline", "dtype", "data", "config", "impl", "cpu_baseline", "e2e"):
         assert key in d, key
     assert d["impl"] == "reference" and d["value"] > 0 and d["higher_is_better"] is True
-    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    # the reference's own kv_quant + SDPA when baseline/_ref holds the reference
+    # install, else the oracle port; always on every host core
+    want = "reference" if os.path.exists(os.path.join(ROOT, "baseline", "_ref", "kv_quant.py")) else "port"
+    assert d["cpu_baseline"]["kind"] == want and d["cpu_baseline"]["cores"] == os.cpu_count()
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert "workload" in d["config"]
