@@ -142,7 +142,10 @@ def cpu_reference(S: int, steps: int, warmup: int, budget_s: float = 20.0):
     `budget_s` seconds (at most 16384 of the tokens).
     Returns (GB/s of packed bytes, sample text, threads, seconds per step, kind)."""
     import torch
-    threads = os.cpu_count() or 1
+    try:
+        threads = len(os.sched_getaffinity(0))     # the cores this process may run on
+    except AttributeError:
+        threads = os.cpu_count() or 1
     torch.set_num_threads(threads)                 # a launcher may have exported OMP_NUM_THREADS=1
     ref = _load_reference_kv_quant()
     g = torch.Generator().manual_seed(1)

@@ -65,6 +65,10 @@ struct DecodeParams {
     int xW, xrank;                   // ranks in the exchange, this rank
     unsigned int* row_epoch;
     long long timeout_ns;
+    // merge folded into the decode kernel (plain decode, uniform lengths):
+    // per-head completion counters (zero between launches) and the bf16 out
+    int* head_cnt;
+    __nv_bfloat16* out;
 };
 
 struct SeqPar {
@@ -157,6 +161,17 @@ __global__ void __launch_bounds__(1024) tile_offsets_kernel(const int* seq_lens,
     if (t == 1023) tile_off[BH] = part[1023];
 }
 
+__host__ __device__ inline void head_cta_range(int64_t a0, int64_t a1, int64_t W, int N, int& c_lo, int& c_hi) {
+    // CTA c owns tiles [floor(cW/N), floor((c+1)W/N)).  c_lo is the last CTA
+    // whose slice starts at or before a0 (floor(cW/N) <= a0 <=> cW < (a0+1)N),
+    // c_hi the last whose slice starts before a1 (cW < a1 N).
+    c_lo = 0; c_hi = -1;
+    if (W <= 0 || a1 <= a0) return;
+    const int64_t lo = ((a0 + 1) * N - 1) / W, hi = (a1 * N - 1) / W;
+    c_lo = (int)(lo < N - 1 ? lo : N - 1);
+    c_hi = (int)(hi < N - 1 ? hi : N - 1);
+}
+
 template <int FMT>
 struct StageLayout {
     static constexpr int KC = 0;                        // 128 ch x 64 B, 64B-swizzled
@@ -167,10 +182,11 @@ struct StageLayout {
     static constexpr uint32_t TX = (FMT == FMT_NVFP4) ? (8192 + 2048 + 8192 + 1024) : 20480;
 };
 
-struct __align__(8) SmemCtl {
+struct __align__(16) SmemCtl {
     uint64_t full[NST];
     uint64_t empty[NST];
     int abort;
+    int fold_last;
 };
 
 __device__ __forceinline__ void set_err(int* err, int code) {
@@ -260,6 +276,51 @@ __device__ __forceinline__ void split_prod(uint32_t q, uint32_t sc, uint32_t& hi
 
 __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
     return row * 64u + 16u * (chunk ^ ((row >> 1) & 3u));
+}
+
+template <int FMT>
+__device__ __forceinline__ void combine_row(const DecodeParams& p, int bh, int h, int mode, int tid, float* csm,
+                                            bool dep_wait, __nv_bfloat16* out, float* acc_out, float& M_o,
+                                            float& L_o, unsigned int& e_o);
+__device__ __forceinline__ void sync128();
+
+// The split-K merge folded into the decode kernel (plain decode of equal
+// lengths).  Once its tile loop is over -- normally or through a timed-out
+// wait, so every consumer warp gets here -- a CTA counts itself done on each
+// head it touched; the CTA that completes a head's count merges that head's
+// rows (its partial slots and bf16 hot tail) into the bf16 output and resets
+// the counter to zero for the next launch.  Each writer fences its partial
+// stores before the count, the merging CTA fences after it and reads the
+// partials at L2.
+template <int FMT>
+__device__ __forceinline__ void fold_merges(const DecodeParams& p, int64_t i0, int64_t i1, float* csm, int* last_s,
+                                         int tid) {
+    __threadfence();
+    sync128();
+    const int h_first = (int)(i0 / p.T), h_last = (int)((i1 - 1) / p.T);
+    for (int bh = h_first; bh <= h_last; ++bh) {
+        if (tid == 0) {
+            int c_lo, c_hi;
+            head_cta_range((int64_t)bh * p.T, (int64_t)(bh + 1) * p.T, p.W, p.N, c_lo, c_hi);
+            const int done = atomicAdd(p.head_cnt + bh, 1) + 1;
+            const int last = done == c_hi - c_lo + 1;
+            if (last) {
+                atomicExch(p.head_cnt + bh, 0);
+                __threadfence();
+            }
+            sts32s(smem_u32(last_s), (uint32_t)last);
+        }
+        sync128();
+        const bool last = lds32s(smem_u32(last_s)) != 0;
+        sync128();
+        if (!last) continue;
+        for (int h = 0; h < p.G; ++h) {
+            float M, L;
+            unsigned int e;
+            combine_row<FMT>(p, bh, h, 0, tid, csm, false, p.out, nullptr, M, L, e);
+            sync128();                                   // csm is reused by the next row
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -569,6 +630,10 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
         if (lane == 0) mbar_arrive(&ctl->empty[s]);
     }
     if (cur >= 0 && !lds32s(abort_s)) flush(cur);
+    if (p.head_cnt) {
+        fold_merges<FMT>(p, i0, i1, reinterpret_cast<float*>(ctl + 1), &ctl->fold_last, warp * 32 + lane);
+        return;
+    }
     // let the dependent merge kernel start its prologue (programmatic launch)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
@@ -670,17 +735,6 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeParams 
 // reduces its channels over the slots with coalesced loads.
 // mode 0 -> normalised bf16 out; mode 1 -> merged (m, l, acc) records.
 // ---------------------------------------------------------------------------
-__host__ __device__ inline void head_cta_range(int64_t a0, int64_t a1, int64_t W, int N, int& c_lo, int& c_hi) {
-    // CTA c owns tiles [floor(cW/N), floor((c+1)W/N)).  c_lo is the last CTA
-    // whose slice starts at or before a0 (floor(cW/N) <= a0 <=> cW < (a0+1)N),
-    // c_hi the last whose slice starts before a1 (cW < a1 N).
-    c_lo = 0; c_hi = -1;
-    if (W <= 0 || a1 <= a0) return;
-    const int64_t lo = ((a0 + 1) * N - 1) / W, hi = (a1 * N - 1) / W;
-    c_lo = (int)(lo < N - 1 ? lo : N - 1);
-    c_hi = (int)(hi < N - 1 ? hi : N - 1);
-}
-
 // V of tail token j (absolute n_full + j) at channel d: bf16 when the caller
 // keeps the partial page unquantised, else dequantised from v_packed.
 template <int FMT>
@@ -691,14 +745,25 @@ __device__ __forceinline__ float tail_v(const DecodeParams& p, int bh, int n_ful
     return gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
 }
 
+// 128 consumer threads of a CTA synchronise on named barrier 1 (the merge
+// runs both as its own kernel and at the end of the decode kernel, whose
+// producer warp has left by then).
+__device__ __forceinline__ void sync128() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// LSE merge of all partial slots of one (kv-head, q-head) row plus its bf16
+// hot tail, by 128 threads (tid = 0..127).  The slot weights exp2(m_s - M)
+// are computed once into shared memory (csm), then every thread reduces its
+// channels over the slots with coalesced loads.  mode 0 -> normalised bf16
+// out; mode 1 -> merged (m, l, acc) records; mode 2 -> this rank's state
+// into its exchange slot of epoch `e`.  Returns the row's M and L.
 template <int FMT>
-__global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int mode, __nv_bfloat16* out,
-                                                      float* m_out, float* l_out, float* acc_out) {
-    extern __shared__ float csm[];
-    const int bh = blockIdx.x, h = blockIdx.y, b = bh / p.Hkv, kvh = bh % p.Hkv;
+__device__ __forceinline__ void combine_row(const DecodeParams& p, int bh, int h, int mode, int tid, float* csm,
+                                            bool dep_wait, __nv_bfloat16* out, float* acc_out, float& M_o,
+                                            float& L_o, unsigned int& e_o) {
+    const int b = bh / p.Hkv, kvh = bh % p.Hkv;
     const int G = p.G, D = p.D, ND = D / BLK;
     const int Lh = head_len(p, bh), n_full = (Lh / BLK) * BLK, hot = Lh - n_full;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = tid >> 5, lane = tid & 31;
     int c_lo = 0, c_hi = -1;
     const int64_t Wt = total_tiles(p);
     const int64_t a0 = head_tile0(p, bh), a1 = head_tile0(p, bh + 1);
@@ -719,7 +784,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     }
     // partial slots are produced by the split kernel launched just before
     // (programmatic dependent launch): wait for its results to be visible
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (dep_wait) asm volatile("griddepcontrol.wait;" ::: "memory");
     auto slot = [&](int i) -> int64_t {
         return ((int64_t)(c_lo + i / NWARP_C + bh) * NWARP_C + (i % NWARP_C)) * G + h;
     };
@@ -728,29 +793,30 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         const int64_t cc = c_lo + i / NWARP_C;
         return tile_start(cc, Wt, p.N) < tile_start(cc + 1, Wt, p.N);
     };
-    for (int i = threadIdx.x; i < ns; i += blockDim.x) w[i] = live(i) ? p.part_m[slot(i)] : -INFINITY;
-    __syncthreads();
+    // partials of other CTAs: read at L2 (never a line this SM cached earlier)
+    for (int i = tid; i < ns; i += 128) w[i] = live(i) ? __ldcg(p.part_m + slot(i)) : -INFINITY;
+    sync128();
     // M = max over slots and hot tokens
     float M = -INFINITY;
-    for (int i = threadIdx.x; i < ns + hot; i += blockDim.x) M = fmaxf(M, w[i]);
+    for (int i = tid; i < ns + hot; i += 128) M = fmaxf(M, w[i]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     if (lane == 0) red[warp] = M;
-    __syncthreads();
+    sync128();
     M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
     const float Mr = (M == -INFINITY) ? 0.f : M;
-    __syncthreads();
+    sync128();
     // weights and L
     float Ls = 0.f;
-    for (int i = threadIdx.x; i < ns + hot; i += blockDim.x) {
+    for (int i = tid; i < ns + hot; i += 128) {
         const float e = exp2f(w[i] - Mr);
-        Ls += (i < ns) ? (e != 0.f ? p.part_l[slot(i)] * e : 0.f) : e;
+        Ls += (i < ns) ? (e != 0.f ? __ldcg(p.part_l + slot(i)) * e : 0.f) : e;
         w[i] = e;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, o);
     if (lane == 0) red[4 + warp] = Ls;
-    __syncthreads();
+    sync128();
     Ls = (red[4] + red[5]) + (red[6] + red[7]);
     const int64_t row = (int64_t)b * p.Hq + kvh * G + h;
     const int rows = p.B * p.Hq;
@@ -771,7 +837,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
             for (int u = 0; u < 4; ++u) {
                 const int i = i0 + 4 * u;
                 wi[u] = i < ns ? w[i] : 0.f;
-                v4[u] = wi[u] != 0.f ? *reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane)
+                v4[u] = wi[u] != 0.f ? __ldcg(reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane))
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
@@ -781,23 +847,37 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         }
         float* sacc = red + 8;                           // [4][128]
         *reinterpret_cast<float4*>(sacc + warp * DH + 4 * lane) = a4;
-        __syncthreads();
-        const int d = threadIdx.x;
+        sync128();
+        const int d = tid;
         float a = (sacc[d] + sacc[DH + d]) + (sacc[2 * DH + d] + sacc[3 * DH + d]);
         for (int j = 0; j < hot; ++j) a += w[ns + j] * tail_v<FMT>(p, bh, n_full, j, d, ND);
         if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
         else if (mode == 1) acc_out[row * D + d] = a;
         else xacc[d] = a;
     } else {
-        for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        for (int d = tid; d < D; d += 128) {
             float a = 0.f;
-            for (int i = 0; i < ns; ++i) if (w[i] != 0.f) a += p.part_acc[slot(i) * D + d] * w[i];
+            for (int i = 0; i < ns; ++i) if (w[i] != 0.f) a += __ldcg(p.part_acc + slot(i) * D + d) * w[i];
             for (int j = 0; j < hot; ++j) a += w[ns + j] * tail_v<FMT>(p, bh, n_full, j, d, ND);
             if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
             else if (mode == 1) acc_out[row * D + d] = a;
             else xacc[d] = a;
         }
     }
+    M_o = M; L_o = Ls; e_o = e;
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int mode, __nv_bfloat16* out,
+                                                      float* m_out, float* l_out, float* acc_out) {
+    extern __shared__ float csm[];
+    const int bh = blockIdx.x, h = blockIdx.y, b = bh / p.Hkv, kvh = bh % p.Hkv;
+    const int G = p.G, D = p.D;
+    float M, Ls;
+    unsigned int e;
+    combine_row<FMT>(p, bh, h, mode, threadIdx.x, csm, true, out, acc_out, M, Ls, e);
+    const int64_t row = (int64_t)b * p.Hq + kvh * G + h;
+    const int rows = p.B * p.Hq;
     if (mode == 1 && threadIdx.x == 0) { m_out[row] = M; l_out[row] = Ls; }
     if (mode != 2) return;
     // ---- sequence-parallel exchange: publish this row, merge every rank's ----
@@ -912,6 +992,12 @@ size_t fast_smem_bytes() {
     return 1024 + NST * StageLayout<FMT>::BYTES + NWARP_C * 8 * PB_PITCH * 2 +
            (FMT == FMT_NVFP4 ? NWARP_C * 32 * 8 * 2 : 0) + sizeof(SmemCtl) + 16;
 }
+// Shared memory the folded merge may add (its slot weights and reduction
+// scratch live after SmemCtl); larger merges use the separate combine kernel.
+constexpr size_t FOLD_SMEM_MAX = 8192;
+// Workspace floats reserved at the start for the per-head completion
+// counters of the folded merge (plain decodes of up to this many B*Hkv heads).
+constexpr int64_t CNT_RESERVE = 4096;
 
 int num_sms(int* dev_out) {
     int dev = 0;
@@ -929,9 +1015,9 @@ int fast_occupancy(int dev) {
     if (!di.occ[k]) {
         const size_t smem = fast_smem_bytes<FMT>();
         if (cudaFuncSetAttribute(decode_fast_kernel<FMT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem) != cudaSuccess ||
+                                 (int)(smem + FOLD_SMEM_MAX)) != cudaSuccess ||
             cudaFuncSetAttribute(decode_fast_kernel<FMT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem) != cudaSuccess)
+                                 (int)(smem + FOLD_SMEM_MAX)) != cudaSuccess)
             return 0;
         int occ = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_fast_kernel<FMT, false>, NTHREADS, smem) !=
@@ -990,8 +1076,17 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     const int occ = fast ? (fmt == FMT_NVFP4 ? fast_occupancy<FMT_NVFP4>(dev) : fast_occupancy<FMT_INT4>(dev)) : 4;
     if (!occ) return record_cuda_error(cudaGetLastError());
     const Plan pl = make_plan(BH, n_full, sms, occ);   // varlen: bounds from the max length S
-    const int64_t need = pl.slots * G * (2 + (int64_t)D) + (seq_lens ? BH + 2 : 0);
+    const int64_t part_floats = pl.slots * G * (2 + (int64_t)D);
+    const int64_t need = pl.W > 0 ? CNT_RESERVE + part_floats + (seq_lens ? BH + 2 : 0) : 0;
     if (need > 0 && (!work || work_floats < need)) return KIVI_ERR_ARG;
+    // a head of T tiles touches at most ceil(T / floor(W/N)) + 1 CTAs
+    int max_ctas = 0;
+    if (pl.W > 0) {
+        const int64_t per = std::max<int64_t>(pl.W / pl.N, 1);
+        max_ctas = seq_lens ? pl.N + 1 : (int)((pl.T + per - 1) / per) + 1;
+    }
+    const size_t fold_bytes = ((size_t)max_ctas * NWARP_C + 16 + 8 + 4 * DH) * sizeof(float);
+    const bool fold = mode == 0 && fast && !seq_lens && !sp && BH <= CNT_RESERVE && fold_bytes <= FOLD_SMEM_MAX;
 
     DecodeParams p{};
     p.q = reinterpret_cast<const __nv_bfloat16*>(q); p.q_sb = q_sb; p.q_sh = q_sh;
@@ -1002,7 +1097,10 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     p.sm_scale = sm_scale; p.g_k = g_k; p.g_v = g_v;
     p.scale2 = sm_scale * 1.4426950408889634f * (fmt == FMT_NVFP4 ? g_k : 1.0f);
     p.T = pl.T; p.W = pl.W; p.N = pl.N;
-    p.part_m = work; p.part_l = work + pl.slots * G; p.part_acc = work + 2 * pl.slots * G;
+    float* parts = work ? work + CNT_RESERVE : nullptr;
+    p.part_m = parts; p.part_l = parts + pl.slots * G; p.part_acc = parts + 2 * pl.slots * G;
+    p.head_cnt = fold ? reinterpret_cast<int*>(work) : nullptr;
+    p.out = reinterpret_cast<__nv_bfloat16*>(out);
     p.err = err;
     p.seq_lens = seq_lens;
     p.v_hot = reinterpret_cast<const __nv_bfloat16*>(v_hot);
@@ -1010,7 +1108,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
         p.xbuf = sp->xbuf; p.peers = sp->peers; p.xW = sp->W; p.xrank = sp->rank;
         p.row_epoch = sp->row_epoch; p.timeout_ns = sp->timeout_ns;
     }
-    p.tile_off = seq_lens ? reinterpret_cast<int*>(work + pl.slots * G * (2 + (int64_t)D)) : nullptr;
+    p.tile_off = seq_lens ? reinterpret_cast<int*>(parts + part_floats) : nullptr;
     cudaStream_t st = (cudaStream_t)stream;
     if (seq_lens && pl.W > 0) {
         tile_offsets_kernel<<<1, 1024, 0, st>>>(seq_lens, B, Hkv, S, p.tile_off);
@@ -1038,26 +1136,22 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
                               CU_TENSOR_MAP_SWIZZLE_NONE);
             }
             if (!ok) return KIVI_ERR_CUDA;
+            const size_t fsm = fold ? fold_bytes : 0;
             if (fmt == FMT_NVFP4 && G <= 4)
-                decode_fast_kernel<FMT_NVFP4, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>(), st>>>(tkc, tks, tvc, tvs, p);
+                decode_fast_kernel<FMT_NVFP4, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>() + fsm, st>>>(tkc, tks, tvc, tvs, p);
             else if (fmt == FMT_NVFP4)
-                decode_fast_kernel<FMT_NVFP4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>(), st>>>(tkc, tks, tvc, tvs, p);
+                decode_fast_kernel<FMT_NVFP4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>() + fsm, st>>>(tkc, tks, tvc, tvs, p);
             else if (G <= 4)
-                decode_fast_kernel<FMT_INT4, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>(), st>>>(tkc, tks, tvc, tvs, p);
+                decode_fast_kernel<FMT_INT4, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>() + fsm, st>>>(tkc, tks, tvc, tvs, p);
             else
-                decode_fast_kernel<FMT_INT4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>(), st>>>(tkc, tks, tvc, tvs, p);
+                decode_fast_kernel<FMT_INT4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>() + fsm, st>>>(tkc, tks, tvc, tvs, p);
         } else {
             if (fmt == FMT_NVFP4) decode_generic_kernel<FMT_NVFP4><<<pl.N, 128, 0, st>>>(p);
             else decode_generic_kernel<FMT_INT4><<<pl.N, 128, 0, st>>>(p);
         }
         int e = check_launch();
         if (e) return e;
-    }
-    // a head of T tiles touches at most ceil(T / floor(W/N)) + 1 CTAs
-    int max_ctas = 0;
-    if (pl.W > 0) {
-        const int64_t per = std::max<int64_t>(pl.W / pl.N, 1);
-        max_ctas = seq_lens ? pl.N + 1 : (int)((pl.T + per - 1) / per) + 1;
+        if (fold) return KIVI_OK;                      // the decode kernel merged every head itself
     }
     const size_t csm = ((size_t)max_ctas * NWARP_C + 16 + 8 + 4 * DH) * sizeof(float);
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
@@ -1086,7 +1180,8 @@ extern "C" int64_t kivi_decode_workspace_floats(int B, int Hq, int Hkv, int S, i
     int sms = num_sms(nullptr);
     if (!sms) sms = 148;
     const Plan pl = make_plan(B * Hkv, (S / BLK) * BLK, sms, MAX_CTAS_PER_SM);
-    return pl.slots * (Hq / Hkv) * (2 + (int64_t)D) + B * Hkv + 2;   // + varlen tile table
+    // merge counters + partial slots + varlen tile table
+    return CNT_RESERVE + pl.slots * (Hq / Hkv) * (2 + (int64_t)D) + B * Hkv + 2;
 }
 
 extern "C" int kivi_decode_varlen(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,

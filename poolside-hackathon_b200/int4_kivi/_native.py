@@ -203,11 +203,13 @@ def poll_errors(device) -> None:
         st["event"] = ev
 
 
-def workspace(device, n_floats: int) -> torch.Tensor:
-    """Grow-only scratch buffer for decode partials, one per (device, stream)."""
-    key = (device_index(device), torch.cuda.current_stream(device).cuda_stream)
+def workspace(device, n_floats: int, kind: str = "decode") -> torch.Tensor:
+    """Grow-only scratch buffer for decode partials, one per (device, stream,
+    kind).  Zero-filled when allocated: kivi_decode keeps self-resetting
+    per-head counters at its start, which must read zero before first use."""
+    key = (device_index(device), torch.cuda.current_stream(device).cuda_stream, kind)
     w = _work_cache.get(key)
     if w is None or w.numel() < n_floats:
-        w = torch.empty(max(n_floats, 1), dtype=torch.float32, device=device)
+        w = torch.zeros(max(n_floats, 1), dtype=torch.float32, device=device)
         _work_cache[key] = w
     return w

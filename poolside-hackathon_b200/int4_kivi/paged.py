@@ -127,7 +127,7 @@ def _decode(fmt, q, kv_cache, block_table, seq_lens, sm_scale, out=None):
         raise ValueError(f"out must be contiguous bf16 or fp32 [{B}, {Hq}, {D}]")
     L = N.lib()
     need = L.kivi_paged_decode_workspace_floats(B, Hq, H, bt.shape[1], D)
-    work = N.workspace(q.device, need)
+    work = N.workspace(q.device, need, kind="paged")
     entry = L.kivi_paged_decode if out.dtype == torch.bfloat16 else L.kivi_paged_decode_f32
     N.check(entry(N.ptr(q), q.stride(0), q.stride(1), N.ptr(kv_cache), kv_cache.shape[0], N.ptr(bt),
                                 bt.shape[1], N.ptr(sl), B, Hq, H, D, N.FMT[fmt], float(sm_scale), N.ptr(out),

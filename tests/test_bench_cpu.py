@@ -25,6 +25,6 @@ def test_reference_arm_prints_contract_line():
     # the reference's own kv_quant + SDPA when baseline/_ref holds the reference
     # install, else the oracle port; always on every host core
     want = "reference" if os.path.exists(os.path.join(ROOT, "baseline", "_ref", "kv_quant.py")) else "port"
-    assert d["cpu_baseline"]["kind"] == want and d["cpu_baseline"]["cores"] == os.cpu_count()
+    assert d["cpu_baseline"]["kind"] == want and d["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert "workload" in d["config"]
