@@ -130,12 +130,8 @@ int kivi_page_dequant(const uint8_t *packed, const void *scale, int rows, int to
 /*           fmt INT4: fp16 scales; NVFP4: e4m3 scales with g_k, g_v.        */
 /* S       : tokens attended (n_full = (S/16)*16 from pages, rest from k_hot)*/
 /* out     : bf16 [B, Hq, D] contiguous.                                     */
-/* work    : fp32 scratch of kivi_decode_workspace_floats(...) floats,      */
-/*           zero-filled once before its first use: its first 4096 words are*/
-/*           per-head completion counters of the merge (folded into the     */
-/*           decode kernel for plain decodes), which every call leaves at   */
-/*           zero again.  Re-zero it after a call that returned or flagged  */
-/*           an error.  Calls sharing one workspace must not overlap.       */
+/* work    : fp32 scratch of kivi_decode_workspace_floats(...) floats      */
+/*           (any contents; calls sharing one workspace must not overlap).   */
 /* err     : optional int32 device flag, set nonzero on a device timeout.    */
 /* Fast path requirements: D == 128, Hq/Hkv <= 8, k_np_stride % 16 == 0,     */
 /* v_s_stride % 16 == 0, 16-byte aligned pointers; otherwise a generic       */

@@ -65,10 +65,6 @@ struct DecodeParams {
     int xW, xrank;                   // ranks in the exchange, this rank
     unsigned int* row_epoch;
     long long timeout_ns;
-    // merge folded into the decode kernel (plain decode, uniform lengths):
-    // per-head completion counters (zero between launches) and the bf16 out
-    int* head_cnt;
-    __nv_bfloat16* out;
 };
 
 struct SeqPar {
@@ -161,17 +157,6 @@ __global__ void __launch_bounds__(1024) tile_offsets_kernel(const int* seq_lens,
     if (t == 1023) tile_off[BH] = part[1023];
 }
 
-__host__ __device__ inline void head_cta_range(int64_t a0, int64_t a1, int64_t W, int N, int& c_lo, int& c_hi) {
-    // CTA c owns tiles [floor(cW/N), floor((c+1)W/N)).  c_lo is the last CTA
-    // whose slice starts at or before a0 (floor(cW/N) <= a0 <=> cW < (a0+1)N),
-    // c_hi the last whose slice starts before a1 (cW < a1 N).
-    c_lo = 0; c_hi = -1;
-    if (W <= 0 || a1 <= a0) return;
-    const int64_t lo = ((a0 + 1) * N - 1) / W, hi = (a1 * N - 1) / W;
-    c_lo = (int)(lo < N - 1 ? lo : N - 1);
-    c_hi = (int)(hi < N - 1 ? hi : N - 1);
-}
-
 template <int FMT>
 struct StageLayout {
     static constexpr int KC = 0;                        // 128 ch x 64 B, 64B-swizzled
@@ -182,11 +167,10 @@ struct StageLayout {
     static constexpr uint32_t TX = (FMT == FMT_NVFP4) ? (8192 + 2048 + 8192 + 1024) : 20480;
 };
 
-struct __align__(16) SmemCtl {
+struct __align__(8) SmemCtl {
     uint64_t full[NST];
     uint64_t empty[NST];
     int abort;
-    int fold_last;
 };
 
 __device__ __forceinline__ void set_err(int* err, int code) {
@@ -276,51 +260,6 @@ __device__ __forceinline__ void split_prod(uint32_t q, uint32_t sc, uint32_t& hi
 
 __device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
     return row * 64u + 16u * (chunk ^ ((row >> 1) & 3u));
-}
-
-template <int FMT>
-__device__ __forceinline__ void combine_row(const DecodeParams& p, int bh, int h, int mode, int tid, float* csm,
-                                            bool dep_wait, __nv_bfloat16* out, float* acc_out, float& M_o,
-                                            float& L_o, unsigned int& e_o);
-__device__ __forceinline__ void sync128();
-
-// The split-K merge folded into the decode kernel (plain decode of equal
-// lengths).  Once its tile loop is over -- normally or through a timed-out
-// wait, so every consumer warp gets here -- a CTA counts itself done on each
-// head it touched; the CTA that completes a head's count merges that head's
-// rows (its partial slots and bf16 hot tail) into the bf16 output and resets
-// the counter to zero for the next launch.  Each writer fences its partial
-// stores before the count, the merging CTA fences after it and reads the
-// partials at L2.
-template <int FMT>
-__device__ __forceinline__ void fold_merges(const DecodeParams& p, int64_t i0, int64_t i1, float* csm, int* last_s,
-                                         int tid) {
-    __threadfence();
-    sync128();
-    const int h_first = (int)(i0 / p.T), h_last = (int)((i1 - 1) / p.T);
-    for (int bh = h_first; bh <= h_last; ++bh) {
-        if (tid == 0) {
-            int c_lo, c_hi;
-            head_cta_range((int64_t)bh * p.T, (int64_t)(bh + 1) * p.T, p.W, p.N, c_lo, c_hi);
-            const int done = atomicAdd(p.head_cnt + bh, 1) + 1;
-            const int last = done == c_hi - c_lo + 1;
-            if (last) {
-                atomicExch(p.head_cnt + bh, 0);
-                __threadfence();
-            }
-            sts32s(smem_u32(last_s), (uint32_t)last);
-        }
-        sync128();
-        const bool last = lds32s(smem_u32(last_s)) != 0;
-        sync128();
-        if (!last) continue;
-        for (int h = 0; h < p.G; ++h) {
-            float M, L;
-            unsigned int e;
-            combine_row<FMT>(p, bh, h, 0, tid, csm, false, p.out, nullptr, M, L, e);
-            sync128();                                   // csm is reused by the next row
-        }
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -545,26 +484,28 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
             }
             // ----------------------------- softmax ----------------------------
             // ca: tokens 4g (c0,c1), 4g+1 (c2,c3); cb: 4g+2, 4g+3; heads 2tq(+1)
+            // raw scores; the softmax scale (> 0, log2 units) is applied in
+            // the exp2 argument and to the running maxima
             float x[8] = {ca[0], ca[2], cb[0], cb[2], ca[1], ca[3], cb[1], cb[3]};
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x[e] *= p.scale2;
             if (MASKED) {
                 const int tk[4] = {4 * g, 4 * g + 1, 4 * g + 2, 4 * g + 3};
 #pragma unroll
                 for (int e = 0; e < 8; ++e) if (tk[e & 3] >= limit) x[e] = -INFINITY;
             }
-            float mx0 = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-            float mx1 = fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7]));
-#pragma unroll
-            for (int o = 4; o < 32; o <<= 1) {
-                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-            }
+            float mx0 = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])) * p.scale2;
+            float mx1 = fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7])) * p.scale2;
             // Lazy rescaling: the running reference max only moves when a new
             // score exceeds it by more than 2^8 (p stays <= 256, exact in the
-            // final normalisation since l uses the same reference).
+            // final normalisation since l uses the same reference).  A lane's
+            // own maxima decide whether any head of the warp needs it; only
+            // then are the maxima reduced over the head's lanes.
             const bool need = (mx0 > m0 + 8.f) || (mx1 > m1 + 8.f);
             if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+                }
                 const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
                 const float al0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - mn0);
                 const float al1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - mn1);
@@ -577,7 +518,10 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
             const float r0 = (m0 == -INFINITY) ? 0.f : m0, r1 = (m1 == -INFINITY) ? 0.f : m1;
             float pr[8];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) { pr[e] = exp2f(x[e] - r0); pr[4 + e] = exp2f(x[4 + e] - r1); }
+            for (int e = 0; e < 4; ++e) {
+                pr[e] = exp2f(fmaf(x[e], p.scale2, -r0));
+                pr[4 + e] = exp2f(fmaf(x[4 + e], p.scale2, -r1));
+            }
             l0 += (pr[0] + pr[1]) + (pr[2] + pr[3]);
             l1 += (pr[4] + pr[5]) + (pr[6] + pr[7]);
             // stage P as fp16 [head][token] for the PV B-fragments
@@ -630,10 +574,6 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
         if (lane == 0) mbar_arrive(&ctl->empty[s]);
     }
     if (cur >= 0 && !lds32s(abort_s)) flush(cur);
-    if (p.head_cnt) {
-        fold_merges<FMT>(p, i0, i1, reinterpret_cast<float*>(ctl + 1), &ctl->fold_last, warp * 32 + lane);
-        return;
-    }
     // let the dependent merge kernel start its prologue (programmatic launch)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
@@ -735,6 +675,17 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeParams 
 // reduces its channels over the slots with coalesced loads.
 // mode 0 -> normalised bf16 out; mode 1 -> merged (m, l, acc) records.
 // ---------------------------------------------------------------------------
+__host__ __device__ inline void head_cta_range(int64_t a0, int64_t a1, int64_t W, int N, int& c_lo, int& c_hi) {
+    // CTA c owns tiles [floor(cW/N), floor((c+1)W/N)).  c_lo is the last CTA
+    // whose slice starts at or before a0 (floor(cW/N) <= a0 <=> cW < (a0+1)N),
+    // c_hi the last whose slice starts before a1 (cW < a1 N).
+    c_lo = 0; c_hi = -1;
+    if (W <= 0 || a1 <= a0) return;
+    const int64_t lo = ((a0 + 1) * N - 1) / W, hi = (a1 * N - 1) / W;
+    c_lo = (int)(lo < N - 1 ? lo : N - 1);
+    c_hi = (int)(hi < N - 1 ? hi : N - 1);
+}
+
 // V of tail token j (absolute n_full + j) at channel d: bf16 when the caller
 // keeps the partial page unquantised, else dequantised from v_packed.
 template <int FMT>
@@ -745,25 +696,14 @@ __device__ __forceinline__ float tail_v(const DecodeParams& p, int bh, int n_ful
     return gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
 }
 
-// 128 consumer threads of a CTA synchronise on named barrier 1 (the merge
-// runs both as its own kernel and at the end of the decode kernel, whose
-// producer warp has left by then).
-__device__ __forceinline__ void sync128() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// LSE merge of all partial slots of one (kv-head, q-head) row plus its bf16
-// hot tail, by 128 threads (tid = 0..127).  The slot weights exp2(m_s - M)
-// are computed once into shared memory (csm), then every thread reduces its
-// channels over the slots with coalesced loads.  mode 0 -> normalised bf16
-// out; mode 1 -> merged (m, l, acc) records; mode 2 -> this rank's state
-// into its exchange slot of epoch `e`.  Returns the row's M and L.
 template <int FMT>
-__device__ __forceinline__ void combine_row(const DecodeParams& p, int bh, int h, int mode, int tid, float* csm,
-                                            bool dep_wait, __nv_bfloat16* out, float* acc_out, float& M_o,
-                                            float& L_o, unsigned int& e_o) {
-    const int b = bh / p.Hkv, kvh = bh % p.Hkv;
+__global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int mode, __nv_bfloat16* out,
+                                                      float* m_out, float* l_out, float* acc_out) {
+    extern __shared__ float csm[];
+    const int bh = blockIdx.x, h = blockIdx.y, b = bh / p.Hkv, kvh = bh % p.Hkv;
     const int G = p.G, D = p.D, ND = D / BLK;
     const int Lh = head_len(p, bh), n_full = (Lh / BLK) * BLK, hot = Lh - n_full;
-    const int warp = tid >> 5, lane = tid & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int c_lo = 0, c_hi = -1;
     const int64_t Wt = total_tiles(p);
     const int64_t a0 = head_tile0(p, bh), a1 = head_tile0(p, bh + 1);
@@ -784,7 +724,7 @@ __device__ __forceinline__ void combine_row(const DecodeParams& p, int bh, int h
     }
     // partial slots are produced by the split kernel launched just before
     // (programmatic dependent launch): wait for its results to be visible
-    if (dep_wait) asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     auto slot = [&](int i) -> int64_t {
         return ((int64_t)(c_lo + i / NWARP_C + bh) * NWARP_C + (i % NWARP_C)) * G + h;
     };
@@ -793,30 +733,29 @@ __device__ __forceinline__ void combine_row(const DecodeParams& p, int bh, int h
         const int64_t cc = c_lo + i / NWARP_C;
         return tile_start(cc, Wt, p.N) < tile_start(cc + 1, Wt, p.N);
     };
-    // partials of other CTAs: read at L2 (never a line this SM cached earlier)
-    for (int i = tid; i < ns; i += 128) w[i] = live(i) ? __ldcg(p.part_m + slot(i)) : -INFINITY;
-    sync128();
+    for (int i = threadIdx.x; i < ns; i += blockDim.x) w[i] = live(i) ? p.part_m[slot(i)] : -INFINITY;
+    __syncthreads();
     // M = max over slots and hot tokens
     float M = -INFINITY;
-    for (int i = tid; i < ns + hot; i += 128) M = fmaxf(M, w[i]);
+    for (int i = threadIdx.x; i < ns + hot; i += blockDim.x) M = fmaxf(M, w[i]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     if (lane == 0) red[warp] = M;
-    sync128();
+    __syncthreads();
     M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
     const float Mr = (M == -INFINITY) ? 0.f : M;
-    sync128();
+    __syncthreads();
     // weights and L
     float Ls = 0.f;
-    for (int i = tid; i < ns + hot; i += 128) {
+    for (int i = threadIdx.x; i < ns + hot; i += blockDim.x) {
         const float e = exp2f(w[i] - Mr);
-        Ls += (i < ns) ? (e != 0.f ? __ldcg(p.part_l + slot(i)) * e : 0.f) : e;
+        Ls += (i < ns) ? (e != 0.f ? p.part_l[slot(i)] * e : 0.f) : e;
         w[i] = e;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, o);
     if (lane == 0) red[4 + warp] = Ls;
-    sync128();
+    __syncthreads();
     Ls = (red[4] + red[5]) + (red[6] + red[7]);
     const int64_t row = (int64_t)b * p.Hq + kvh * G + h;
     const int rows = p.B * p.Hq;
@@ -837,7 +776,7 @@ __device__ __forceinline__ void combine_row(const DecodeParams& p, int bh, int h
             for (int u = 0; u < 4; ++u) {
                 const int i = i0 + 4 * u;
                 wi[u] = i < ns ? w[i] : 0.f;
-                v4[u] = wi[u] != 0.f ? __ldcg(reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane))
+                v4[u] = wi[u] != 0.f ? *reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane)
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
@@ -847,37 +786,23 @@ __device__ __forceinline__ void combine_row(const DecodeParams& p, int bh, int h
         }
         float* sacc = red + 8;                           // [4][128]
         *reinterpret_cast<float4*>(sacc + warp * DH + 4 * lane) = a4;
-        sync128();
-        const int d = tid;
+        __syncthreads();
+        const int d = threadIdx.x;
         float a = (sacc[d] + sacc[DH + d]) + (sacc[2 * DH + d] + sacc[3 * DH + d]);
         for (int j = 0; j < hot; ++j) a += w[ns + j] * tail_v<FMT>(p, bh, n_full, j, d, ND);
         if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
         else if (mode == 1) acc_out[row * D + d] = a;
         else xacc[d] = a;
     } else {
-        for (int d = tid; d < D; d += 128) {
+        for (int d = threadIdx.x; d < D; d += blockDim.x) {
             float a = 0.f;
-            for (int i = 0; i < ns; ++i) if (w[i] != 0.f) a += __ldcg(p.part_acc + slot(i) * D + d) * w[i];
+            for (int i = 0; i < ns; ++i) if (w[i] != 0.f) a += p.part_acc[slot(i) * D + d] * w[i];
             for (int j = 0; j < hot; ++j) a += w[ns + j] * tail_v<FMT>(p, bh, n_full, j, d, ND);
             if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
             else if (mode == 1) acc_out[row * D + d] = a;
             else xacc[d] = a;
         }
     }
-    M_o = M; L_o = Ls; e_o = e;
-}
-
-template <int FMT>
-__global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int mode, __nv_bfloat16* out,
-                                                      float* m_out, float* l_out, float* acc_out) {
-    extern __shared__ float csm[];
-    const int bh = blockIdx.x, h = blockIdx.y, b = bh / p.Hkv, kvh = bh % p.Hkv;
-    const int G = p.G, D = p.D;
-    float M, Ls;
-    unsigned int e;
-    combine_row<FMT>(p, bh, h, mode, threadIdx.x, csm, true, out, acc_out, M, Ls, e);
-    const int64_t row = (int64_t)b * p.Hq + kvh * G + h;
-    const int rows = p.B * p.Hq;
     if (mode == 1 && threadIdx.x == 0) { m_out[row] = M; l_out[row] = Ls; }
     if (mode != 2) return;
     // ---- sequence-parallel exchange: publish this row, merge every rank's ----
@@ -992,12 +917,6 @@ size_t fast_smem_bytes() {
     return 1024 + NST * StageLayout<FMT>::BYTES + NWARP_C * 8 * PB_PITCH * 2 +
            (FMT == FMT_NVFP4 ? NWARP_C * 32 * 8 * 2 : 0) + sizeof(SmemCtl) + 16;
 }
-// Shared memory the folded merge may add (its slot weights and reduction
-// scratch live after SmemCtl); larger merges use the separate combine kernel.
-constexpr size_t FOLD_SMEM_MAX = 8192;
-// Workspace floats reserved at the start for the per-head completion
-// counters of the folded merge (plain decodes of up to this many B*Hkv heads).
-constexpr int64_t CNT_RESERVE = 4096;
 
 int num_sms(int* dev_out) {
     int dev = 0;
@@ -1015,9 +934,9 @@ int fast_occupancy(int dev) {
     if (!di.occ[k]) {
         const size_t smem = fast_smem_bytes<FMT>();
         if (cudaFuncSetAttribute(decode_fast_kernel<FMT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)(smem + FOLD_SMEM_MAX)) != cudaSuccess ||
+                                 (int)smem) != cudaSuccess ||
             cudaFuncSetAttribute(decode_fast_kernel<FMT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)(smem + FOLD_SMEM_MAX)) != cudaSuccess)
+                                 (int)smem) != cudaSuccess)
             return 0;
         int occ = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_fast_kernel<FMT, false>, NTHREADS, smem) !=
@@ -1067,7 +986,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     const int sms = num_sms(&dev);
     if (!sms) return record_cuda_error(cudaGetLastError());
 
-    const bool fast = D == DH && G <= 8 && k_np_stride % 16 == 0 && v_s_stride % 16 == 0 &&
+    const bool fast = D == DH && G <= 8 && sm_scale > 0.0f && k_np_stride % 16 == 0 && v_s_stride % 16 == 0 &&
                       (uintptr_t)k_packed % 16 == 0 && (uintptr_t)k_scale % 16 == 0 &&
                       (uintptr_t)v_packed % 16 == 0 && (uintptr_t)v_scale % 16 == 0 &&
                       q_sh % 2 == 0 && (uintptr_t)q % 4 == 0 && n_full > 0 &&
@@ -1076,17 +995,8 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     const int occ = fast ? (fmt == FMT_NVFP4 ? fast_occupancy<FMT_NVFP4>(dev) : fast_occupancy<FMT_INT4>(dev)) : 4;
     if (!occ) return record_cuda_error(cudaGetLastError());
     const Plan pl = make_plan(BH, n_full, sms, occ);   // varlen: bounds from the max length S
-    const int64_t part_floats = pl.slots * G * (2 + (int64_t)D);
-    const int64_t need = pl.W > 0 ? CNT_RESERVE + part_floats + (seq_lens ? BH + 2 : 0) : 0;
+    const int64_t need = pl.slots * G * (2 + (int64_t)D) + (seq_lens ? BH + 2 : 0);
     if (need > 0 && (!work || work_floats < need)) return KIVI_ERR_ARG;
-    // a head of T tiles touches at most ceil(T / floor(W/N)) + 1 CTAs
-    int max_ctas = 0;
-    if (pl.W > 0) {
-        const int64_t per = std::max<int64_t>(pl.W / pl.N, 1);
-        max_ctas = seq_lens ? pl.N + 1 : (int)((pl.T + per - 1) / per) + 1;
-    }
-    const size_t fold_bytes = ((size_t)max_ctas * NWARP_C + 16 + 8 + 4 * DH) * sizeof(float);
-    const bool fold = mode == 0 && fast && !seq_lens && !sp && BH <= CNT_RESERVE && fold_bytes <= FOLD_SMEM_MAX;
 
     DecodeParams p{};
     p.q = reinterpret_cast<const __nv_bfloat16*>(q); p.q_sb = q_sb; p.q_sh = q_sh;
@@ -1097,10 +1007,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     p.sm_scale = sm_scale; p.g_k = g_k; p.g_v = g_v;
     p.scale2 = sm_scale * 1.4426950408889634f * (fmt == FMT_NVFP4 ? g_k : 1.0f);
     p.T = pl.T; p.W = pl.W; p.N = pl.N;
-    float* parts = work ? work + CNT_RESERVE : nullptr;
-    p.part_m = parts; p.part_l = parts + pl.slots * G; p.part_acc = parts + 2 * pl.slots * G;
-    p.head_cnt = fold ? reinterpret_cast<int*>(work) : nullptr;
-    p.out = reinterpret_cast<__nv_bfloat16*>(out);
+    p.part_m = work; p.part_l = work + pl.slots * G; p.part_acc = work + 2 * pl.slots * G;
     p.err = err;
     p.seq_lens = seq_lens;
     p.v_hot = reinterpret_cast<const __nv_bfloat16*>(v_hot);
@@ -1108,7 +1015,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
         p.xbuf = sp->xbuf; p.peers = sp->peers; p.xW = sp->W; p.xrank = sp->rank;
         p.row_epoch = sp->row_epoch; p.timeout_ns = sp->timeout_ns;
     }
-    p.tile_off = seq_lens ? reinterpret_cast<int*>(parts + part_floats) : nullptr;
+    p.tile_off = seq_lens ? reinterpret_cast<int*>(work + pl.slots * G * (2 + (int64_t)D)) : nullptr;
     cudaStream_t st = (cudaStream_t)stream;
     if (seq_lens && pl.W > 0) {
         tile_offsets_kernel<<<1, 1024, 0, st>>>(seq_lens, B, Hkv, S, p.tile_off);
@@ -1136,22 +1043,26 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
                               CU_TENSOR_MAP_SWIZZLE_NONE);
             }
             if (!ok) return KIVI_ERR_CUDA;
-            const size_t fsm = fold ? fold_bytes : 0;
             if (fmt == FMT_NVFP4 && G <= 4)
-                decode_fast_kernel<FMT_NVFP4, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>() + fsm, st>>>(tkc, tks, tvc, tvs, p);
+                decode_fast_kernel<FMT_NVFP4, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>(), st>>>(tkc, tks, tvc, tvs, p);
             else if (fmt == FMT_NVFP4)
-                decode_fast_kernel<FMT_NVFP4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>() + fsm, st>>>(tkc, tks, tvc, tvs, p);
+                decode_fast_kernel<FMT_NVFP4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>(), st>>>(tkc, tks, tvc, tvs, p);
             else if (G <= 4)
-                decode_fast_kernel<FMT_INT4, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>() + fsm, st>>>(tkc, tks, tvc, tvs, p);
+                decode_fast_kernel<FMT_INT4, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>(), st>>>(tkc, tks, tvc, tvs, p);
             else
-                decode_fast_kernel<FMT_INT4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>() + fsm, st>>>(tkc, tks, tvc, tvs, p);
+                decode_fast_kernel<FMT_INT4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>(), st>>>(tkc, tks, tvc, tvs, p);
         } else {
             if (fmt == FMT_NVFP4) decode_generic_kernel<FMT_NVFP4><<<pl.N, 128, 0, st>>>(p);
             else decode_generic_kernel<FMT_INT4><<<pl.N, 128, 0, st>>>(p);
         }
         int e = check_launch();
         if (e) return e;
-        if (fold) return KIVI_OK;                      // the decode kernel merged every head itself
+    }
+    // a head of T tiles touches at most ceil(T / floor(W/N)) + 1 CTAs
+    int max_ctas = 0;
+    if (pl.W > 0) {
+        const int64_t per = std::max<int64_t>(pl.W / pl.N, 1);
+        max_ctas = seq_lens ? pl.N + 1 : (int)((pl.T + per - 1) / per) + 1;
     }
     const size_t csm = ((size_t)max_ctas * NWARP_C + 16 + 8 + 4 * DH) * sizeof(float);
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
@@ -1180,8 +1091,7 @@ extern "C" int64_t kivi_decode_workspace_floats(int B, int Hq, int Hkv, int S, i
     int sms = num_sms(nullptr);
     if (!sms) sms = 148;
     const Plan pl = make_plan(B * Hkv, (S / BLK) * BLK, sms, MAX_CTAS_PER_SM);
-    // merge counters + partial slots + varlen tile table
-    return CNT_RESERVE + pl.slots * (Hq / Hkv) * (2 + (int64_t)D) + B * Hkv + 2;
+    return pl.slots * (Hq / Hkv) * (2 + (int64_t)D) + B * Hkv + 2;   // + varlen tile table
 }
 
 extern "C" int kivi_decode_varlen(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,

@@ -205,8 +205,7 @@ def poll_errors(device) -> None:
 
 def workspace(device, n_floats: int, kind: str = "decode") -> torch.Tensor:
     """Grow-only scratch buffer for decode partials, one per (device, stream,
-    kind).  Zero-filled when allocated: kivi_decode keeps self-resetting
-    per-head counters at its start, which must read zero before first use."""
+    kind: the contiguous and the paged decode keep separate ones)."""
     key = (device_index(device), torch.cuda.current_stream(device).cuda_stream, kind)
     w = _work_cache.get(key)
     if w is None or w.numel() < n_floats:
