@@ -89,15 +89,23 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
         uint2* sc = reinterpret_cast<uint2*>(st_smem);                              // [ppc][D+1]
         uint16_t* ss = reinterpret_cast<uint16_t*>(sc + (size_t)ppc * (D + 1));     // [ppc][D+2]
         const T* src = k + h * a.sk_h + (int64_t)p0 * BLK * a.sk_s;
-        for (int b = tid; b < np_here * D; b += 256) {
+        auto kload = [&](int b, float (&x)[BLK]) {
             const int p = b / D, c = b - p * D;
-            float x[BLK];
             load_strided16<T>(src + (int64_t)p * BLK * a.sk_s + c * a.sk_d, a.sk_s, x);
+        };
+        float x[BLK];
+        if (tid < np_here * D) kload(tid, x);
+        for (int b = tid; b < np_here * D; b += 256) {
+            float xn[BLK];                               // next block's loads in flight
+            if (b + 256 < np_here * D) kload(b + 256, xn);
+            const int p = b / D, c = b - p * D;
             uint2 pk;
             uint16_t sb;
             quant_pack<FMT>(x, a.calib_k, a.alphas, a.n_alphas, a.g_k, pk, sb);
             sc[p * (D + 1) + c] = pk;
             ss[p * (D + 2) + c] = sb;
+#pragma unroll
+            for (int e = 0; e < BLK; ++e) x[e] = xn[e];
         }
         __syncthreads();
         for (int b = tid; b < np_here * D; b += 256) {
@@ -110,20 +118,124 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
         return;
     }
     const int64_t nv = (int64_t)a.H * a.S_v * ND;
-    const int nv_ctas = gridDim.x - nk_ctas;
-    for (int64_t j = (int64_t)(blockIdx.x - nk_ctas) * 256 + tid; j < nv; j += (int64_t)nv_ctas * 256) {
+    const int64_t vstride = (int64_t)(gridDim.x - nk_ctas) * 256;
+    auto vload = [&](int64_t j, float (&x)[BLK]) {
         const int db = (int)(j % ND);
         const int64_t r = j / ND;
         const int t = (int)(r % a.S_v), h = (int)(r / a.S_v);
-        float x[BLK];
+        load_contig16<T>(v + h * a.sv_h + t * a.sv_s + (int64_t)db * BLK * a.sv_d, a.sv_d, x);
+    };
+    const int64_t j0 = (int64_t)(blockIdx.x - nk_ctas) * 256 + tid;
+    float x[BLK];
+    if (j0 < nv) vload(j0, x);
+    for (int64_t j = j0; j < nv; j += vstride) {
+        float xn[BLK];                                   // next block's loads in flight
+        if (j + vstride < nv) vload(j + vstride, xn);
+        const int db = (int)(j % ND);
+        const int64_t r = j / ND;
+        const int t = (int)(r % a.S_v), h = (int)(r / a.S_v);
         uint2 pk;
         uint16_t sb;
-        load_contig16<T>(v + h * a.sv_h + t * a.sv_s + (int64_t)db * BLK * a.sv_d, a.sv_d, x);
         quant_pack<FMT>(x, a.calib_v, a.alphas, a.n_alphas, a.g_v, pk, sb);
+#pragma unroll
+        for (int e = 0; e < BLK; ++e) x[e] = xn[e];
         const int64_t row = ((int64_t)h * a.v_s_stride + a.vtok0 + t) * ND + db;
         reinterpret_cast<uint2*>(a.v_packed)[row] = pk;
         if (FMT == FMT_NVFP4) reinterpret_cast<uint8_t*>(a.v_scale)[row] = (uint8_t)sb;
         else reinterpret_cast<uint16_t*>(a.v_scale)[row] = sb;
+    }
+}
+
+// Small MSE stores (the per-step append): one warp per block, the clip ratios
+// of the search spread over the lanes (lane a evaluates ratio a, a + 32, ...)
+// and the first-index argmin found with shuffles, so a few blocks do not
+// leave one thread running the whole 32-ratio search.  Same arithmetic per
+// ratio as calibrate16 / nvfp4_calibrate16 and the same tie rule (the first
+// ratio with the smallest error; no finite error gives scale 0).
+template <typename T, int FMT>
+__global__ void __launch_bounds__(256) store_warp_kernel(StoreArgs a) {
+    const T* k = reinterpret_cast<const T*>(a.k);
+    const T* v = reinterpret_cast<const T*>(a.v);
+    const int D = a.D, ND = D / BLK, NP = a.S_k / BLK;
+    const int lane = threadIdx.x & 31;
+    const int64_t nk = (int64_t)a.H * NP * D, nv = (int64_t)a.H * a.S_v * ND;
+    const int64_t wid = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t i = wid; i < nk + nv; i += nwarps) {
+        const bool isk = i < nk;
+        float x[BLK];
+        int calib;
+        float g;
+        int64_t row;
+        if (isk) {
+            const int d = (int)(i % D);
+            const int64_t r = i / D;
+            const int p = (int)(r % NP), h = (int)(r / NP);
+            load_strided16<T>(k + h * a.sk_h + (int64_t)p * BLK * a.sk_s + d * a.sk_d, a.sk_s, x);
+            calib = a.calib_k; g = a.g_k;
+            row = ((int64_t)h * D + d) * a.k_np_stride + a.kpage0 + p;
+        } else {
+            const int64_t j = i - nk;
+            const int db = (int)(j % ND);
+            const int64_t r = j / ND;
+            const int t = (int)(r % a.S_v), h = (int)(r / a.S_v);
+            load_contig16<T>(v + h * a.sv_h + t * a.sv_s + (int64_t)db * BLK * a.sv_d, a.sv_d, x);
+            calib = a.calib_v; g = a.g_v;
+            row = ((int64_t)h * a.v_s_stride + a.vtok0 + t) * ND + db;
+        }
+        const float amax = absmax16(x);
+        const float qmax = FMT == FMT_NVFP4 ? 6.0f : 7.0f;
+        // this lane's best ratio: (error, ratio index, scale, e4m3 byte)
+        float best = __int_as_float(0x7f800000), bs = 0.0f;
+        int bi = 0x7fffffff;
+        uint32_t bsc = 0;
+        // INT4 absmax takes amax / 7 as is; every other case searches (NVFP4
+        // absmax too: its one candidate passes the same finite-error test)
+        const int nA = calib == CAL_ABSMAX ? 1 : a.n_alphas;
+        for (int al = lane; al < nA && !(FMT != FMT_NVFP4 && calib == CAL_ABSMAX); al += 32) {
+            float s = calib == CAL_ABSMAX ? __fdiv_rn(amax, qmax) : __fdiv_rn(__fmul_rn(a.alphas[al], amax), qmax);
+            uint32_t sc = 0;
+            if (FMT == FMT_NVFP4) {
+                sc = f32_to_e4m3(__fdiv_rn(s, g));
+                s = __fmul_rn(e4m3_to_f32((uint8_t)sc), g);
+            }
+            const float err = block_err(x, s, FMT);
+            if (err < best) { best = err; bs = s; bi = al; bsc = sc; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+            const uint32_t oc = __shfl_xor_sync(0xffffffffu, bsc, o);
+            if (ob < best || (ob == best && oi < bi)) { best = ob; bi = oi; bs = os; bsc = oc; }
+        }
+        if (!(best < __int_as_float(0x7f800000))) { bs = 0.0f; bsc = 0; }   // no finite error
+        if (FMT != FMT_NVFP4 && calib == CAL_ABSMAX) bs = __fdiv_rn(amax, qmax);
+        // lanes 0..15 quantise one element each; the nibbles are OR-reduced
+        uint32_t nib = 0;
+        float xl = x[0];
+#pragma unroll
+        for (int e = 1; e < BLK; ++e) xl = lane == e ? x[e] : xl;
+        if (lane < BLK) {
+            if (FMT == FMT_NVFP4) {
+                if (bs != 0.0f) {
+                    const float y = quot_for_grid(xl, bs, __frcp_rn(bs), FMT_NVFP4);
+                    nib = (uint32_t)e2m1_index(fabsf(y)) | (y < 0.0f ? 8u : 0u);
+                }
+            } else {
+                nib = (uint32_t)(int)q_grid_div(xl, bs, __frcp_rn(bs), FMT) & 0xFu;
+            }
+        }
+        const uint32_t lo = __reduce_or_sync(0xffffffffu, lane < 8 ? nib << (4 * lane) : 0u);
+        const uint32_t hi = __reduce_or_sync(0xffffffffu, (lane >= 8 && lane < BLK) ? nib << (4 * (lane - 8)) : 0u);
+        if (lane == 0) {
+            uint8_t* pk = isk ? a.k_packed : a.v_packed;
+            void* sp = isk ? a.k_scale : a.v_scale;
+            reinterpret_cast<uint2*>(pk)[row] = make_uint2(lo, hi);
+            if (FMT == FMT_NVFP4) reinterpret_cast<uint8_t*>(sp)[row] = (uint8_t)bsc;
+            else reinterpret_cast<uint16_t*>(sp)[row] = __half_as_ushort(__float2half_rn(bs));
+        }
     }
 }
 
@@ -297,6 +409,10 @@ static int grid_for(int64_t n) {
 using namespace kivi;
 
 namespace {
+// Up to this many blocks an MSE store runs one warp per block (the search
+// spread over lanes); above it one thread per block fills the GPU anyway.
+constexpr int64_t SMALL_MSE_BLOCKS = 148LL * 64;
+
 template <typename T, int FMT>
 int launch_store(const StoreArgs& a, cudaStream_t st) {
     const int NP = a.S_k / BLK, ND = a.D / BLK;
@@ -310,6 +426,12 @@ int launch_store(const StoreArgs& a, cudaStream_t st) {
     int64_t nv_ctas = (nv + 255) / 256;
     if (nv_ctas > 148LL * 16) nv_ctas = 148LL * 16;
     if (nk_ctas64 + nv_ctas > 0x7fffffffLL) return KIVI_ERR_UNSUPPORTED;
+    const int64_t nblocks = (int64_t)a.H * NP * a.D + nv;
+    if ((a.calib_k == CAL_MSE || a.calib_v == CAL_MSE) && nblocks <= SMALL_MSE_BLOCKS) {
+        const int64_t ctas = (nblocks + 7) / 8;              // 8 warps, one block each
+        store_warp_kernel<T, FMT><<<(int)ctas, 256, 0, st>>>(a);
+        return check_launch();
+    }
     const size_t smem = nk_ctas64 > 0 ? store_smem<T>(a.D, ppc) : 0;
     if (smem > 48 * 1024) {
         int dev = 0;
