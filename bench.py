@@ -707,6 +707,86 @@ def serving_main(args, rank: int, world: int, local: int) -> None:
         os._exit(0)
 
 
+def serving_attention_main(args, rank: int, world: int, local: int) -> None:
+    """Config 3's KV read alone, sharded the way the attention op shards:
+    batch 1..256, lengths U[1K, 32K] (the same seeded draw as the model
+    sweep), 24 layers of decode attention per step, no dense layers.  The
+    (sequence, kv-head group) units of plan_shards go to the ranks -- by
+    sequence, and by kv-head group too when the batch is smaller than the
+    world -- so every GPU streams about the same bytes and no rank talks to
+    another.  Each rank's units are one varlen decode per layer (captured in
+    a CUDA graph); the step time is the max over ranks."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from int4_kivi import store_kivi
+    from int4_kivi.decode import decode_packed
+    from int4_kivi.distributed import plan_shards
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    L_ = SERVE_LAYERS
+    G = HQ // HKV
+    rng = np.random.default_rng(3)
+    results = {}
+    for Bg in (1, 2, 4, 8, 16, 32, 64, 128, 256):
+        lens_all = rng.integers(1024, 32769, size=Bg).tolist()
+        units = plan_shards(lens_all, HKV, world)[rank]
+        hg = units[0][2] - units[0][1] if units else HKV
+        lens = [lens_all[b] for b, _, _ in units] or [16]
+        Bu, S_max = len(lens), max(lens)
+        per_layer = Bu * hg * S_max * BYTES_PER_TOKEN_HEAD
+        n_caches = L_ if per_layer * L_ <= 40e9 else 1
+        caches = []
+        for li in range(n_caches):
+            g = torch.Generator(device=dev).manual_seed(1000 * Bg + li + 77 * rank)
+            k = torch.randn(Bu * hg, S_max, D, device=dev, generator=g).bfloat16()
+            v = torch.randn(Bu * hg, S_max, D, device=dev, generator=g).bfloat16()
+            c = store_kivi(k, v, "absmax", "absmax")
+            khot = torch.zeros(Bu * hg, 16, D, dtype=torch.bfloat16, device=dev)
+            for u, Lb in enumerate(lens):
+                nf = (Lb // 16) * 16
+                if Lb > nf:
+                    khot[u * hg:(u + 1) * hg, :Lb - nf] = k[u * hg:(u + 1) * hg, nf:Lb]
+            del k, v
+            caches.append(dict(k_packed=c.k_packed, k_scale=c.k_scale, k_hot=khot, v_packed=c.v_packed,
+                               v_scale=c.v_scale, H=hg, S=S_max, D=D, B=Bu,
+                               seq_lens=torch.tensor(lens, dtype=torch.int32, device=dev)))
+        q = torch.randn(Bu, hg * G, D, device=dev).bfloat16()
+        out = torch.empty(Bu, hg * G, D, dtype=torch.bfloat16, device=dev)
+
+        def step():
+            for li in range(L_):
+                decode_packed(q, caches[li % n_caches], hg * G, out=out)
+        gr = graph_step(step)
+        ms = time_graph(gr, seconds=0.5)
+        t = torch.tensor([ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+        kv_bytes = sum(lens_all) * HKV * BYTES_PER_TOKEN_HEAD * L_
+        results[Bg] = {"ms_per_step": round(ms, 4), "tok_s": round(Bg / ms * 1e3, 1),
+                       "kv_GB_s": round(kv_bytes / ms / 1e6, 1), "kv_heads_per_unit": hg,
+                       "units_on_rank0": len(units) if rank == 0 else None}
+        del gr, caches
+        torch.cuda.empty_cache()
+    if rank == 0:
+        line = {"metric": "decode tok/s of the 24-layer KV read alone (INT4-KIVI, serving sweep)",
+                "value": results[256]["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": None,
+                "warmup": 3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "int4 KV, f16 MMA, f32 accumulate", "data": "synthetic (seeded lengths U[1K,32K])",
+                "config": {"workload": "c3 attention-only sweep", "layers": L_,
+                           "parallelism": f"plan_shards x{world}: sequences, and kv-head groups when B < GPUs; "
+                                          "no collective"},
+                "sweep": results}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        sys.stdout.flush()
+        os._exit(0)
+
+
 def paged_main(args, rank: int, world: int, local: int) -> None:
     """The paged vLLM block layout: B=8 sequences per GPU of --seq tokens in a
     shuffled block table, INT4 (or --fmt nvfp4) paged decode per step; CUDA
@@ -787,9 +867,11 @@ def main():
     ap.add_argument("--merge", default="fused", choices=["fused", "p2p", "nccl"],
                     help="longctx: merge the partial states inside the decode's combine kernel over NVLink "
                          "peer memory, with separate publish/merge launches over peer memory, or by NCCL")
-    ap.add_argument("--workload", default="batch", choices=["batch", "longctx", "serving", "paged"],
+    ap.add_argument("--workload", default="batch", choices=["batch", "longctx", "serving", "serving-attn", "paged"],
                     help="batch: B=8 sequences per GPU (weak scaling, no collective); "
-                         "longctx: one 262144-token sequence split across GPUs with an NCCL (m,l,o) merge")
+                         "longctx: one 262144-token sequence split across GPUs, (m,l,o) merged over NVLink; "
+                         "serving: the config-3 model sweep; serving-attn: its KV read alone, sharded by "
+                         "sequence and kv-head group")
     args = ap.parse_args()
     S = args.seq
     rank = int(os.environ.get("RANK", "0"))
@@ -801,6 +883,8 @@ def main():
         return longctx_main(args, rank, world, local)
     if args.workload == "serving" and args.impl == "ours":
         return serving_main(args, rank, world, local)
+    if args.workload == "serving-attn" and args.impl == "ours":
+        return serving_attention_main(args, rank, world, local)
     if args.workload == "paged" and args.impl == "ours":
         return paged_main(args, rank, world, local)
     if args.impl == "reference":
