@@ -91,7 +91,7 @@ __device__ __forceinline__ void quant_pack(const float x[BLK], int calib, const 
 // V blocks (16 channels of one token) are contiguous in the input and in the
 // output, so V CTAs take one block per thread directly.
 // Grid: [0, nk_ctas) K chunks (head-major), then V CTAs (grid-stride).
-template <typename T, int FMT>
+template <typename T, int FMT, bool ANY_MSE>
 __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_chunks, int nk_ctas) {
     extern __shared__ __align__(16) uint8_t st_smem[];
     const T* k = reinterpret_cast<const T*>(a.k);
@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
             load_strided16<T>(src + (int64_t)p * BLK * a.sk_s + c * a.sk_d, a.sk_s, x);
             uint2 pk;
             uint16_t sb;
-            quant_pack<FMT>(x, a.calib_k, a.alphas, a.n_alphas, a.g_k, pk, sb);
+            quant_pack<FMT>(x, ANY_MSE ? a.calib_k : (int)CAL_ABSMAX, a.alphas, a.n_alphas, a.g_k, pk, sb);
             sc[p * (D + 1) + c] = pk;
             ss[p * (D + 2) + c] = sb;
         }
@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
         uint2 pk;
         uint16_t sb;
         load_contig16<T>(v + h * a.sv_h + t * a.sv_s + (int64_t)db * BLK * a.sv_d, a.sv_d, x);
-        quant_pack<FMT>(x, a.calib_v, a.alphas, a.n_alphas, a.g_v, pk, sb);
+        quant_pack<FMT>(x, ANY_MSE ? a.calib_v : (int)CAL_ABSMAX, a.alphas, a.n_alphas, a.g_v, pk, sb);
         const int64_t row = ((int64_t)h * a.v_s_stride + a.vtok0 + t) * ND + db;
         reinterpret_cast<uint2*>(a.v_packed)[row] = pk;
         if (FMT == FMT_NVFP4) reinterpret_cast<uint8_t*>(a.v_scale)[row] = (uint8_t)sb;
@@ -236,7 +236,8 @@ __global__ void __launch_bounds__(256) store_warp_kernel(StoreArgs a) {
 }
 
 // Pages per K chunk: 16 (a 32-byte run of fp16 scales per channel), fewer
-// for wide heads so the staged output stays within 40 KB of shared memory.
+// for wide heads so the staged output stays within 40 KB of shared memory
+// (under the 48 KB a launch gets without opting in).
 template <typename T>
 static int store_ppc(int D) {
     const int p = 40960 / (D * 10 + 18);
@@ -428,22 +429,13 @@ int launch_store(const StoreArgs& a, cudaStream_t st) {
         store_warp_kernel<T, FMT><<<(int)ctas, 256, 0, st>>>(a);
         return check_launch();
     }
+    // the staged K output stays within 48 KB (store_ppc), no opt-in needed
     const size_t smem = nk_ctas64 > 0 ? store_smem<T>(a.D, ppc) : 0;
-    if (smem > 48 * 1024) {
-        int dev = 0;
-        cudaError_t e = cudaGetDevice(&dev);
-        if (e != cudaSuccess) return record_cuda_error(e);
-        static int set_bytes[64];                  // largest size configured, per device
-        if (dev >= 0 && dev < 64 && set_bytes[dev] < (int)smem) {
-            e = cudaFuncSetAttribute(store_kernel<T, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return record_cuda_error(e);
-            set_bytes[dev] = (int)smem;
-        } else if (dev < 0 || dev >= 64) {
-            e = cudaFuncSetAttribute(store_kernel<T, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return record_cuda_error(e);
-        }
-    }
-    store_kernel<T, FMT><<<(int)(nk_ctas64 + nv_ctas), 256, smem, st>>>(a, ppc, n_chunks, (int)nk_ctas64);
+    const unsigned grid = (unsigned)(nk_ctas64 + nv_ctas);
+    if (a.calib_k == CAL_MSE || a.calib_v == CAL_MSE)
+        store_kernel<T, FMT, true><<<grid, 256, smem, st>>>(a, ppc, n_chunks, (int)nk_ctas64);
+    else   // absmax only: the MSE search is compiled out, fewer registers, more resident threads
+        store_kernel<T, FMT, false><<<grid, 256, smem, st>>>(a, ppc, n_chunks, (int)nk_ctas64);
     return check_launch();
 }
 }  // namespace
