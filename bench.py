@@ -861,6 +861,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq", type=int, default=65536)
+    ap.add_argument("--headline-only", action="store_true",
+                    help="time the headline decode only (no config 4, other configs or CPU baseline): "
+                         "the command the ncu summaries capture")
     ap.add_argument("--fmt", default="int4", choices=["int4", "nvfp4"], help="paged workload format")
     ap.add_argument("--layout", default="contiguous", choices=["contiguous", "paged"],
                     help="serving: KV cache layout (paged = the vLLM block layout of config 3)")
@@ -970,6 +973,16 @@ def main():
     ms, ms_e2e = t.tolist()
     del st
     torch.cuda.empty_cache()
+    if args.headline_only:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": round(world * packed_bytes / (ms * 1e-3) / 1e9, 2),
+                              "unit": "GB/s", "n_gpus": world, "steps": args.steps, "ms_per_step": round(ms, 4),
+                              "higher_is_better": True, "config": {"workload": workload},
+                              "note": "headline only (profiling run)"}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     # config 4 on the same ranks: one 262144-token sequence split across them
     c4 = longctx_measure("fused", 200, args.warmup, rank, world, dev)
     if rank == 0:

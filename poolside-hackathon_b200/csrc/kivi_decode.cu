@@ -733,7 +733,27 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         const int64_t cc = c_lo + i / NWARP_C;
         return tile_start(cc, Wt, p.N) < tile_start(cc + 1, Wt, p.N);
     };
-    for (int i = threadIdx.x; i < ns; i += blockDim.x) w[i] = live(i) ? p.part_m[slot(i)] : -INFINITY;
+    // One round trip for every partial the row needs: m and l of all slots,
+    // and (the long-sequence path) the first acc vectors of this warp's slots,
+    // all issued before any of them is used.  Partials of another kernel are
+    // read at L2.
+    float* wl = w + ns + 16 + 8 + 4 * DH;                // [ns] l of each slot
+    for (int i = threadIdx.x; i < ns; i += blockDim.x) {
+        const bool lv = live(i);
+        w[i] = lv ? __ldcg(p.part_m + slot(i)) : -INFINITY;
+        wl[i] = lv ? __ldcg(p.part_l + slot(i)) : 0.f;
+    }
+    constexpr int PRE = 8;                               // slots per warp loaded up front
+    float4 pre[PRE];
+    const bool wide = D == DH && ns >= 16;
+    if (wide) {
+#pragma unroll
+        for (int u = 0; u < PRE; ++u) {
+            const int i = warp + 4 * u;
+            pre[u] = (i < ns && live(i)) ? __ldcg(reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
     __syncthreads();
     // M = max over slots and hot tokens
     float M = -INFINITY;
@@ -749,7 +769,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     float Ls = 0.f;
     for (int i = threadIdx.x; i < ns + hot; i += blockDim.x) {
         const float e = exp2f(w[i] - Mr);
-        Ls += (i < ns) ? (e != 0.f ? p.part_l[slot(i)] * e : 0.f) : e;
+        Ls += (i < ns) ? (e != 0.f ? wl[i] * e : 0.f) : e;
         w[i] = e;
     }
 #pragma unroll
@@ -765,18 +785,26 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         e = p.row_epoch[row] + 1;
         xacc = xslot(p.xbuf, p.xW, rows, D, e) + 2 * rows + row * D;
     }
-    if (D == DH && ns >= 16) {
-        // many slots (long single sequences): warps split the slots, each lane
-        // owns 4 channels (float4 loads), then a shared-memory reduction
+    if (wide) {
+        // many slots (long sequences): warp w takes slots w, w + 4, ...; each
+        // lane owns 4 channels (float4), then a shared-memory reduction
         float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int i0 = warp; i0 < ns; i0 += 16) {        // four loads in flight per iteration
+#pragma unroll
+        for (int u = 0; u < PRE; ++u) {
+            const int i = warp + 4 * u;
+            const float wi = i < ns ? w[i] : 0.f;
+            if (wi != 0.f) {
+                a4.x += pre[u].x * wi; a4.y += pre[u].y * wi; a4.z += pre[u].z * wi; a4.w += pre[u].w * wi;
+            }
+        }
+        for (int i0 = warp + 4 * PRE; i0 < ns; i0 += 16) {   // four loads in flight per iteration
             float4 v4[4];
             float wi[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int i = i0 + 4 * u;
                 wi[u] = i < ns ? w[i] : 0.f;
-                v4[u] = wi[u] != 0.f ? *reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane)
+                v4[u] = wi[u] != 0.f ? __ldcg(reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane))
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
@@ -796,7 +824,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     } else {
         for (int d = threadIdx.x; d < D; d += blockDim.x) {
             float a = 0.f;
-            for (int i = 0; i < ns; ++i) if (w[i] != 0.f) a += p.part_acc[slot(i) * D + d] * w[i];
+            for (int i = 0; i < ns; ++i) if (w[i] != 0.f) a += __ldcg(p.part_acc + slot(i) * D + d) * w[i];
             for (int j = 0; j < hot; ++j) a += w[ns + j] * tail_v<FMT>(p, bh, n_full, j, d, ND);
             if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
             else if (mode == 1) acc_out[row * D + d] = a;
@@ -827,13 +855,13 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         if (ok) {
             float Mx = -INFINITY;
             for (int j = 0; j < p.xW; ++j)
-                Mx = fmaxf(Mx, xslot(reinterpret_cast<uint8_t*>(p.peers[j]), p.xW, rows, D, e)[row]);
+                Mx = fmaxf(Mx, __ldcg(xslot(reinterpret_cast<uint8_t*>(p.peers[j]), p.xW, rows, D, e) + row));
             const float Mxr = (Mx == -INFINITY) ? 0.f : Mx;
             float Lx = 0.f;
             for (int j = 0; j < p.xW; ++j) {
                 const float* sj = xslot(reinterpret_cast<uint8_t*>(p.peers[j]), p.xW, rows, D, e);
-                x_w[j] = exp2f(sj[row] - Mxr);
-                Lx += sj[rows + row] * x_w[j];
+                x_w[j] = exp2f(__ldcg(sj + row) - Mxr);
+                Lx += __ldcg(sj + rows + row) * x_w[j];
             }
             x_l = Lx;
             p.row_epoch[row] = e;
@@ -844,7 +872,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float a = 0.f;
         for (int j = 0; j < p.xW; ++j)
-            a += xslot(reinterpret_cast<uint8_t*>(p.peers[j]), p.xW, rows, D, e)[2 * rows + row * D + d] * x_w[j];
+            a += __ldcg(xslot(reinterpret_cast<uint8_t*>(p.peers[j]), p.xW, rows, D, e) + 2 * rows + row * D + d) * x_w[j];
         out[row * D + d] = __float2bfloat16_rn(x_l > 0.f ? a / x_l : 0.f);
     }
 }
@@ -1064,7 +1092,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
         const int64_t per = std::max<int64_t>(pl.W / pl.N, 1);
         max_ctas = seq_lens ? pl.N + 1 : (int)((pl.T + per - 1) / per) + 1;
     }
-    const size_t csm = ((size_t)max_ctas * NWARP_C + 16 + 8 + 4 * DH) * sizeof(float);
+    const size_t csm = ((size_t)2 * max_ctas * NWARP_C + 16 + 8 + 4 * DH) * sizeof(float);
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
     const dim3 cgrid(BH, G);
     cudaLaunchConfig_t cfg = {};

@@ -34,6 +34,16 @@ __device__ __forceinline__ void load_contig16(const T* __restrict__ p, int64_t s
     }
 }
 
+// The two 16-bit values of a 32-bit word (element 2i in the low half) as fp32.
+template <typename T> __device__ __forceinline__ float lo16_f32(uint32_t w);
+template <typename T> __device__ __forceinline__ float hi16_f32(uint32_t w);
+template <> __device__ __forceinline__ float lo16_f32<__nv_bfloat16>(uint32_t w) { return __uint_as_float(w << 16); }
+template <> __device__ __forceinline__ float hi16_f32<__nv_bfloat16>(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+template <> __device__ __forceinline__ float lo16_f32<__half>(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
+template <> __device__ __forceinline__ float hi16_f32<__half>(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+template <> __device__ __forceinline__ float lo16_f32<float>(uint32_t) { return 0.f; }
+template <> __device__ __forceinline__ float hi16_f32<float>(uint32_t) { return 0.f; }
+
 // Quantise one block into 8 packed bytes; returns the stored scale bits.
 template <int FMT>
 __device__ __forceinline__ void quant_pack(const float x[BLK], int calib, const float* alphas,
@@ -104,15 +114,42 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
         uint2* sc = reinterpret_cast<uint2*>(st_smem);                              // [ppc][D+1]
         uint16_t* ss = reinterpret_cast<uint16_t*>(sc + (size_t)ppc * (D + 1));     // [ppc][D+2]
         const T* src = k + h * a.sk_h + (int64_t)p0 * BLK * a.sk_s;
-        for (int b = tid; b < np_here * D; b += 256) {
-            const int p = b / D, c = b - p * D;
-            float x[BLK];
-            load_strided16<T>(src + (int64_t)p * BLK * a.sk_s + c * a.sk_d, a.sk_s, x);
-            uint2 pk;
-            uint16_t sb;
-            quant_pack<FMT>(x, ANY_MSE ? a.calib_k : (int)CAL_ABSMAX, a.alphas, a.n_alphas, a.g_k, pk, sb);
-            sc[p * (D + 1) + c] = pk;
-            ss[p * (D + 2) + c] = sb;
+        const int calib = ANY_MSE ? a.calib_k : (int)CAL_ABSMAX;
+        if (sizeof(T) == 2 && a.sk_d == 1 && a.sk_s % 2 == 0 && (reinterpret_cast<uintptr_t>(src) & 3) == 0) {
+            // a thread takes a channel pair: each token load is one 32-bit word
+            // (a 128-byte row segment across the warp) and feeds two blocks
+            const int npair = D / 2;
+            for (int b = tid; b < np_here * npair; b += 256) {
+                const int p = b / npair, c = 2 * (b - p * npair);
+                uint32_t raw[BLK];
+#pragma unroll
+                for (int j = 0; j < BLK; ++j)
+                    raw[j] = __ldg(reinterpret_cast<const uint32_t*>(src + ((int64_t)p * BLK + j) * a.sk_s + c));
+                float x[BLK];
+                uint2 pk;
+                uint16_t sb;
+#pragma unroll
+                for (int j = 0; j < BLK; ++j) x[j] = lo16_f32<T>(raw[j]);
+                quant_pack<FMT>(x, calib, a.alphas, a.n_alphas, a.g_k, pk, sb);
+                sc[p * (D + 1) + c] = pk;
+                ss[p * (D + 2) + c] = sb;
+#pragma unroll
+                for (int j = 0; j < BLK; ++j) x[j] = hi16_f32<T>(raw[j]);
+                quant_pack<FMT>(x, calib, a.alphas, a.n_alphas, a.g_k, pk, sb);
+                sc[p * (D + 1) + c + 1] = pk;
+                ss[p * (D + 2) + c + 1] = sb;
+            }
+        } else {
+            for (int b = tid; b < np_here * D; b += 256) {
+                const int p = b / D, c = b - p * D;
+                float x[BLK];
+                load_strided16<T>(src + (int64_t)p * BLK * a.sk_s + c * a.sk_d, a.sk_s, x);
+                uint2 pk;
+                uint16_t sb;
+                quant_pack<FMT>(x, calib, a.alphas, a.n_alphas, a.g_k, pk, sb);
+                sc[p * (D + 1) + c] = pk;
+                ss[p * (D + 2) + c] = sb;
+            }
         }
         __syncthreads();
         for (int b = tid; b < np_here * D; b += 256) {
@@ -126,6 +163,36 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
     }
     const int64_t nv = (int64_t)a.H * a.S_v * ND;
     const int nv_ctas = gridDim.x - nk_ctas;
+    const int calib_v = ANY_MSE ? a.calib_v : (int)CAL_ABSMAX;
+    if (sizeof(T) == 2 && a.sv_d == 1 && ND % 2 == 0 && (a.sv_s * 2) % 16 == 0 && (a.sv_h * 2) % 16 == 0 &&
+        (reinterpret_cast<uintptr_t>(v) & 15) == 0) {
+        // a thread takes two neighbouring blocks of one token: 64 contiguous
+        // bytes in four 16-byte loads, all in flight before either is used
+        const int64_t npairs = nv / 2;
+        for (int64_t q = (int64_t)(blockIdx.x - nk_ctas) * 256 + tid; q < npairs; q += (int64_t)nv_ctas * 256) {
+            const int db = (int)(2 * q % ND);
+            const int64_t r = 2 * q / ND;
+            const int t = (int)(r % a.S_v), h = (int)(r / a.S_v);
+            const uint4* src = reinterpret_cast<const uint4*>(v + h * a.sv_h + t * a.sv_s + (int64_t)db * BLK);
+            const uint4 r0 = __ldg(src), r1 = __ldg(src + 1), r2 = __ldg(src + 2), r3 = __ldg(src + 3);
+            const int64_t row = ((int64_t)h * a.v_s_stride + a.vtok0 + t) * ND + db;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const uint4 u0 = half ? r2 : r0, u1 = half ? r3 : r1;
+                const uint32_t wds[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+                float x[BLK];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) { x[2 * e] = lo16_f32<T>(wds[e]); x[2 * e + 1] = hi16_f32<T>(wds[e]); }
+                uint2 pk;
+                uint16_t sb;
+                quant_pack<FMT>(x, calib_v, a.alphas, a.n_alphas, a.g_v, pk, sb);
+                reinterpret_cast<uint2*>(a.v_packed)[row + half] = pk;
+                if (FMT == FMT_NVFP4) reinterpret_cast<uint8_t*>(a.v_scale)[row + half] = (uint8_t)sb;
+                else reinterpret_cast<uint16_t*>(a.v_scale)[row + half] = sb;
+            }
+        }
+        return;
+    }
     for (int64_t j = (int64_t)(blockIdx.x - nk_ctas) * 256 + tid; j < nv; j += (int64_t)nv_ctas * 256) {
         const int db = (int)(j % ND);
         const int64_t r = j / ND;
@@ -134,7 +201,7 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
         uint2 pk;
         uint16_t sb;
         load_contig16<T>(v + h * a.sv_h + t * a.sv_s + (int64_t)db * BLK * a.sv_d, a.sv_d, x);
-        quant_pack<FMT>(x, ANY_MSE ? a.calib_v : (int)CAL_ABSMAX, a.alphas, a.n_alphas, a.g_v, pk, sb);
+        quant_pack<FMT>(x, calib_v, a.alphas, a.n_alphas, a.g_v, pk, sb);
         const int64_t row = ((int64_t)h * a.v_s_stride + a.vtok0 + t) * ND + db;
         reinterpret_cast<uint2*>(a.v_packed)[row] = pk;
         if (FMT == FMT_NVFP4) reinterpret_cast<uint8_t*>(a.v_scale)[row] = (uint8_t)sb;
