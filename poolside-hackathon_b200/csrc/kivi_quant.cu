@@ -115,9 +115,11 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
         uint16_t* ss = reinterpret_cast<uint16_t*>(sc + (size_t)ppc * (D + 1));     // [ppc][D+2]
         const T* src = k + h * a.sk_h + (int64_t)p0 * BLK * a.sk_s;
         const int calib = ANY_MSE ? a.calib_k : (int)CAL_ABSMAX;
-        if (sizeof(T) == 2 && a.sk_d == 1 && a.sk_s % 2 == 0 && (reinterpret_cast<uintptr_t>(src) & 3) == 0) {
-            // a thread takes a channel pair: each token load is one 32-bit word
-            // (a 128-byte row segment across the warp) and feeds two blocks
+        if (!ANY_MSE && sizeof(T) == 2 && a.sk_d == 1 && a.sk_s % 2 == 0 &&
+            (reinterpret_cast<uintptr_t>(src) & 3) == 0) {
+            // absmax: a thread takes a channel pair, so each token load is one
+            // 32-bit word (a 128-byte row segment across the warp) feeding two
+            // blocks (the MSE search is ALU-bound and keeps one block per thread)
             const int npair = D / 2;
             for (int b = tid; b < np_here * npair; b += 256) {
                 const int p = b / npair, c = 2 * (b - p * npair);
@@ -164,10 +166,11 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
     const int64_t nv = (int64_t)a.H * a.S_v * ND;
     const int nv_ctas = gridDim.x - nk_ctas;
     const int calib_v = ANY_MSE ? a.calib_v : (int)CAL_ABSMAX;
-    if (sizeof(T) == 2 && a.sv_d == 1 && ND % 2 == 0 && (a.sv_s * 2) % 16 == 0 && (a.sv_h * 2) % 16 == 0 &&
-        (reinterpret_cast<uintptr_t>(v) & 15) == 0) {
-        // a thread takes two neighbouring blocks of one token: 64 contiguous
-        // bytes in four 16-byte loads, all in flight before either is used
+    if (!ANY_MSE && sizeof(T) == 2 && a.sv_d == 1 && ND % 2 == 0 && (a.sv_s * 2) % 16 == 0 &&
+        (a.sv_h * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0) {
+        // absmax: a thread takes two neighbouring blocks of one token, 64
+        // contiguous bytes in four 16-byte loads all in flight before either
+        // is used
         const int64_t npairs = nv / 2;
         for (int64_t q = (int64_t)(blockIdx.x - nk_ctas) * 256 + tid; q < npairs; q += (int64_t)nv_ctas * 256) {
             const int db = (int)(2 * q % ND);
