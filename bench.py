@@ -42,9 +42,9 @@ METRIC = "packed-KV HBM GB/s (INT4-KIVI fused decode, 64K ctx)"
 GPU_LAUNCHES_PER_STEP = 2           # split-K decode kernel + combine kernel
 REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode_fast_kernel launch
-# at the headline shape (65536 tokens, B=8), from a one-pass ncu capture of
-# that launch (gpu__time_duration + dram bytes) of the kernel as committed.
-TRAFFIC_PER_LAUNCH = 749.7e6
+# at the headline shape (65536 tokens, B=8): 701.72 MB + 3.94 MB from a
+# one-pass ncu capture of that launch (1.052 x the 671.1 MB algorithmic).
+TRAFFIC_PER_LAUNCH = 705.66e6
 # same for the paged decode kernel, a 16384-token capture scaled by tokens
 PAGED_TRAFFIC_16K = 155.28e6
 

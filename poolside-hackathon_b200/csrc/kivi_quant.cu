@@ -71,13 +71,19 @@ __device__ __forceinline__ void quant_pack(const float x[BLK], int calib, const 
             // [-7, 7] (no clamp), and y = x * r is within 2.2e-6 of the IEEE
             // quotient, so only |frac| within 1e-5 of one half needs the
             // exact division to round like kv_quant.
+            // Adding 1.5 * 2^23 rounds y to the nearest integer (ties to
+            // even, like rint) and leaves it, two's complement, in the low
+            // mantissa bits, so its nibble is inserted with one bit-field op.
+            constexpr float MAGIC = 12582912.0f;
 #pragma unroll
             for (int i = 0; i < BLK; ++i) {
-                float y = __fmul_rn(x[i], r);
-                float n = rintf(y);
-                if (fabsf(fabsf(y - n) - 0.5f) < 1e-5f) n = rintf(__fdiv_rn(x[i], s));
-                const uint32_t nib = (uint32_t)(int)n & 0xF;
-                if (i < 8) lo |= nib << (4 * i); else hi |= nib << (4 * (i - 8));
+                const float y = __fmul_rn(x[i], r);
+                float t = __fadd_rn(y, MAGIC);
+                if (fabsf(__fsub_rn(y, __fsub_rn(t, MAGIC))) > 0.5f - 1e-5f)
+                    t = __fadd_rn(__fdiv_rn(x[i], s), MAGIC);
+                uint32_t& w = i < 8 ? lo : hi;
+                const uint32_t pos = 4 * (i & 7);
+                asm("bfi.b32 %0, %1, %0, %2, 4;" : "+r"(w) : "r"(__float_as_uint(t)), "r"(pos));
             }
         } else {
 #pragma unroll
