@@ -728,8 +728,10 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     auto slot = [&](int i) -> int64_t {
         return ((int64_t)(c_lo + i / NWARP_C + bh) * NWARP_C + (i % NWARP_C)) * G + h;
     };
-    // an idle CTA (empty slice, possible on varlen grids) wrote no slots
+    // an idle CTA (empty slice, possible on varlen grids only: a uniform grid
+    // has no more CTAs than tiles) wrote no slots
     auto live = [&](int i) -> bool {
+        if (!p.tile_off) return true;
         const int64_t cc = c_lo + i / NWARP_C;
         return tile_start(cc, Wt, p.N) < tile_start(cc + 1, Wt, p.N);
     };
