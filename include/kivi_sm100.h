@@ -223,6 +223,28 @@ int kivi_decode_noalloc(const void *q, int64_t q_sb, int64_t q_sh,
                         float sm_scale, float g_k, float g_v,
                         void *out, int *err, kivi_stream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* Multi-query (speculative / chunked) decode: Tq query tokens per sequence, */
+/* query j at position q_pos + j of the cache attending tokens 0..q_pos + j  */
+/* (causal); q_pos + Tq <= S, so the queries' own K/V are already stored.    */
+/* The reference's decode takes one query token (int4_kivi/decode.py:439-   */
+/* 477 takes q [B, Hq, D]); this extends it the way a verify step of         */
+/* speculative decoding needs.  q bf16 [B, Tq, Hq, D] (strides q_sb, q_st,   */
+/* q_sh; last dim contiguous); out bf16 [B, Tq, Hq, D] contiguous; cache     */
+/* arguments as kivi_decode.  The (query, head) pairs of a kv head form the  */
+/* kernel's column group (Tq * Hq/Hkv <= 8 on the fast path, <= 16 on the    */
+/* CUDA-core path); work: kivi_decode_workspace_floats(B, Tq * Hq, Hkv, S,   */
+/* D) floats.                                                                */
+/* ------------------------------------------------------------------------ */
+int kivi_decode_multiquery(const void *q, int64_t q_sb, int64_t q_st, int64_t q_sh,
+                           const uint8_t *k_packed, const void *k_scale, int k_np_stride,
+                           const void *k_hot, int hot_stride,
+                           const uint8_t *v_packed, const void *v_scale, int v_s_stride,
+                           int B, int Tq, int q_pos, int Hq, int Hkv, int S, int D, int fmt,
+                           float sm_scale, float g_k, float g_v,
+                           void *out, float *work, int64_t work_floats, int *err,
+                           kivi_stream_t stream);
+
 /* Log-sum-exp merge of R partial records laid out [R, rows] / [R, rows, D]  */
 /* (int4_kivi/decode.py:320-340 semantics) -> bf16 out [rows, D].            */
 int kivi_lse_merge(const float *m, const float *l, const float *acc, int R, int rows,

@@ -39,6 +39,13 @@ constexpr int PB_PITCH = 40;     // halves per head row in the P staging buffer
 
 struct DecodeParams {
     const __nv_bfloat16* q; int64_t q_sb, q_sh;
+    // multi-query decode: Tq query tokens per sequence (stride q_st), the
+    // kernels' group G = Tq * Gq covers (query, head) pairs; Gq / Hq0 are the
+    // real GQA group and q-head count.  Tq = 1 is the plain decode.
+    int64_t q_st; int Tq, Gq, Hq0;
+    int mq;                  // 1: multi-query (per-query causal limits), 0: plain decode
+    int q_pos;               // multi-query: query j sits at q_pos + j and sees tokens 0 .. q_pos + j
+    int nf_real;             // full-page tokens of the cache (the split kernels may see fewer)
     const uint8_t* k_packed; const void* k_scale; int k_np_stride;
     const __nv_bfloat16* k_hot; int hot_stride;
     const uint8_t* v_packed; const void* v_scale; int v_s_stride;
@@ -95,6 +102,16 @@ __host__ __device__ inline int64_t tile_start(int64_t c, int64_t W, int N) { ret
 // read the sequence length of the head's batch entry.
 __device__ __forceinline__ int head_len(const DecodeParams& p, int bh) {
     return p.seq_lens ? min(max(p.seq_lens[bh / p.Hkv], 0), p.S) : p.S;
+}
+// q row and output row of (sequence b, kv head kvh, column qh of the group):
+// column qh is query token qh / Gq of head kvh * Gq + qh % Gq.
+__device__ __forceinline__ const __nv_bfloat16* q_row(const DecodeParams& p, int b, int kvh, int qh) {
+    const int j = qh / p.Gq, gh = qh - j * p.Gq;
+    return p.q + b * p.q_sb + j * p.q_st + (int64_t)(kvh * p.Gq + gh) * p.q_sh;
+}
+__device__ __forceinline__ int64_t out_row(const DecodeParams& p, int b, int kvh, int qh) {
+    const int j = qh / p.Gq, gh = qh - j * p.Gq;
+    return ((int64_t)b * p.Tq + j) * p.Hq0 + kvh * p.Gq + gh;
 }
 __device__ __forceinline__ int64_t total_tiles(const DecodeParams& p) {
     return p.tile_off ? (int64_t)p.tile_off[p.B * p.Hkv] : p.W;
@@ -384,7 +401,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
             for (int t = 0; t < 8; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
             const int b = bh / p.Hkv, kvh = bh % p.Hkv;
             const int qh = PAIRED ? (g & 3) : g;
-            const __nv_bfloat16* qp = p.q + b * p.q_sb + (int64_t)(kvh * G + qh) * p.q_sh;
+            const __nv_bfloat16* qp = q_row(p, b, kvh, qh < G ? qh : 0);
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
 #pragma unroll
@@ -627,7 +644,7 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeParams 
             const int b = bh / p.Hkv, kvh = bh % p.Hkv;
             for (int h = 0; h < G; ++h) {
                 m[h] = -INFINITY; l[h] = 0.f;
-                const __nv_bfloat16* qp = p.q + b * p.q_sb + (int64_t)(kvh * G + h) * p.q_sh;
+                const __nv_bfloat16* qp = q_row(p, b, kvh, h);
                 for (int e = 0; e < GEN_MAXC; ++e) {
                     const int d = lane + 32 * e;
                     q[h][e] = d < D ? __bfloat162float(qp[d]) : 0.f;
@@ -702,22 +719,38 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     extern __shared__ float csm[];
     const int bh = blockIdx.x, h = blockIdx.y, b = bh / p.Hkv, kvh = bh % p.Hkv;
     const int G = p.G, D = p.D, ND = D / BLK;
-    const int Lh = head_len(p, bh), n_full = (Lh / BLK) * BLK, hot = Lh - n_full;
+    const int Lh = head_len(p, bh), n_full = (Lh / BLK) * BLK;
+    // tail tokens [n_full, tail_end) merged here: the bf16 hot page; for a
+    // multi-query decode also the tokens past the pages every query sees, up
+    // to this query's own causal limit (a query at position S - Tq + j sees
+    // tokens 0 .. S - Tq + j)
+    const int hot = (p.mq ? p.q_pos + 1 + h / p.Gq : Lh) - n_full;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int c_lo = 0, c_hi = -1;
     const int64_t Wt = total_tiles(p);
     const int64_t a0 = head_tile0(p, bh), a1 = head_tile0(p, bh + 1);
     if (Wt > 0 && a1 > a0) head_cta_range(a0, a1, Wt, p.N, c_lo, c_hi);
     const int ns = (c_hi - c_lo + 1) * NWARP_C;          // partial slots of this head
-    float* w = csm;                                      // [ns + 16] weights (slots, then hot tokens)
-    float* red = csm + ns + 16;                          // [8] block reduction scratch
+    const int wcap = ns + ((16 + p.Tq - 1 + 3) & ~3);   // slots, then up to 15 + Tq - 1 tail tokens
+    float* w = csm;                                      // [wcap] weights (slots, then tail tokens)
+    float* red = csm + wcap;                             // [8] block reduction scratch
     const float sc2 = p.sm_scale * 1.4426950408889634f;
-    const __nv_bfloat16* qp = p.q + b * p.q_sb + (int64_t)(kvh * G + h) * p.q_sh;
-    // hot-tail scores (log2 units), one warp per token
+    const __nv_bfloat16* qp = q_row(p, b, kvh, h);
+    // K of tail token n_full + j at channel d: from the packed pages when it is
+    // in one (multi-query tails), else from the bf16 hot page
+    auto k_tail = [&](int j, int d) -> float {
+        const int t = n_full + j;
+        if (t < p.nf_real) {
+            const int64_t kr = ((int64_t)bh * D + d) * p.k_np_stride + t / BLK;
+            const uint32_t kb = p.k_packed[kr * PACKB + (t % BLK) / 2];
+            return gen_code<FMT>((kb >> (4 * (t & 1))) & 0xF) * gen_scale<FMT>(p.k_scale, kr, p.g_k);
+        }
+        return __bfloat162float(p.k_hot[((int64_t)bh * p.hot_stride + (t - p.nf_real)) * D + d]);
+    };
+    // tail scores (log2 units), one warp per token
     for (int j = warp; j < hot; j += 4) {
-        const __nv_bfloat16* kp = p.k_hot + ((int64_t)bh * p.hot_stride + j) * D;
         float sdot = 0.f;
-        for (int d = lane; d < D; d += 32) sdot += __bfloat162float(qp[d]) * __bfloat162float(kp[d]);
+        for (int d = lane; d < D; d += 32) sdot += __bfloat162float(qp[d]) * k_tail(j, d);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, o);
         if (lane == 0) w[ns + j] = sdot * sc2;
@@ -739,7 +772,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     // and (the long-sequence path) the first acc vectors of this warp's slots,
     // all issued before any of them is used.  Partials of another kernel are
     // read at L2.
-    float* wl = w + ns + 16 + 8 + 4 * DH;                // [ns] l of each slot
+    float* wl = w + wcap + 8 + 4 * DH;                   // [ns] l of each slot
     for (int i = threadIdx.x; i < ns; i += blockDim.x) {
         const bool lv = live(i);
         w[i] = lv ? __ldcg(p.part_m + slot(i)) : -INFINITY;
@@ -779,7 +812,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     if (lane == 0) red[4 + warp] = Ls;
     __syncthreads();
     Ls = (red[4] + red[5]) + (red[6] + red[7]);
-    const int64_t row = (int64_t)b * p.Hq + kvh * G + h;
+    const int64_t row = out_row(p, b, kvh, h);           // == b * Hq + kvh * G + h unless multi-query
     const int rows = p.B * p.Hq;
     unsigned int e = 0;
     float* xacc = nullptr;                               // mode 2: this row's acc in my slot
@@ -997,21 +1030,30 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
                 int S, int D, int fmt, float sm_scale, float g_k, float g_v, void* out, float* m_out,
                 float* l_out, float* acc_out, float* work, int64_t work_floats, int* err,
                 kivi_stream_t stream, const int* seq_lens = nullptr, const void* v_hot = nullptr,
-                const SeqPar* sp = nullptr) {
+                const SeqPar* sp = nullptr, int Tq = 1, int64_t q_st = 0, int q_pos = -1) {
     if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || S < 0 || D <= 0 || D % BLK) return KIVI_ERR_ARG;
     if (fmt != FMT_INT4 && fmt != FMT_NVFP4) return KIVI_ERR_ARG;
-    const int G = Hq / Hkv, BH = B * Hkv;
-    const int n_full = (S / BLK) * BLK, hot = S - n_full;
-    const int v_tokens = v_hot ? n_full : S;          // tokens v_packed must cover
-    if (k_np_stride < n_full / BLK || v_s_stride < v_tokens || (hot > 0 && hot_stride < hot)) return KIVI_ERR_ARG;
-    if (hot > 0 && v_hot && !k_hot) return KIVI_ERR_ARG;
+    const bool mq = q_pos >= 0;                       // multi-query decode
+    if (Tq < 1 || (!mq && Tq != 1) || (mq && (mode != 0 || seq_lens || v_hot || sp || q_pos + Tq > S)))
+        return KIVI_ERR_ARG;
+    const int Gq = Hq / Hkv, BH = B * Hkv;
+    const int G = Gq * Tq;                            // columns of the group: (query, head) pairs
+    const int nf_real = (S / BLK) * BLK, hot_real = S - nf_real;
+    // the split kernels see the page-aligned prefix every query attends; a
+    // multi-query decode's later tokens go to the merge with per-query limits
+    const int S_eff = mq ? ((q_pos + 1) / BLK) * BLK : S;
+    const int n_full = (S_eff / BLK) * BLK, hot = S_eff - n_full;
+    const int v_tokens = v_hot ? nf_real : S;         // tokens v_packed must cover
+    if (k_np_stride < nf_real / BLK || v_s_stride < v_tokens || (hot_real > 0 && hot_stride < hot_real))
+        return KIVI_ERR_ARG;
+    if (hot_real > 0 && v_hot && !k_hot) return KIVI_ERR_ARG;
     if (!q || (!out && mode != 1) || (mode == 1 && (!m_out || !l_out || !acc_out))) return KIVI_ERR_ARG;
     if (mode == 2 && (!sp || !sp->xbuf || !sp->peers || !sp->row_epoch || sp->W <= 0 || sp->W > 16 ||
                       sp->rank < 0 || sp->rank >= sp->W || sp->timeout_ns <= 0))
         return KIVI_ERR_ARG;
-    if (n_full > 0 && (!k_packed || !k_scale)) return KIVI_ERR_ARG;
+    if (nf_real > 0 && (!k_packed || !k_scale)) return KIVI_ERR_ARG;
     if (v_tokens > 0 && (!v_packed || !v_scale)) return KIVI_ERR_ARG;
-    if (hot > 0 && !k_hot) return KIVI_ERR_ARG;
+    if (hot_real > 0 && !k_hot) return KIVI_ERR_ARG;
     int dev = 0;
     const int sms = num_sms(&dev);
     if (!sms) return record_cuda_error(cudaGetLastError());
@@ -1019,7 +1061,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     const bool fast = D == DH && G <= 8 && sm_scale > 0.0f && k_np_stride % 16 == 0 && v_s_stride % 16 == 0 &&
                       (uintptr_t)k_packed % 16 == 0 && (uintptr_t)k_scale % 16 == 0 &&
                       (uintptr_t)v_packed % 16 == 0 && (uintptr_t)v_scale % 16 == 0 &&
-                      q_sh % 2 == 0 && (uintptr_t)q % 4 == 0 && n_full > 0 &&
+                      q_sh % 2 == 0 && q_st % 2 == 0 && (uintptr_t)q % 4 == 0 && n_full > 0 &&
                       (int64_t)BH * v_s_stride < (1LL << 31) && (int64_t)BH * D < (1LL << 31);
     if (!fast && (G > GEN_MAXG || D > 32 * GEN_MAXC)) return KIVI_ERR_UNSUPPORTED;
     const int occ = fast ? (fmt == FMT_NVFP4 ? fast_occupancy<FMT_NVFP4>(dev) : fast_occupancy<FMT_INT4>(dev)) : 4;
@@ -1030,10 +1072,11 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
 
     DecodeParams p{};
     p.q = reinterpret_cast<const __nv_bfloat16*>(q); p.q_sb = q_sb; p.q_sh = q_sh;
+    p.q_st = q_st; p.Tq = Tq; p.Gq = Gq; p.Hq0 = Hq; p.mq = mq; p.q_pos = q_pos; p.nf_real = nf_real;
     p.k_packed = k_packed; p.k_scale = k_scale; p.k_np_stride = k_np_stride;
     p.k_hot = reinterpret_cast<const __nv_bfloat16*>(k_hot); p.hot_stride = hot_stride;
     p.v_packed = v_packed; p.v_scale = v_scale; p.v_s_stride = v_s_stride;
-    p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.S = S; p.D = D; p.n_full = n_full; p.hot = hot;
+    p.B = B; p.Hq = Hkv * G; p.Hkv = Hkv; p.G = G; p.S = S_eff; p.D = D; p.n_full = n_full; p.hot = hot;
     p.sm_scale = sm_scale; p.g_k = g_k; p.g_v = g_v;
     p.scale2 = sm_scale * 1.4426950408889634f * (fmt == FMT_NVFP4 ? g_k : 1.0f);
     p.T = pl.T; p.W = pl.W; p.N = pl.N;
@@ -1094,7 +1137,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
         const int64_t per = std::max<int64_t>(pl.W / pl.N, 1);
         max_ctas = seq_lens ? pl.N + 1 : (int)((pl.T + per - 1) / per) + 1;
     }
-    const size_t csm = ((size_t)2 * max_ctas * NWARP_C + 16 + 8 + 4 * DH) * sizeof(float);
+    const size_t csm = ((size_t)2 * max_ctas * NWARP_C + ((16 + Tq - 1 + 3) & ~3) + 8 + 4 * DH) * sizeof(float);
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
     const dim3 cgrid(BH, G);
     cudaLaunchConfig_t cfg = {};
@@ -1144,6 +1187,19 @@ extern "C" int kivi_decode(const void* q, int64_t q_sb, int64_t q_sh, const uint
     return decode_impl(0, q, q_sb, q_sh, k_packed, k_scale, k_np_stride, k_hot, hot_stride, v_packed, v_scale,
                        v_s_stride, B, Hq, Hkv, S, D, fmt, sm_scale, g_k, g_v, out, nullptr, nullptr, nullptr,
                        work, work_floats, err, stream);
+}
+
+extern "C" int kivi_decode_multiquery(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh,
+                                      const uint8_t* k_packed, const void* k_scale, int k_np_stride,
+                                      const void* k_hot, int hot_stride, const uint8_t* v_packed,
+                                      const void* v_scale, int v_s_stride, int B, int Tq, int q_pos, int Hq,
+                                      int Hkv, int S, int D, int fmt, float sm_scale, float g_k, float g_v,
+                                      void* out, float* work, int64_t work_floats, int* err,
+                                      kivi_stream_t stream) {
+    if (Tq < 1 || q_pos < 0) return KIVI_ERR_ARG;
+    return decode_impl(0, q, q_sb, q_sh, k_packed, k_scale, k_np_stride, k_hot, hot_stride, v_packed, v_scale,
+                       v_s_stride, B, Hq, Hkv, S, D, fmt, sm_scale, g_k, g_v, out, nullptr, nullptr, nullptr,
+                       work, work_floats, err, stream, nullptr, nullptr, nullptr, Tq, q_st, q_pos);
 }
 
 extern "C" int kivi_decode_bf16_tail(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,

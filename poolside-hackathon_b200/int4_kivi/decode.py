@@ -12,6 +12,8 @@ Public (unchanged signatures):
   kivi_decode_attention_batched(q [B,Hq,D], stacked, n_qh, sm_scale=None, split=8, block_n=64)
   kivi_decode_attention_gqa(q [B,Hq,D], stacked, n_qh, sm_scale=None, split=16, block_n=64)
   stack_caches([KIVICache, ...]) -> dict
+and, beyond the reference (which decodes one token per call):
+  kivi_decode_attention_multiquery(q [B,Tq,Hq,D], stacked, n_qh, sm_scale=None, q_pos=None)
 """
 from __future__ import annotations
 
@@ -147,6 +149,57 @@ def _decode_packed(q, st, n_qh, sm_scale, fmt, g_k, g_v, out, partial, v_hot, ex
         N.ptr(err), N.stream_of(q))
     N.check(rc, "kivi_decode")
     return out
+
+
+def kivi_decode_attention_multiquery(q: Tensor, stacked: dict, n_qh: int, sm_scale: Optional[float] = None,
+                                     q_pos: Optional[int] = None) -> Tensor:
+    """Decode Tq query tokens per sequence at once (a speculative-decoding
+    verify step, or a small prefill chunk): q [B, Tq, n_qh, D] bf16 over a
+    stacked cache that already holds the queries' own K/V; query j sits at
+    position q_pos + j (default S - Tq, the last Tq tokens) and attends
+    tokens 0 .. q_pos + j.  Returns bf16 [B, Tq, n_qh, D].
+
+    The reference decodes one token per call (decode.py:439-477).  Here the
+    (query, head) pairs of each kv head share one pass over its pages; the
+    queries go in chunks of at most 8 // group per launch so each launch stays
+    on the tensor-core fast path."""
+    B, H, S, D = stacked["B"], stacked["H"], stacked["S"], stacked["D"]
+    fmt = stacked.get("fmt", "int4")
+    assert q.dim() == 4 and q.shape[0] == B and q.shape[2] == n_qh and q.shape[3] == D, \
+        f"q must be [B={B}, Tq, n_qh={n_qh}, D={D}]"
+    assert n_qh % H == 0, "n_q_heads must be a multiple of n_kv_heads"
+    assert stacked.get("seq_lens") is None, "multi-query decode takes equal-length caches"
+    N.require_cuda(q, stacked["v_packed"])
+    Tq = q.shape[1]
+    q_pos = S - Tq if q_pos is None else q_pos
+    if q_pos < 0 or q_pos + Tq > S:
+        raise ValueError(f"queries at {q_pos}..{q_pos + Tq - 1} are outside the {S}-token cache")
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    q = q.to(torch.bfloat16)
+    if q.stride(3) != 1:
+        q = q.contiguous()
+    nps, ss, st = _stacked_geometry(stacked)
+    khot = st["k_hot"]
+    if khot.shape[1] and (khot.stride(2) != 1 or khot.stride(1) != D):
+        khot = khot.contiguous()
+    G = n_qh // H
+    chunk = max(1, 8 // G)
+    L = N.lib()
+    outs = []
+    for j0 in range(0, Tq, chunk):
+        qc = q[:, j0:j0 + chunk]
+        tc = qc.shape[1]
+        work = N.workspace(q.device, L.kivi_decode_workspace_floats(B, tc * n_qh, H, S, D))
+        oc = torch.empty((B, tc, n_qh, D), dtype=torch.bfloat16, device=q.device)
+        N.check(L.kivi_decode_multiquery(
+            N.ptr(qc), qc.stride(0), qc.stride(1), qc.stride(2), N.ptr(st["k_packed"]), N.ptr(st["k_scale"]), nps,
+            N.ptr(khot) if khot.shape[1] else None, khot.shape[1], N.ptr(st["v_packed"]), N.ptr(st["v_scale"]), ss,
+            B, tc, q_pos + j0, n_qh, H, S, D, N.FMT[fmt], sm_scale, stacked.get("g_k", 1.0), stacked.get("g_v", 1.0),
+            N.ptr(oc), N.ptr(work), work.numel(), N.ptr(N.err_flag(q.device)), N.stream_of(q)),
+            "kivi_decode_multiquery")
+        outs.append(oc)
+    return outs[0] if len(outs) == 1 else torch.cat(outs, dim=1)
 
 
 def _single(cache) -> dict:
