@@ -282,6 +282,34 @@ def extra_configs(dev, peak: float, int4_ms: float | None = None) -> dict:
     return res
 
 
+def multiquery_configs(dev, peak: float) -> dict:
+    """Speculative-decoding verify steps at the headline shapes (B=8, Hq=32,
+    Hkv=8, 65536 tokens): Tq = 2 and 4 query tokens per sequence, each at its
+    own causal position, through kivi_decode_attention_multiquery (graph
+    captured).  Bytes = the packed cache once per launch (Tq = 4 takes two
+    launches of two queries each, the fast path's column limit at group 4)."""
+    import torch
+    from int4_kivi.decode import kivi_decode_attention_multiquery
+    S = 65536
+    k, v, _ = make_inputs(S, seed=21, device=dev)
+    st = build_stacked(k, v)
+    del k, v
+    res = {}
+    for Tq in (2, 4):
+        q = torch.randn(B, Tq, HQ, D, device=dev).bfloat16()
+        gr = graph_step(lambda: kivi_decode_attention_multiquery(q, st, HQ))
+        ms = time_graph(gr, seconds=1.0)
+        launches = (Tq + 1) // 2
+        by = B * HKV * S * BYTES_PER_TOKEN_HEAD * launches
+        res[f"multiquery_Tq{Tq}_S65536"] = {"ms_per_step": round(ms, 4), "GB/s": round(by / ms / 1e6, 1),
+                                           "frac": round(by / ms / 1e6 / peak, 4),
+                                           "query_tok_s": round(B * Tq / ms * 1e3, 1), "bytes_per_step": by}
+        del gr
+    del st
+    torch.cuda.empty_cache()
+    return res
+
+
 def store_configs(dev, peak: float) -> dict:
     """The quantise-and-store path: config 0's store ([1, 8, 4096, 128] K and
     V, absmax and MSE), the 64-head x 65536-token store (the headline cache),
@@ -994,6 +1022,7 @@ def main():
         if world == 1:
             extra = extra_configs(dev, peak, ms if S == 65536 else None)
             extra.update(store_configs(dev, peak))
+            extra.update(multiquery_configs(dev, peak))
             extra["reference_triton_gpu"] = reference_gpu_comparator(local)
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,

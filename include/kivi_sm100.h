@@ -231,14 +231,16 @@ int kivi_decode_noalloc(const void *q, int64_t q_sb, int64_t q_sh,
 /* 477 takes q [B, Hq, D]); this extends it the way a verify step of         */
 /* speculative decoding needs.  q bf16 [B, Tq, Hq, D] (strides q_sb, q_st,   */
 /* q_sh; last dim contiguous); out bf16 [B, Tq, Hq, D] contiguous; cache     */
-/* arguments as kivi_decode.  The (query, head) pairs of a kv head form the  */
+/* arguments as kivi_decode; v_hot (nullable) as kivi_decode_bf16_tail: the */
+/* partial page's V in bf16 [BH, hot_stride, D].  The (query, head) pairs of */
+/* a kv head form the                                                        */
 /* kernel's column group (Tq * Hq/Hkv <= 8 on the fast path, <= 16 on the    */
 /* CUDA-core path); work: kivi_decode_workspace_floats(B, Tq * Hq, Hkv, S,   */
 /* D) floats.                                                                */
 /* ------------------------------------------------------------------------ */
 int kivi_decode_multiquery(const void *q, int64_t q_sb, int64_t q_st, int64_t q_sh,
                            const uint8_t *k_packed, const void *k_scale, int k_np_stride,
-                           const void *k_hot, int hot_stride,
+                           const void *k_hot, const void *v_hot, int hot_stride,
                            const uint8_t *v_packed, const void *v_scale, int v_s_stride,
                            int B, int Tq, int q_pos, int Hq, int Hkv, int S, int D, int fmt,
                            float sm_scale, float g_k, float g_v,

@@ -707,8 +707,10 @@ __host__ __device__ inline void head_cta_range(int64_t a0, int64_t a1, int64_t W
 // keeps the partial page unquantised, else dequantised from v_packed.
 template <int FMT>
 __device__ __forceinline__ float tail_v(const DecodeParams& p, int bh, int n_full, int j, int d, int ND) {
-    if (p.v_hot) return __bfloat162float(p.v_hot[((int64_t)bh * p.hot_stride + j) * p.D + d]);
-    const int64_t vr = ((int64_t)bh * p.v_s_stride + n_full + j) * ND + d / BLK;
+    const int t = n_full + j;                           // absolute token
+    if (p.v_hot && t >= p.nf_real)
+        return __bfloat162float(p.v_hot[((int64_t)bh * p.hot_stride + (t - p.nf_real)) * p.D + d]);
+    const int64_t vr = ((int64_t)bh * p.v_s_stride + t) * ND + d / BLK;
     const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
     return gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
 }
@@ -1034,7 +1036,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || S < 0 || D <= 0 || D % BLK) return KIVI_ERR_ARG;
     if (fmt != FMT_INT4 && fmt != FMT_NVFP4) return KIVI_ERR_ARG;
     const bool mq = q_pos >= 0;                       // multi-query decode
-    if (Tq < 1 || (!mq && Tq != 1) || (mq && (mode != 0 || seq_lens || v_hot || sp || q_pos + Tq > S)))
+    if (Tq < 1 || (!mq && Tq != 1) || (mq && (mode != 0 || seq_lens || sp || q_pos + Tq > S)))
         return KIVI_ERR_ARG;
     const int Gq = Hq / Hkv, BH = B * Hkv;
     const int G = Gq * Tq;                            // columns of the group: (query, head) pairs
@@ -1191,15 +1193,15 @@ extern "C" int kivi_decode(const void* q, int64_t q_sb, int64_t q_sh, const uint
 
 extern "C" int kivi_decode_multiquery(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh,
                                       const uint8_t* k_packed, const void* k_scale, int k_np_stride,
-                                      const void* k_hot, int hot_stride, const uint8_t* v_packed,
-                                      const void* v_scale, int v_s_stride, int B, int Tq, int q_pos, int Hq,
-                                      int Hkv, int S, int D, int fmt, float sm_scale, float g_k, float g_v,
-                                      void* out, float* work, int64_t work_floats, int* err,
-                                      kivi_stream_t stream) {
+                                      const void* k_hot, const void* v_hot, int hot_stride,
+                                      const uint8_t* v_packed, const void* v_scale, int v_s_stride, int B,
+                                      int Tq, int q_pos, int Hq, int Hkv, int S, int D, int fmt, float sm_scale,
+                                      float g_k, float g_v, void* out, float* work, int64_t work_floats,
+                                      int* err, kivi_stream_t stream) {
     if (Tq < 1 || q_pos < 0) return KIVI_ERR_ARG;
     return decode_impl(0, q, q_sb, q_sh, k_packed, k_scale, k_np_stride, k_hot, hot_stride, v_packed, v_scale,
                        v_s_stride, B, Hq, Hkv, S, D, fmt, sm_scale, g_k, g_v, out, nullptr, nullptr, nullptr,
-                       work, work_floats, err, stream, nullptr, nullptr, nullptr, Tq, q_st, q_pos);
+                       work, work_floats, err, stream, nullptr, v_hot, nullptr, Tq, q_st, q_pos);
 }
 
 extern "C" int kivi_decode_bf16_tail(const void* q, int64_t q_sb, int64_t q_sh, const uint8_t* k_packed,

@@ -68,8 +68,8 @@ def lib():
             L.kivi_lse_merge.argtypes = [P, P, P, I, I, I, P, P]
             L.kivi_decode_varlen.argtypes = [P, I64, I64, P, P, I, P, I, P, P, I, P, I, I, I, I, I, I, F, F,
                                              F, P, P, I64, P, P]
-            L.kivi_decode_multiquery.argtypes = [P, I64, I64, I64, P, P, I, P, I, P, P, I, I, I, I, I, I, I, I,
-                                                 I, F, F, F, P, P, I64, P, P]
+            L.kivi_decode_multiquery.argtypes = [P, I64, I64, I64, P, P, I, P, P, I, P, P, I, I, I, I, I, I, I,
+                                                 I, I, F, F, F, P, P, I64, P, P]
             L.kivi_decode_bf16_tail.argtypes = [P, I64, I64, P, P, I, P, P, I, P, P, I, I, I, I, I, I, I, F, F, F,
                                                 P, P, I64, P, P]
             L.kivi_seqpar_buffer_bytes.restype = I64

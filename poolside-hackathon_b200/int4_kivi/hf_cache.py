@@ -22,7 +22,9 @@ Fused read path (`Int4KiviCache(config, fused_decode=True)` together with
 not materialise bf16 K/V at all.  `update` stores the token and returns an
 empty placeholder tagged with its layer; the "int4_kivi" attention function
 then runs the fused decode on the packed pages plus the bf16 partial page
-(K and V both unquantised, as `update` would have returned them).  Prefill
+(K and V both unquantised, as `update` would have returned them).  Steps of
+up to FUSED_MAX_Q tokens (a speculative verify step) take the multi-query
+decode, each query at its causal position.  Prefill
 and sliding-window layers keep the dequantise + SDPA path, with the
 dequantised prefix built per call instead of kept, so the cache holds only
 packed pages and at most 15 bf16 tokens per layer.
@@ -37,6 +39,9 @@ from transformers.cache_utils import Cache, CacheLayerMixin
 from .cache import BLOCK, KIVICache, alloc_packed, append_kivi, dequant_kivi, store_kivi
 
 ATTN_IMPL = "int4_kivi"
+# Steps of up to this many new tokens (a decode step, or a speculative verify
+# step) take the fused read path; longer ones (prefill) take SDPA.
+FUSED_MAX_Q = 8
 
 
 class _Int4KiviLayer(CacheLayerMixin):
@@ -165,7 +170,7 @@ class _Int4KiviLayer(CacheLayerMixin):
             self.hot_v = torch.cat([self.hot_v, v_new], dim=1)
         self._freeze_pages()
         self._evict_sliding(n_new)
-        if self.fused and n_new == 1:
+        if self.fused and n_new <= FUSED_MAX_Q:
             # the "int4_kivi" attention function reads the packed pages itself
             stub = torch.empty((B, H, 0, D), dtype=torch.bfloat16, device=k_new.device)
             stub._kivi_layer = self
@@ -191,9 +196,11 @@ class _Int4KiviLayer(CacheLayerMixin):
         return k_full.view(B, H, *k_full.shape[1:]), v_full.view(B, H, *v_full.shape[1:])
 
     def fused_decode(self, query: Tensor, scaling: float | None) -> Tensor:
-        """Attention of one query token per head over everything stored:
-        query [B, Hq, 1, D] -> bf16 [B, Hq, D]."""
-        from .decode import decode_packed
+        """Attention of the step's query tokens over everything stored, each
+        query at its causal position (the last q_len stored tokens are the
+        step's own): query [B, Hq, q_len, D] -> bf16 [B, Hq, D] for q_len 1,
+        else [B, q_len, Hq, D]."""
+        from .decode import decode_packed, kivi_decode_attention_multiquery
         Hq, D = query.shape[1], query.shape[3]
         frozen, t = self._frozen_len(), self._hot_len()
         c = self.store
@@ -202,6 +209,9 @@ class _Int4KiviLayer(CacheLayerMixin):
                   k_hot=self.hot_k if t else torch.empty((self._B * self._H, 0, D), dtype=torch.bfloat16,
                                                          device=query.device),
                   H=self._H, S=frozen + t, D=D, B=self._B)
+        if query.shape[2] > 1:
+            return kivi_decode_attention_multiquery(query.transpose(1, 2).to(torch.bfloat16), st, Hq,
+                                                    sm_scale=scaling, v_hot=self.hot_v if t else None)
         q = query[:, :, 0].to(torch.bfloat16)
         return decode_packed(q, st, Hq, sm_scale=scaling, v_hot=self.hot_v if t else None)
 
@@ -283,31 +293,38 @@ def kivi_attention_forward(module, query: Tensor, key: Tensor, value: Tensor, at
     layer's dequantised K/V, since the fused decode attends to every token."""
     from transformers.integrations.sdpa_attention import sdpa_attention_forward
     layer = getattr(key, "_kivi_layer", None)
-    if layer is not None and not _attends_all(attention_mask):
-        key, value = layer._dense_kv(1)
+    q_len = query.shape[2]
+    if layer is not None and not _causal_over_all(attention_mask, q_len):
+        key, value = layer._dense_kv(q_len)
         layer = None
     if layer is None:
         return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout,
                                       scaling=scaling, **kwargs)
-    if query.shape[2] != 1:
-        raise ValueError("fused decode takes one query token per sequence")
-    out = layer.fused_decode(query, scaling)              # [B, Hq, D]
-    return out[:, None].to(query.dtype), None             # [B, q_len, Hq, D]
+    out = layer.fused_decode(query, scaling)              # [B, Hq, D] or [B, q_len, Hq, D]
+    if q_len == 1:
+        out = out[:, None]
+    return out.to(query.dtype), None                      # [B, q_len, Hq, D]
 
 
 _mask_memo: list = [None, -1, True]   # [mask tensor of the last check, its version, its result]
 
 
-def _attends_all(mask) -> bool:
-    """True when `mask` (None, bool where True attends, or additive float)
-    hides no key position.  Every layer of one forward step gets the same
-    mask tensor, so the answer (which needs a device-to-host read) is
+def _causal_over_all(mask, q_len: int) -> bool:
+    """True when `mask` (None, bool where True attends, or additive float,
+    [B, 1, q_len, kv_len]) is the plain causal mask over every stored key:
+    query j sees keys 0 .. kv_len - q_len + j and nothing is padded.  That is
+    what the fused path computes.  Every layer of one forward step gets the
+    same mask tensor, so the answer (which needs a device-to-host read) is
     computed once per step and reused for the other layers."""
     if mask is None:
         return True
     if _mask_memo[0] is mask and _mask_memo[1] == mask._version:
         return _mask_memo[2]
-    ok = bool(mask.all()) if mask.dtype == torch.bool else bool((mask == 0).all())
+    allowed = mask if mask.dtype == torch.bool else (mask == 0)
+    kv, nq = allowed.shape[-1], allowed.shape[-2]
+    j = torch.arange(nq, device=allowed.device)[:, None]
+    t = torch.arange(kv, device=allowed.device)[None, :]
+    ok = nq == q_len and bool((allowed == (t <= kv - nq + j)).all())
     _mask_memo[:] = [mask, mask._version, ok]
     return ok
 

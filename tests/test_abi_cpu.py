@@ -129,16 +129,26 @@ def test_device_index_spellings():
 
 
 def test_fused_attention_mask_check():
-    """The fused hf decode runs only when the mask hides no key position
-    (a left-padded batch goes to SDPA over the dequantised K/V)."""
+    """The fused hf read path runs only when the mask is the plain causal mask
+    over every stored key (a left-padded batch goes to SDPA over the
+    dequantised K/V); single-token and multi-token steps."""
     import torch
-    from int4_kivi.hf_cache import _attends_all
-    assert _attends_all(None)
+    from int4_kivi.hf_cache import _causal_over_all
+    assert _causal_over_all(None, 1) and _causal_over_all(None, 3)
     m = torch.ones(2, 1, 1, 9, dtype=torch.bool)
-    assert _attends_all(m)
-    m[1, 0, 0, 0] = False
-    assert not _attends_all(m)
+    assert _causal_over_all(m, 1)
+    m[1, 0, 0, 0] = False                               # in place: the memo sees the new version
+    assert not _causal_over_all(m, 1)
     f = torch.zeros(2, 1, 1, 9)
-    assert _attends_all(f)
+    assert _causal_over_all(f, 1)
     f[0, 0, 0, 3] = torch.finfo(torch.float32).min
-    assert not _attends_all(f)
+    assert not _causal_over_all(f, 1)
+    c = torch.tril(torch.ones(3, 9, dtype=torch.bool), diagonal=6)[None, None].repeat(2, 1, 1, 1)
+    assert _causal_over_all(c, 3)
+    assert not _causal_over_all(c[:, :, 1:].contiguous(), 3)    # wrong query count
+    c2 = c.clone()
+    c2[0, 0, 0, 0] = False                              # left padding
+    assert not _causal_over_all(c2, 3)
+    c3 = c.clone()
+    c3[1, 0, 0, 7] = True                               # a future key visible
+    assert not _causal_over_all(c3, 3)

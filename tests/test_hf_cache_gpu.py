@@ -134,6 +134,34 @@ def test_fused_decode_matches_dequant_path(cuda_dev):
         assert fused._deq_k is None                          # no bf16 copy kept in fused mode
 
 
+def test_fused_multi_token_steps(cuda_dev):
+    """Steps of 2..8 new tokens (speculative verify) on the fused read path:
+    each query attends the stored tokens up to its own position, compared
+    with fp32 attention over exactly those tokens, across page boundaries and
+    from an empty cache."""
+    from conftest import check_decode_bf16
+    from int4_kivi.hf_cache import _Int4KiviLayer
+    H, Hq, D = 2, 8, 128
+    k, v, _ = gen_kv(H, 160, D, seed=31)
+    kd, vd = k.to(cuda_dev), v.to(cuda_dev)
+    g = torch.Generator().manual_seed(32)
+    fused = _Int4KiviLayer(fused_decode=True)
+    pos = 0
+    for n in (3, 8, 5, 2, 7, 16, 4, 6):
+        stub, _ = fused.update(kd[None, :, pos:pos + n], vd[None, :, pos:pos + n])
+        pos += n
+        if n > 8:                                      # prefill-sized step: the dense path
+            assert stub.shape[2] == pos
+            continue
+        assert stub.shape[2] == 0 and stub._kivi_layer is fused
+        q = torch.randn(1, Hq, n, D, generator=g).bfloat16().to(cuda_dev)
+        out = fused.fused_decode(q, D ** -0.5)[0].float().cpu()        # [n, Hq, D]
+        ek, ev = _exact_kv(fused)
+        ref = torch.stack([_ref_attention(q[0, :, j].cpu(), ek[:, :pos - n + j + 1], ev[:, :pos - n + j + 1],
+                                          D ** -0.5) for j in range(n)])
+        check_decode_bf16(out, ref, f"pos={pos} n={n}")
+
+
 def test_fused_generate_tiny_random_model(cuda_dev):
     """Teacher-forced decode of a random tiny Llama: the fused path's logits
     track the dequantise + SDPA path's; greedy generate runs end to end."""
@@ -155,6 +183,18 @@ def test_fused_generate_tiny_random_model(cuda_dev):
         got = [model(ids[:, :40], past_key_values=c_f).logits[:, -1]]
         for t in range(40, 80):
             got.append(model(ids[:, t:t + 1], past_key_values=c_f).logits[:, -1])
+        # the same tokens fed 4 at a time (a speculative verify step): every
+        # position's logits, through the multi-query fused path vs SDPA
+        c_m = Int4KiviCache(config=cfg, fused_decode=True)
+        model(ids[:, :40], past_key_values=c_m)
+        multi = [model(ids[:, t:t + 4], past_key_values=c_m).logits[0] for t in range(40, 80, 4)]
+        model.set_attn_implementation("sdpa")
+        c_r = Int4KiviCache(config=cfg)
+        model(ids[:, :40], past_key_values=c_r)
+        multi_ref = [model(ids[:, t:t + 4], past_key_values=c_r).logits[0] for t in range(40, 80, 4)]
+        enable_fused_decode(model)
+    mr, mg = torch.cat(multi_ref).float(), torch.cat(multi).float()
+    assert (mr - mg).abs().max().item() <= 0.02 * mr.abs().max().item()
     r, g_ = torch.stack(ref).float(), torch.stack(got).float()
     assert torch.equal(r[0], g_[0])                           # prefill takes the same path
     assert (r - g_).abs().max().item() <= 0.02 * r.abs().max().item()
