@@ -708,8 +708,10 @@ __host__ __device__ inline void head_cta_range(int64_t a0, int64_t a1, int64_t W
 template <int FMT>
 __device__ __forceinline__ float tail_v(const DecodeParams& p, int bh, int n_full, int j, int d, int ND) {
     const int t = n_full + j;                           // absolute token
-    if (p.v_hot && t >= p.nf_real)
-        return __bfloat162float(p.v_hot[((int64_t)bh * p.hot_stride + (t - p.nf_real)) * p.D + d]);
+    // the bf16 partial page starts at the cache's last full page (plain
+    // decodes: n_full itself; varlen heads each have their own n_full)
+    if (p.v_hot && (!p.mq || t >= p.nf_real))
+        return __bfloat162float(p.v_hot[((int64_t)bh * p.hot_stride + (p.mq ? t - p.nf_real : j)) * p.D + d]);
     const int64_t vr = ((int64_t)bh * p.v_s_stride + t) * ND + d / BLK;
     const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
     return gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
@@ -742,12 +744,12 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     // in one (multi-query tails), else from the bf16 hot page
     auto k_tail = [&](int j, int d) -> float {
         const int t = n_full + j;
-        if (t < p.nf_real) {
+        if (p.mq && t < p.nf_real) {
             const int64_t kr = ((int64_t)bh * D + d) * p.k_np_stride + t / BLK;
             const uint32_t kb = p.k_packed[kr * PACKB + (t % BLK) / 2];
             return gen_code<FMT>((kb >> (4 * (t & 1))) & 0xF) * gen_scale<FMT>(p.k_scale, kr, p.g_k);
         }
-        return __bfloat162float(p.k_hot[((int64_t)bh * p.hot_stride + (t - p.nf_real)) * D + d]);
+        return __bfloat162float(p.k_hot[((int64_t)bh * p.hot_stride + (p.mq ? t - p.nf_real : j)) * D + d]);
     };
     // tail scores (log2 units), one warp per token
     for (int j = warp; j < hot; j += 4) {

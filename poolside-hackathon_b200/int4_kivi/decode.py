@@ -84,7 +84,7 @@ def _decode_packed(q, st, n_qh, sm_scale, fmt, g_k, g_v, out, partial, v_hot, ex
     else:
         nps, ss, st = _stacked_geometry(st)
     khot = st["k_hot"]
-    if khot.shape[1] and khot.stride(2) != 1 or khot.shape[1] and khot.stride(1) != D:
+    if khot.shape[1] and not khot.is_contiguous():      # rows are addressed as (bh * hot_stride + j) * D
         khot = khot.contiguous()
     hot_stride = khot.shape[1]
     dev = q.device
@@ -187,7 +187,7 @@ def kivi_decode_attention_multiquery(q: Tensor, stacked: dict, n_qh: int, sm_sca
     else:
         nps, ss, st = _stacked_geometry(stacked)
     khot = st["k_hot"]
-    if khot.shape[1] and (khot.stride(2) != 1 or khot.stride(1) != D):
+    if khot.shape[1] and not khot.is_contiguous():      # rows are addressed as (bh * hot_stride + j) * D
         khot = khot.contiguous()
     vh = None
     if v_hot is not None and khot.shape[1]:

@@ -74,3 +74,24 @@ def test_single_query_at_the_end_equals_decode(cuda_dev, S):
     want = decode_packed(q3, st, 32)
     got = kivi_decode_attention_multiquery(q3[:, None], st, 32)[:, 0]
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 7])
+def test_hf_layer_tail_only_noncontiguous_inputs(cuda_dev, n):
+    """The HF cache layer with fewer than 16 tokens (no packed page yet), fed
+    K/V as strided views: the bf16 tail rows must be read at their own row
+    stride.  Query j attends tokens 0 .. j in exact bf16 (fp32 reference)."""
+    from int4_kivi.hf_cache import _Int4KiviLayer
+    H, Hq = 2, 8
+    k, v, _ = gen_kv(H, 40, D, seed=31)
+    layer = _Int4KiviLayer(fused_decode=True)
+    layer.update(k[None, :, :n].to(cuda_dev), v[None, :, :n].to(cuda_dev))   # views with row stride 40 * D
+    q = torch.randn(1, Hq, n, D, generator=torch.Generator().manual_seed(1)).bfloat16()
+    out = layer.fused_decode(q.to(cuda_dev), D ** -0.5)
+    out = (out[0] if n > 1 else out).float().cpu().reshape(n, Hq, D)
+    for j in range(n):
+        kk = k[:, :j + 1].float().repeat_interleave(Hq // H, 0)
+        vv = v[:, :j + 1].float().repeat_interleave(Hq // H, 0)
+        p = torch.softmax((q[0, :, j].float()[:, None] @ kk.transpose(1, 2))[:, 0] * D ** -0.5, -1)
+        want = (p[:, None] @ vv)[:, 0]
+        torch.testing.assert_close(out[j], want, atol=2e-2, rtol=2e-2, msg=f"query {j}")
