@@ -874,8 +874,8 @@ def paged_main(args, rank: int, world: int, local: int) -> None:
                              "frac": round(by / ms / 1e6 / peak, 4), "peak_kind": kind,
                              "timed": "whole step (tile table + decode + merge), CUDA events",
                              "traffic": round(PAGED_TRAFFIC_16K * S / 16384) if args.fmt == "int4" else None,
-                             "traffic_note": "ncu dram read+write of one 16384-token launch scaled by tokens "
-                                             "(profiles/paged_decode_int4_64k.md)"},
+                             "traffic_note": "ncu dram read+write of one 16384-token paged launch, "
+                                             "scaled by tokens"},
                 "gpu_launches": 3 * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
