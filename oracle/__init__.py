@@ -11,6 +11,9 @@ Reference behaviour restated (paths inside a1exxd0/poolside-hackathon):
   * int4_kivi/triton_kernels.py:21-24, 109-131, 137-286 -- packing, store,
     dequant geometry; int4_kivi/cache.py:48-201 -- KIVICache layout
   * scripts/validate_int4_kivi_decode.py:37-84 -- fp32-exact decode reference
+  * kv_quant.py:215-217 `int3` grid with the KIVI V geometry -- the V half
+    of the mixed INT4-K / INT3-V cache (WRITEUP.md:336-339 names it; the
+    reference has no packed INT3 layout, the 3-bit packing is this library's)
   * scripts/diag_kernel_perchannel.py:30-48, WRITEUP.md:97-107 -- e4m3 block
     scales rounded inside the MSE search (NVFP4 variant)
   * WRITEUP.md:82-95,117-124, scripts/validate_paged_decode.py:32-64,
@@ -61,6 +64,8 @@ def lib():
         L.orc_store_int4.argtypes = [P, P, I, I, I, I, I, P, I, P, P, P, P]
         L.orc_dequant_int4.argtypes = [P, P, P, P, I, I, I, P, P]
         L.orc_store_nvfp4.argtypes = [P, P, I, I, I, I, I, P, I, F, F, P, P, P, P]
+        L.orc_store_v3.argtypes = [P, I, I, I, I, P, I, P, P]
+        L.orc_dequant_v3.argtypes = [P, P, I, I, I, P]
         L.orc_dequant_nvfp4.argtypes = [P, P, P, P, I, I, I, F, F, P, P]
         L.orc_decode_attention.argtypes = [P, P, P, P, I, I, I, I, I, F, P]
         L.orc_f32_to_f16.argtypes = [F]
@@ -166,6 +171,47 @@ def dequant_int4(c: dict) -> tuple[np.ndarray, np.ndarray]:
     kp = np.ascontiguousarray(c["k_packed"]); ks = np.ascontiguousarray(c["k_scale"]).view(np.uint16)
     vp = np.ascontiguousarray(c["v_packed"]); vs = np.ascontiguousarray(c["v_scale"]).view(np.uint16)
     lib().orc_dequant_int4(_p(kp), _p(ks), _p(vp), _p(vs), H, S, D, _p(k), _p(v))
+    n_full = (S // BLOCK) * BLOCK
+    if n_full < S:
+        k[:, n_full:] = _f32(c["k_hot"])
+    return k, v
+
+
+def store_int3v(k, v, k_calib: str = "mse", v_calib: str = "mse", n_alphas: int = 32) -> dict:
+    """The mixed-precision cache (K INT4 as store_int4, V INT3 per token on the
+    kv_quant `int3` grid): v_packed u8 [H,S,ND,6] (3-bit two's-complement codes,
+    element i at bits 3i..3i+2 of a little-endian 48-bit word), v_scale f16."""
+    c = store_int4(k, v, k_calib, "absmax", n_alphas)
+    vf = _f32(v)
+    H, S, D = vf.shape
+    vp = np.zeros((H, S, D // BLOCK, 6), np.uint8)
+    vs = np.zeros((H, S, D // BLOCK), np.uint16)
+    lib().orc_store_v3(_p(vf), H, S, D, CALIB[v_calib], _p(alphas(n_alphas)), n_alphas, _p(vp), _p(vs))
+    c.update(v_packed=vp, v_scale=vs.view(np.float16))
+    return c
+
+
+def unpack_int3(packed: np.ndarray) -> np.ndarray:
+    """[..., 6] INT3 blocks -> int8 codes [..., 16]."""
+    b = packed.astype(np.uint64)
+    w = np.zeros(packed.shape[:-1], np.uint64)
+    for j in range(6):
+        w |= b[..., j] << np.uint64(8 * j)
+    f = np.stack([(w >> np.uint64(3 * i)) & np.uint64(7) for i in range(BLOCK)], axis=-1).astype(np.int8)
+    return np.where(f >= 4, f - 8, f).astype(np.int8)
+
+
+def dequant_int3v(c: dict) -> tuple[np.ndarray, np.ndarray]:
+    """fp32 K (as dequant_int4) and V (code * fp32(fp16 scale)) [H, S, D]."""
+    H, S, D = c["H"], c["S"], c["D"]
+    k = np.zeros((H, S, D), np.float32)
+    v = np.zeros((H, S, D), np.float32)
+    kp = np.ascontiguousarray(c["k_packed"]); ks = np.ascontiguousarray(c["k_scale"]).view(np.uint16)
+    dummy_p = np.zeros((H, S, D // BLOCK, PACK), np.uint8)
+    dummy_s = np.zeros((H, S, D // BLOCK), np.uint16)
+    lib().orc_dequant_int4(_p(kp), _p(ks), _p(dummy_p), _p(dummy_s), H, S, D, _p(k), _p(v))
+    vp = np.ascontiguousarray(c["v_packed"]); vs = np.ascontiguousarray(c["v_scale"]).view(np.uint16)
+    lib().orc_dequant_v3(_p(vp), _p(vs), H, S, D, _p(v))
     n_full = (S // BLOCK) * BLOCK
     if n_full < S:
         k[:, n_full:] = _f32(c["k_hot"])

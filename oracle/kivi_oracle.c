@@ -310,6 +310,56 @@ void orc_dequant_int4(const uint8_t *k_packed, const uint16_t *k_scale,
 }
 
 /* ------------------------------------------------------------------------- */
+/* Mixed-precision cache, V half (K is orc_store_int4's K): INT3 per token    */
+/* over 16-channel blocks on the kv_quant.py:215-217 `int3` grid (qmax 3,     */
+/* kv_quant.py:247-266 calibration), codes against the fp32 scale, scale      */
+/* stored as fp16.  The reference has no packed INT3 layout; this library's:  */
+/* 16 three-bit two's-complement codes, element i in bits [3i, 3i + 3) of a   */
+/* little-endian 48-bit word, 6 bytes per block.                              */
+/* ------------------------------------------------------------------------- */
+static void pack16_3(const int c[BLK], uint8_t out[6]) {
+    uint64_t w = 0;
+    for (int i = 0; i < BLK; ++i) w |= (uint64_t)(c[i] & 7) << (3 * i);
+    for (int j = 0; j < 6; ++j) out[j] = (uint8_t)(w >> (8 * j));
+}
+
+/* v: fp32 [H, S, D] -> v_packed [H, S, ND, 6], v_scale f16 [H, S, ND]. */
+void orc_store_v3(const float *v, int H, int S, int D, int calib_v, const float *alphas,
+                  int n_alphas, uint8_t *v_packed, uint16_t *v_scale) {
+    int ND = D / BLK;
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int h = 0; h < H; ++h)
+        for (int t = 0; t < S; ++t)
+            for (int db = 0; db < ND; ++db) {
+                float x[BLK]; int c[BLK];
+                gather_block(v, S, D, LAYOUT_HEADDIM, h, t, db, x);
+                float s = orc_calibrate_block(x, FMT_INT3, calib_v, alphas, n_alphas);
+                for (int j = 0; j < BLK; ++j) c[j] = (int)q_grid(x[j] / s, FMT_INT3);
+                size_t r = ((size_t)h * S + t) * ND + db;
+                pack16_3(c, v_packed + r * 6);
+                v_scale[r] = orc_f32_to_f16(s);
+            }
+}
+
+/* value = code * fp32(f16 scale), fp32; vout [H, S, D]. */
+void orc_dequant_v3(const uint8_t *v_packed, const uint16_t *v_scale, int H, int S, int D, float *vout) {
+    int ND = D / BLK;
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int h = 0; h < H; ++h)
+        for (int t = 0; t < S; ++t)
+            for (int db = 0; db < ND; ++db) {
+                size_t r = ((size_t)h * S + t) * ND + db;
+                uint64_t w = 0;
+                for (int j = 0; j < 6; ++j) w |= (uint64_t)v_packed[r * 6 + j] << (8 * j);
+                float s = orc_f16_to_f32(v_scale[r]);
+                for (int c = 0; c < BLK; ++c) {
+                    int f = (int)((w >> (3 * c)) & 7);
+                    vout[((size_t)h * S + t) * D + db * BLK + c] = (float)(f >= 4 ? f - 8 : f) * s;
+                }
+            }
+}
+
+/* ------------------------------------------------------------------------- */
 /* NVFP4-KIVI store.  Reference semantics: kv_quant.py:220-229 (`nvfp4`:     */
 /* e2m1 grid, qmax 6, bucketize ties toward the smaller magnitude) with the   */
 /* fp8-e4m3 block scale of the paged fork (scripts/diag_kernel_perchannel.py: */

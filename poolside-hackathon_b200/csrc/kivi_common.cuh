@@ -17,7 +17,12 @@ namespace kivi {
 constexpr int BLK = 16;   // elements per quant block; tokens per K page
 constexpr int PACKB = 8;  // bytes per packed block
 
-enum Fmt { FMT_INT4 = 0, FMT_INT3 = 1, FMT_NVFP4 = 2 };
+// FMT_MIX43: the mixed-precision cache, K INT4 (the KIVI K layout) and V INT3
+// per token over 16-channel blocks (the kv_quant.py:215-217 `int3` grid,
+// qmax 3); a V block is 16 three-bit two's-complement codes, element i in
+// bits [3i, 3i + 3) of a little-endian 48-bit word (6 bytes).
+enum Fmt { FMT_INT4 = 0, FMT_INT3 = 1, FMT_NVFP4 = 2, FMT_MIX43 = 3 };
+constexpr int PACKB3 = 6;  // bytes per packed INT3 block
 enum Calib { CAL_ABSMAX = 0, CAL_MSE = 1 };
 
 __device__ __forceinline__ float qmax_of(int fmt) {
@@ -156,6 +161,15 @@ template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return
 template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
 
 __device__ __forceinline__ int sx4(int n) { return n >= 8 ? n - 16 : n; }
+
+// Code i (0..15) of a 6-byte INT3 block (FMT_MIX43 V).
+__device__ __forceinline__ int int3_code(const uint8_t* blk, int i) {
+    const int b = 3 * i, byte = b >> 3, sh = b & 7;
+    uint32_t w = blk[byte];
+    if (sh > 5) w |= (uint32_t)blk[byte + 1] << 8;   // the field crosses into the next byte
+    const int f = (int)((w >> sh) & 7u);
+    return f >= 4 ? f - 8 : f;
+}
 
 // ---------------------------------------------------------------------------
 // PTX wrappers: mbarrier, TMA, ldmatrix, mma.sync

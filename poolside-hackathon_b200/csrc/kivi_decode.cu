@@ -612,6 +612,14 @@ __device__ __forceinline__ float gen_code(uint32_t nib) {
     if (FMT == FMT_NVFP4) { float l = e2m1_level(nib & 7); return (nib & 8) ? -l : l; }
     return (float)sx4((int)nib);
 }
+// Dequantised V at packed row vr (one token's 16-channel block), channel d.
+template <int FMT>
+__device__ __forceinline__ float gen_v(const DecodeParams& p, int64_t vr, int d) {
+    if (FMT == FMT_MIX43)
+        return (float)int3_code(p.v_packed + vr * PACKB3, d % BLK) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
+    const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
+    return gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
+}
 
 template <int FMT>
 __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeParams p) {
@@ -663,9 +671,7 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeParams 
                     const int64_t kr = ((int64_t)bh * D + d) * p.k_np_stride + pg;
                     const uint32_t kb = p.k_packed[kr * PACKB + j / 2];
                     kv[e] = gen_code<FMT>((kb >> (4 * (j & 1))) & 0xF) * gen_scale<FMT>(p.k_scale, kr, p.g_k);
-                    const int64_t vr = ((int64_t)bh * p.v_s_stride + t) * ND + d / BLK;
-                    const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
-                    vv[e] = gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
+                    vv[e] = gen_v<FMT>(p, ((int64_t)bh * p.v_s_stride + t) * ND + d / BLK, d);
                 }
             }
             for (int h = 0; h < G; ++h) {
@@ -712,9 +718,7 @@ __device__ __forceinline__ float tail_v(const DecodeParams& p, int bh, int n_ful
     // decodes: n_full itself; varlen heads each have their own n_full)
     if (p.v_hot && (!p.mq || t >= p.nf_real))
         return __bfloat162float(p.v_hot[((int64_t)bh * p.hot_stride + (p.mq ? t - p.nf_real : j)) * p.D + d]);
-    const int64_t vr = ((int64_t)bh * p.v_s_stride + t) * ND + d / BLK;
-    const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
-    return gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
+    return gen_v<FMT>(p, ((int64_t)bh * p.v_s_stride + t) * ND + d / BLK, d);
 }
 
 template <int FMT>
@@ -1036,7 +1040,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
                 kivi_stream_t stream, const int* seq_lens = nullptr, const void* v_hot = nullptr,
                 const SeqPar* sp = nullptr, int Tq = 1, int64_t q_st = 0, int q_pos = -1) {
     if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || S < 0 || D <= 0 || D % BLK) return KIVI_ERR_ARG;
-    if (fmt != FMT_INT4 && fmt != FMT_NVFP4) return KIVI_ERR_ARG;
+    if (fmt != FMT_INT4 && fmt != FMT_NVFP4 && fmt != FMT_MIX43) return KIVI_ERR_ARG;
     const bool mq = q_pos >= 0;                       // multi-query decode
     if (Tq < 1 || (!mq && Tq != 1) || (mq && (mode != 0 || seq_lens || sp || q_pos + Tq > S)))
         return KIVI_ERR_ARG;
@@ -1062,7 +1066,8 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     const int sms = num_sms(&dev);
     if (!sms) return record_cuda_error(cudaGetLastError());
 
-    const bool fast = D == DH && G <= 8 && sm_scale > 0.0f && k_np_stride % 16 == 0 && v_s_stride % 16 == 0 &&
+    // the mixed INT4-K / INT3-V cache runs on the CUDA-core path only
+    const bool fast = fmt != FMT_MIX43 && D == DH && G <= 8 && sm_scale > 0.0f && k_np_stride % 16 == 0 && v_s_stride % 16 == 0 &&
                       (uintptr_t)k_packed % 16 == 0 && (uintptr_t)k_scale % 16 == 0 &&
                       (uintptr_t)v_packed % 16 == 0 && (uintptr_t)v_scale % 16 == 0 &&
                       q_sh % 2 == 0 && q_st % 2 == 0 && (uintptr_t)q % 4 == 0 && n_full > 0 &&
@@ -1130,6 +1135,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
                 decode_fast_kernel<FMT_INT4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_INT4>(), st>>>(tkc, tks, tvc, tvs, p);
         } else {
             if (fmt == FMT_NVFP4) decode_generic_kernel<FMT_NVFP4><<<pl.N, 128, 0, st>>>(p);
+            else if (fmt == FMT_MIX43) decode_generic_kernel<FMT_MIX43><<<pl.N, 128, 0, st>>>(p);
             else decode_generic_kernel<FMT_INT4><<<pl.N, 128, 0, st>>>(p);
         }
         int e = check_launch();
@@ -1156,6 +1162,8 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     cfg.numAttrs = 1;
     cudaError_t le = (fmt == FMT_NVFP4)
         ? cudaLaunchKernelEx(&cfg, combine_kernel<FMT_NVFP4>, p, mode, o, m_out, l_out, acc_out)
+        : (fmt == FMT_MIX43)
+        ? cudaLaunchKernelEx(&cfg, combine_kernel<FMT_MIX43>, p, mode, o, m_out, l_out, acc_out)
         : cudaLaunchKernelEx(&cfg, combine_kernel<FMT_INT4>, p, mode, o, m_out, l_out, acc_out);
     if (le != cudaSuccess) return record_cuda_error(le);
     return check_launch();

@@ -98,6 +98,22 @@ __device__ __forceinline__ void quant_pack(const float x[BLK], int calib, const 
     packed = make_uint2(lo, hi);
 }
 
+// One V block of the mixed cache: INT3 codes against the fp32 scale (scale
+// stored as fp16, like every KIVI scale), packed 3 bits per element; writes
+// the 6 bytes at v_packed + row * 6 as three 16-bit words.
+__device__ __forceinline__ void store_v3(const float x[BLK], int calib, const float* alphas, int n_alphas,
+                                         uint8_t* v_packed, void* v_scale, int64_t row) {
+    const float s = calibrate16(x, FMT_INT3, calib, alphas, n_alphas);
+    const float r = __frcp_rn(s);
+    uint64_t w = 0;
+#pragma unroll
+    for (int i = 0; i < BLK; ++i)
+        w |= (uint64_t)((uint32_t)(int)q_grid_div(x[i], s, r, FMT_INT3) & 7u) << (3 * i);
+    uint16_t* o = reinterpret_cast<uint16_t*>(v_packed + row * PACKB3);
+    o[0] = (uint16_t)w; o[1] = (uint16_t)(w >> 16); o[2] = (uint16_t)(w >> 32);
+    reinterpret_cast<uint16_t*>(v_scale)[row] = __half_as_ushort(__float2half_rn(s));
+}
+
 // K blocks (per channel, 16-token pages): a CTA owns PPC pages x D channels
 // of one head.  Threads take consecutive channels, so each of a block's 16
 // token loads is a contiguous row segment across the warp; the packed
@@ -110,6 +126,7 @@ __device__ __forceinline__ void quant_pack(const float x[BLK], int calib, const 
 template <typename T, int FMT, bool ANY_MSE>
 __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_chunks, int nk_ctas) {
     extern __shared__ __align__(16) uint8_t st_smem[];
+    constexpr int KF = FMT == FMT_MIX43 ? FMT_INT4 : FMT;    // K format
     const T* k = reinterpret_cast<const T*>(a.k);
     const T* v = reinterpret_cast<const T*>(a.v);
     const int D = a.D, ND = D / BLK, tid = threadIdx.x;
@@ -138,12 +155,12 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
                 uint16_t sb;
 #pragma unroll
                 for (int j = 0; j < BLK; ++j) x[j] = lo16_f32<T>(raw[j]);
-                quant_pack<FMT>(x, calib, a.alphas, a.n_alphas, a.g_k, pk, sb);
+                quant_pack<KF>(x, calib, a.alphas, a.n_alphas, a.g_k, pk, sb);
                 sc[p * (D + 1) + c] = pk;
                 ss[p * (D + 2) + c] = sb;
 #pragma unroll
                 for (int j = 0; j < BLK; ++j) x[j] = hi16_f32<T>(raw[j]);
-                quant_pack<FMT>(x, calib, a.alphas, a.n_alphas, a.g_k, pk, sb);
+                quant_pack<KF>(x, calib, a.alphas, a.n_alphas, a.g_k, pk, sb);
                 sc[p * (D + 1) + c + 1] = pk;
                 ss[p * (D + 2) + c + 1] = sb;
             }
@@ -154,7 +171,7 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
                 load_strided16<T>(src + (int64_t)p * BLK * a.sk_s + c * a.sk_d, a.sk_s, x);
                 uint2 pk;
                 uint16_t sb;
-                quant_pack<FMT>(x, calib, a.alphas, a.n_alphas, a.g_k, pk, sb);
+                quant_pack<KF>(x, calib, a.alphas, a.n_alphas, a.g_k, pk, sb);
                 sc[p * (D + 1) + c] = pk;
                 ss[p * (D + 2) + c] = sb;
             }
@@ -172,7 +189,7 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
     const int64_t nv = (int64_t)a.H * a.S_v * ND;
     const int nv_ctas = gridDim.x - nk_ctas;
     const int calib_v = ANY_MSE ? a.calib_v : (int)CAL_ABSMAX;
-    if (!ANY_MSE && sizeof(T) == 2 && a.sv_d == 1 && ND % 2 == 0 && (a.sv_s * 2) % 16 == 0 &&
+    if (FMT != FMT_MIX43 && !ANY_MSE && sizeof(T) == 2 && a.sv_d == 1 && ND % 2 == 0 && (a.sv_s * 2) % 16 == 0 &&
         (a.sv_h * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0) {
         // absmax: a thread takes two neighbouring blocks of one token, 64
         // contiguous bytes in four 16-byte loads all in flight before either
@@ -210,8 +227,12 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
         uint2 pk;
         uint16_t sb;
         load_contig16<T>(v + h * a.sv_h + t * a.sv_s + (int64_t)db * BLK * a.sv_d, a.sv_d, x);
-        quant_pack<FMT>(x, calib_v, a.alphas, a.n_alphas, a.g_v, pk, sb);
         const int64_t row = ((int64_t)h * a.v_s_stride + a.vtok0 + t) * ND + db;
+        if constexpr (FMT == FMT_MIX43) {
+            store_v3(x, calib_v, a.alphas, a.n_alphas, a.v_packed, a.v_scale, row);
+            continue;
+        }
+        quant_pack<FMT>(x, calib_v, a.alphas, a.n_alphas, a.g_v, pk, sb);
         reinterpret_cast<uint2*>(a.v_packed)[row] = pk;
         if (FMT == FMT_NVFP4) reinterpret_cast<uint8_t*>(a.v_scale)[row] = (uint8_t)sb;
         else reinterpret_cast<uint16_t*>(a.v_scale)[row] = sb;
@@ -366,9 +387,15 @@ __global__ void __launch_bounds__(256) dequant_kernel(DequantArgs a) {
             const int64_t r = jj / ND;
             const int t = (int)(r % a.S), h = (int)(r / a.S);
             const int64_t row = ((int64_t)h * a.v_s_stride + t) * ND + db;
-            const uint2 pk = reinterpret_cast<const uint2*>(a.v_packed)[row];
             const float s = load_scale<FMT>(a.v_scale, row, a.g_v);
             __nv_bfloat16* o = vo + h * a.so_h + t * a.so_s + (int64_t)db * BLK * a.so_d;
+            if constexpr (FMT == FMT_MIX43) {
+                const uint8_t* blk = a.v_packed + row * PACKB3;
+#pragma unroll
+                for (int c = 0; c < BLK; ++c) o[c * a.so_d] = __float2bfloat16_rn(__fmul_rn((float)int3_code(blk, c), s));
+                continue;
+            }
+            const uint2 pk = reinterpret_cast<const uint2*>(a.v_packed)[row];
 #pragma unroll
             for (int c = 0; c < BLK; ++c) {
                 uint32_t nib = ((c < 8 ? pk.x : pk.y) >> (4 * (c & 7))) & 0xF;
@@ -500,10 +527,12 @@ int launch_store(const StoreArgs& a, cudaStream_t st) {
     if (nv_ctas > 148LL * 16) nv_ctas = 148LL * 16;
     if (nk_ctas64 + nv_ctas > 0x7fffffffLL) return KIVI_ERR_UNSUPPORTED;
     const int64_t nblocks = (int64_t)a.H * NP * a.D + nv;
-    if ((a.calib_k == CAL_MSE || a.calib_v == CAL_MSE) && nblocks <= SMALL_MSE_BLOCKS) {
-        const int64_t ctas = (nblocks + 7) / 8;              // 8 warps, one block each
-        store_warp_kernel<T, FMT><<<(int)ctas, 256, 0, st>>>(a);
-        return check_launch();
+    if constexpr (FMT != FMT_MIX43) {        // (the mixed cache's INT3 V blocks use the thread-per-block kernel)
+        if ((a.calib_k == CAL_MSE || a.calib_v == CAL_MSE) && nblocks <= SMALL_MSE_BLOCKS) {
+            const int64_t ctas = (nblocks + 7) / 8;          // 8 warps, one block each
+            store_warp_kernel<T, FMT><<<(int)ctas, 256, 0, st>>>(a);
+            return check_launch();
+        }
     }
     // the staged K output stays within 48 KB (store_ppc), no opt-in needed
     const size_t smem = nk_ctas64 > 0 ? store_smem<T>(a.D, ppc) : 0;
@@ -523,7 +552,7 @@ extern "C" int kivi_store(const void* k, const void* v, int in_dtype, int64_t sk
                           int kpage0, int k_np_stride, uint8_t* v_packed, void* v_scale, int vtok0,
                           int v_s_stride, kivi_stream_t stream) {
     if (H < 0 || S_k < 0 || S_v < 0 || D <= 0 || D % BLK) return KIVI_ERR_ARG;
-    if (fmt != FMT_INT4 && fmt != FMT_NVFP4) return KIVI_ERR_ARG;
+    if (fmt != FMT_INT4 && fmt != FMT_NVFP4 && fmt != FMT_MIX43) return KIVI_ERR_ARG;
     if ((unsigned)calib_k > 1 || (unsigned)calib_v > 1) return KIVI_ERR_ARG;
     if ((calib_k == CAL_MSE || calib_v == CAL_MSE) && (!alphas || n_alphas <= 0)) return KIVI_ERR_ARG;
     if (in_dtype != KIVI_DT_BF16 && in_dtype != KIVI_DT_F16 && in_dtype != KIVI_DT_F32) return KIVI_ERR_ARG;
@@ -542,11 +571,14 @@ extern "C" int kivi_store(const void* k, const void* v, int in_dtype, int64_t sk
     cudaStream_t st = (cudaStream_t)stream;
     switch (in_dtype) {
         case KIVI_DT_BF16: return fmt == FMT_INT4 ? launch_store<__nv_bfloat16, FMT_INT4>(a, st)
-                                                  : launch_store<__nv_bfloat16, FMT_NVFP4>(a, st);
+                                : fmt == FMT_NVFP4 ? launch_store<__nv_bfloat16, FMT_NVFP4>(a, st)
+                                                   : launch_store<__nv_bfloat16, FMT_MIX43>(a, st);
         case KIVI_DT_F16: return fmt == FMT_INT4 ? launch_store<__half, FMT_INT4>(a, st)
-                                                 : launch_store<__half, FMT_NVFP4>(a, st);
+                               : fmt == FMT_NVFP4 ? launch_store<__half, FMT_NVFP4>(a, st)
+                                                  : launch_store<__half, FMT_MIX43>(a, st);
         default: return fmt == FMT_INT4 ? launch_store<float, FMT_INT4>(a, st)
-                                        : launch_store<float, FMT_NVFP4>(a, st);
+                      : fmt == FMT_NVFP4 ? launch_store<float, FMT_NVFP4>(a, st)
+                                         : launch_store<float, FMT_MIX43>(a, st);
     }
 }
 
@@ -555,7 +587,7 @@ extern "C" int kivi_dequant(const uint8_t* k_packed, const void* k_scale, int k_
                             int S, int D, int fmt, float g_k, float g_v, void* k_out, void* v_out,
                             int64_t so_h, int64_t so_s, int64_t so_d, kivi_stream_t stream) {
     if (H < 0 || S < 0 || D <= 0 || D % BLK) return KIVI_ERR_ARG;
-    if (fmt != FMT_INT4 && fmt != FMT_NVFP4) return KIVI_ERR_ARG;
+    if (fmt != FMT_INT4 && fmt != FMT_NVFP4 && fmt != FMT_MIX43) return KIVI_ERR_ARG;
     if (k_np_stride < S / BLK || v_s_stride < S) return KIVI_ERR_ARG;
     if ((uintptr_t)k_packed % 8 || (uintptr_t)v_packed % 8) return KIVI_ERR_ALIGN;
     const int64_t n = (int64_t)H * (S / BLK) * D + (int64_t)H * S * (D / BLK);
@@ -564,7 +596,8 @@ extern "C" int kivi_dequant(const uint8_t* k_packed, const void* k_scale, int k_
                   g_k, g_v, k_out, v_out, so_h, so_s, so_d};
     cudaStream_t st = (cudaStream_t)stream;
     if (fmt == FMT_INT4) dequant_kernel<FMT_INT4><<<grid_for(n), 256, 0, st>>>(a);
-    else dequant_kernel<FMT_NVFP4><<<grid_for(n), 256, 0, st>>>(a);
+    else if (fmt == FMT_NVFP4) dequant_kernel<FMT_NVFP4><<<grid_for(n), 256, 0, st>>>(a);
+    else dequant_kernel<FMT_MIX43><<<grid_for(n), 256, 0, st>>>(a);
     return check_launch();
 }
 

@@ -16,7 +16,7 @@ import torch
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("KIVI_LIB_PATH") or os.path.join(os.path.dirname(_HERE), "libkivi_sm100.so")
 
-FMT = {"int4": 0, "int3": 1, "nvfp4": 2}
+FMT = {"int4": 0, "int3": 1, "nvfp4": 2, "int4k_int3v": 3}
 CALIB = {"absmax": 0, "mse": 1}
 LAYOUT = {"headdim": 0, "channel": 1}
 DTYPE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}

@@ -66,15 +66,16 @@ class KIVICache:
 # --------------------------------------------------------------------------- #
 # capacity-backed allocation
 # --------------------------------------------------------------------------- #
-def alloc_packed(H: int, S: int, D: int, device, scale_dtype, s_cap: Optional[int] = None):
+def alloc_packed(H: int, S: int, D: int, device, scale_dtype, s_cap: Optional[int] = None, v_pack: int = PACK):
     """Zeroed capacity buffers (k_packed, k_scale, v_packed, v_scale) for up to
-    s_cap tokens; page and token strides are multiples of 16."""
+    s_cap tokens; page and token strides are multiples of 16.  v_pack is the
+    bytes per packed V block (8; 6 for the INT3 V of the mixed cache)."""
     s_cap = _round_up(max(s_cap or S, S, 1), ALIGN * BLOCK)
     np_cap = s_cap // BLOCK
     ND = D // BLOCK
     kp = torch.zeros((H, D, np_cap, PACK), dtype=torch.uint8, device=device)
     ks = torch.zeros((H, D, np_cap), dtype=scale_dtype, device=device)
-    vp = torch.zeros((H, s_cap, ND, PACK), dtype=torch.uint8, device=device)
+    vp = torch.zeros((H, s_cap, ND, v_pack), dtype=torch.uint8, device=device)
     vs = torch.zeros((H, s_cap, ND), dtype=scale_dtype, device=device)
     return kp, ks, vp, vs
 
@@ -85,12 +86,13 @@ def cache_geometry(c) -> tuple[int, int]:
     `c` is a cache object or a (k_packed, k_scale, v_packed, v_scale) tuple."""
     kp, ks, vp, vs = c if isinstance(c, tuple) else (c.k_packed, c.k_scale, c.v_packed, c.v_scale)
     np_stride = kp.stride(1) // PACK if kp.dim() == 4 else 0
-    s_stride = vp.stride(0) // (vp.shape[2] * PACK) if vp.dim() == 4 and vp.shape[2] else 0
+    VP = vp.shape[3] if vp.dim() == 4 else PACK           # bytes per V block
+    s_stride = vp.stride(0) // (vp.shape[2] * VP) if vp.dim() == 4 and vp.shape[2] else 0
     ok = (kp.dim() == 4 and kp.stride(3) == 1 and kp.stride(2) == PACK and kp.stride(1) == np_stride * PACK
           and kp.stride(0) == kp.shape[1] * np_stride * PACK
           and ks.dim() == 3 and ks.stride(2) == 1 and ks.stride(1) == np_stride and ks.stride(0) == ks.shape[1] * np_stride
-          and vp.dim() == 4 and vp.stride(3) == 1 and vp.stride(2) == PACK and vp.stride(1) == vp.shape[2] * PACK
-          and vp.stride(0) == s_stride * vp.shape[2] * PACK
+          and vp.dim() == 4 and vp.stride(3) == 1 and vp.stride(2) == VP and vp.stride(1) == vp.shape[2] * VP
+          and vp.stride(0) == s_stride * vp.shape[2] * VP
           and vs.dim() == 3 and vs.stride(2) == 1 and vs.stride(1) == vs.shape[2] and vs.stride(0) == s_stride * vs.shape[2])
     if not ok:
         raise ValueError("packed cache tensors do not have the page/token-strided layout")
@@ -101,7 +103,7 @@ def relayout(c):
     """Copy a cache whose packed tensors are arbitrary (e.g. user-built or
     torch.cat'ed with odd page counts) into 16-aligned capacity buffers."""
     H, S, D = c.k_packed.shape[0], c.S, c.D
-    kp, ks, vp, vs = alloc_packed(H, S, D, c.k_packed.device, c.k_scale.dtype)
+    kp, ks, vp, vs = alloc_packed(H, S, D, c.k_packed.device, c.k_scale.dtype, v_pack=c.v_packed.shape[3])
     NP = c.k_packed.shape[2]
     kp[:, :, :NP].copy_(c.k_packed); ks[:, :, :NP].copy_(c.k_scale)
     vp[:, :S].copy_(c.v_packed); vs[:, :S].copy_(c.v_scale)
@@ -166,7 +168,7 @@ def full_views(c):
     ND = D // BLOCK
     kp = c.k_packed.as_strided((H, D, np_stride, PACK), c.k_packed.stride())
     ks = c.k_scale.as_strided((H, D, np_stride), c.k_scale.stride())
-    vp = c.v_packed.as_strided((H, s_stride, ND, PACK), c.v_packed.stride())
+    vp = c.v_packed.as_strided((H, s_stride, ND, c.v_packed.shape[3]), c.v_packed.stride())
     vs = c.v_scale.as_strided((H, s_stride, ND), c.v_scale.stride())
     return kp, ks, vp, vs
 
@@ -190,7 +192,8 @@ def append_kivi(cache, k_new: Tensor, v_new: Tensor, k_calib: str = "mse", v_cal
     except ValueError:
         fits = False
     if not fits:
-        kp, ks, vp, vs = alloc_packed(H, S1, D, k_new.device, cache.k_scale.dtype, s_cap=2 * S1)
+        kp, ks, vp, vs = alloc_packed(H, S1, D, k_new.device, cache.k_scale.dtype, s_cap=2 * S1,
+                                      v_pack=cache.v_packed.shape[3])
         NP0 = cache.k_packed.shape[2]
         kp[:, :, :NP0].copy_(cache.k_packed); ks[:, :, :NP0].copy_(cache.k_scale)
         vp[:, :S0].copy_(cache.v_packed); vs[:, :S0].copy_(cache.v_scale)

@@ -36,7 +36,8 @@ def _stacked_geometry(st: dict) -> tuple[int, int, dict]:
     except ValueError:
         BH, D, NP, _ = st["k_packed"].shape
         S = st["v_packed"].shape[1]
-        kp, ks, vp, vs = alloc_packed(BH, S, D, st["k_packed"].device, st["k_scale"].dtype)
+        kp, ks, vp, vs = alloc_packed(BH, S, D, st["k_packed"].device, st["k_scale"].dtype,
+                                      v_pack=st["v_packed"].shape[3])
         kp[:, :, :NP].copy_(st["k_packed"]); ks[:, :, :NP].copy_(st["k_scale"])
         vp[:, :S].copy_(st["v_packed"]); vs[:, :S].copy_(st["v_scale"])
         out = dict(st, k_packed=kp[:, :, :NP], k_scale=ks[:, :, :NP], v_packed=vp[:, :S], v_scale=vs[:, :S])
@@ -259,7 +260,7 @@ def stack_caches(caches: list) -> dict:
         return _stack_varlen(caches)
     B = len(caches)
     NP = c0.k_packed.shape[2]
-    kp, ks, vp, vs = alloc_packed(B * H, S, D, c0.k_packed.device, c0.k_scale.dtype)
+    kp, ks, vp, vs = alloc_packed(B * H, S, D, c0.k_packed.device, c0.k_scale.dtype, v_pack=c0.v_packed.shape[3])
     for b, c in enumerate(caches):
         kp[b * H:(b + 1) * H, :, :NP].copy_(c.k_packed)
         ks[b * H:(b + 1) * H, :, :NP].copy_(c.k_scale)
@@ -285,7 +286,7 @@ def _stack_varlen(caches: list) -> dict:
     S = max(c.S for c in caches)
     NP = S // BLOCK
     dev = c0.k_packed.device
-    kp, ks, vp, vs = alloc_packed(B * H, S, D, dev, c0.k_scale.dtype)
+    kp, ks, vp, vs = alloc_packed(B * H, S, D, dev, c0.k_scale.dtype, v_pack=c0.v_packed.shape[3])
     khot = torch.zeros(B * H, BLOCK, D, dtype=torch.bfloat16, device=dev)
     for b, c in enumerate(caches):
         npb = c.k_packed.shape[2]

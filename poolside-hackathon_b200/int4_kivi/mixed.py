@@ -1,0 +1,65 @@
+"""Mixed-precision KIVI cache: K INT4 per channel, V INT3 per token.
+
+The reference names a 3-bit-V / 4-bit-K cache as its next step past the
+uniform 4-bit floor (WRITEUP.md:336-339) and defines the INT3 grid in
+kv_quant.py:215-217 (`int3`: round half to even, clamp to [-3, 3], scale =
+absmax / 3 or the MSE clip search over the same 32-point alpha grid,
+kv_quant.py:247-266).  It ships no packed INT3 store or decode, so the cache
+layout below is this library's own:
+
+    K exactly as KIVICache (INT4 codes, fp16 scale per channel and 16-token
+      page, the S % 16 tail kept bf16 in k_hot);
+    V codes against the fp32 block scale, the scale stored as fp16 (as every
+      KIVI scale); a 16-channel block is 16 three-bit two's-complement codes,
+      element i in bits [3i, 3i + 3) of a little-endian 48-bit word:
+        v_packed u8 [H, S, D/16, 6],  v_scale f16 [H, S, D/16].
+
+Per token and kv-head the cache holds 64 + 16 + 48 + 16 = 144 bytes (160 for
+INT4 KIVI, 512 for bf16).  The fused decode runs on the CUDA-core path of
+libkivi_sm100 (the tensor-core path takes INT4 and NVFP4 pages only).
+"""
+from __future__ import annotations
+
+import dataclasses
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from .cache import BLOCK, KIVICache, alloc_packed, dequant_packed, store_into
+
+PACK3 = 6           # bytes per packed INT3 V block
+QMAX3 = 3
+
+
+@dataclasses.dataclass
+class Int3VKIVICache(KIVICache):
+    """KIVICache with INT3 V blocks (v_packed [H, S, D/16, 6])."""
+    g_k: float = 1.0
+    g_v: float = 1.0
+
+    def __post_init__(self):
+        self.fmt = "int4k_int3v"
+
+
+def store_kivi_int3v(k: Tensor, v: Tensor, k_calib: str = "mse", v_calib: str = "mse",
+                     capacity: Optional[int] = None) -> Int3VKIVICache:
+    """Quantise bf16 k/v [H, S, D] (CUDA): K INT4 per channel, V INT3 per token.
+    `capacity` (tokens) reserves room for in-place `append_kivi`."""
+    assert k.shape == v.shape, "k and v must share shape [H, S, D]"
+    assert k.is_cuda and v.is_cuda, "inputs must be on CUDA"
+    H, S, D = k.shape
+    assert D % BLOCK == 0, "head_dim must be a multiple of 16"
+    k = k.to(torch.bfloat16)
+    v = v.to(torch.bfloat16)
+    n_full = (S // BLOCK) * BLOCK
+    NP = n_full // BLOCK
+    kp, ks, vp, vs = alloc_packed(H, S, D, k.device, torch.float16, capacity, v_pack=PACK3)
+    store_into(k, v, "int4k_int3v", k_calib, v_calib, kp, ks, vp, vs, 0, 0)
+    return Int3VKIVICache(k_packed=kp[:, :, :NP], k_scale=ks[:, :, :NP], k_hot=k[:, n_full:].contiguous(),
+                          v_packed=vp[:, :S], v_scale=vs[:, :S], H=H, S=S, D=D)
+
+
+def dequant_kivi_int3v(cache: Int3VKIVICache) -> tuple[Tensor, Tensor]:
+    """bf16 [H, S, D] K and V (K tail verbatim bf16)."""
+    return dequant_packed(cache)

@@ -264,3 +264,26 @@ def test_heavy_tail_store_oracle(calib):
     assert np.array_equal(c["v_scale"].view(np.uint16), g[f"{calib}_v_scale"])
     rt = torch.from_numpy(oracle.roundtrip_f32(k, "int4", "channel", calib)).to(torch.bfloat16)
     assert torch.equal(rt, bf16_from_bits(g[f"{calib}_k_rt"]))
+
+
+@pytest.mark.parametrize("calib", CALIBS)
+def test_int3v_store_pinned_to_roundtrip(calib):
+    """The mixed cache's INT3 V codes, times the fp32 block scale, are the
+    reference's kv_quant.roundtrip(v, "int3", "headdim", calib) bit for bit;
+    the stored fp16 scale is that fp32 scale rounded; dequant = code * scale."""
+    g = load_golden("kvq_roundtrip.npz")
+    k, v = bf16_from_bits(g["k"]), bf16_from_bits(g["v"])
+    H, S, D = v.shape
+    c = oracle.store_int3v(k, v, calib, calib)
+    assert c["v_packed"].shape == (H, S, D // 16, 6)
+    codes = oracle.unpack_int3(c["v_packed"]).astype(np.float32)
+    assert codes.min() >= -3 and codes.max() <= 3
+    s32 = oracle.calibrate(v.float().numpy().reshape(-1, 16), "int3", calib).reshape(H, S, D // 16, 1)
+    got = torch.from_numpy((codes * s32).reshape(H, S, D)).to(torch.bfloat16)
+    assert torch.equal(got, bf16_from_bits(g[f"v_int3_headdim_{calib}"]))
+    assert np.array_equal(c["v_scale"], s32[..., 0].astype(np.float16))
+    _, vd = oracle.dequant_int3v(c)
+    assert np.array_equal(vd, (codes * c["v_scale"][..., None].astype(np.float32)).reshape(H, S, D))
+    # K is the INT4 cache's K
+    c4 = oracle.store_int4(k, v, calib, calib)
+    assert np.array_equal(c["k_packed"], c4["k_packed"]) and np.array_equal(c["k_scale"], c4["k_scale"])
