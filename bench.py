@@ -277,6 +277,21 @@ def extra_configs(dev, peak: float, int4_ms: float | None = None) -> dict:
                                       "bytes_per_step": by2}
     del st2, c, g2, kp, ks, vp, vs
     torch.cuda.empty_cache()
+    # ---- mixed cache (K INT4, V INT3; CUDA-core decode path) at 65536 ----
+    from int4_kivi.mixed import store_kivi_int3v
+    k, v, q = make_inputs(S2, seed=9, device=dev)
+    cm = store_kivi_int3v(k.reshape(BH, S2, D), v.reshape(BH, S2, D), "absmax", "absmax")
+    del k, v
+    stm = dict(k_packed=cm.k_packed, k_scale=cm.k_scale, k_hot=cm.k_hot, v_packed=cm.v_packed,
+               v_scale=cm.v_scale, H=HKV, S=S2, D=D, B=B, fmt="int4k_int3v", g_k=1.0, g_v=1.0)
+    gm = graph_step(lambda: decode_packed(q, stm, HQ, out=out))
+    msm = time_graph(gm)
+    bym = BH * S2 * 144
+    res["int4k_int3v_S65536"] = {"ms_per_step": round(msm, 4), "GB/s": round(bym / msm / 1e6, 1),
+                                 "frac": round(bym / msm / 1e6 / peak, 4), "decode_tok_s": round(B / msm * 1e3, 1),
+                                 "bytes_per_step": bym}
+    del stm, cm, gm
+    torch.cuda.empty_cache()
     res.update(paged_configs(dev, peak))
     res.update(bf16_comparator(dev, peak, int4_ms))
     return res
@@ -341,6 +356,14 @@ def store_configs(dev, peak: float) -> dict:
                 r["alpha_evals_per_s"] = round(2 * BH * S * (D // 16) * 32 / (ms * 1e-3), 1)
             res[f"{name}_{calib}"] = r
             del gr
+        if S == 65536:      # the mixed cache (K INT4, V INT3) from the same inputs
+            kp3, ks3, vp3, vs3 = alloc_packed(BH, S, D, dev, torch.float16, v_pack=12)
+            by3 = 2 * BH * S * D * 2 + BH * S * 144
+            gr = graph_step(lambda: store_into(k, v, "int4k_int3v", "absmax", "absmax", kp3, ks3, vp3, vs3, 0, 0))
+            ms = time_graph(gr, seconds=0.5)
+            res[f"{name}_int4k_int3v_absmax"] = {"us": round(ms * 1e3, 2), "GB/s": round(by3 / ms / 1e6, 1),
+                                                 "frac": round(by3 / ms / 1e6 / peak, 4), "bytes": by3}
+            del gr, kp3, ks3, vp3, vs3
         del k, v, kp, ks, vp, vs
     for Bs in (1, 8, 32):
         g = torch.Generator(device=dev).manual_seed(4)

@@ -179,12 +179,13 @@ def dequant_int4(c: dict) -> tuple[np.ndarray, np.ndarray]:
 
 def store_int3v(k, v, k_calib: str = "mse", v_calib: str = "mse", n_alphas: int = 32) -> dict:
     """The mixed-precision cache (K INT4 as store_int4, V INT3 per token on the
-    kv_quant `int3` grid): v_packed u8 [H,S,ND,6] (3-bit two's-complement codes,
-    element i at bits 3i..3i+2 of a little-endian 48-bit word), v_scale f16."""
+    kv_quant `int3` grid): v_packed u8 [H,S,D/32,12] (block pairs: words A_2k,
+    A_2k+1 with the low two bits of each code, S_k with the sign bits; see
+    kivi_oracle.c), v_scale f16 [H,S,D/16]."""
     c = store_int4(k, v, k_calib, "absmax", n_alphas)
     vf = _f32(v)
     H, S, D = vf.shape
-    vp = np.zeros((H, S, D // BLOCK, 6), np.uint8)
+    vp = np.zeros((H, S, D // (2 * BLOCK), 12), np.uint8)
     vs = np.zeros((H, S, D // BLOCK), np.uint16)
     lib().orc_store_v3(_p(vf), H, S, D, CALIB[v_calib], _p(alphas(n_alphas)), n_alphas, _p(vp), _p(vs))
     c.update(v_packed=vp, v_scale=vs.view(np.float16))
@@ -192,13 +193,19 @@ def store_int3v(k, v, k_calib: str = "mse", v_calib: str = "mse", n_alphas: int 
 
 
 def unpack_int3(packed: np.ndarray) -> np.ndarray:
-    """[..., 6] INT3 blocks -> int8 codes [..., 16]."""
-    b = packed.astype(np.uint64)
-    w = np.zeros(packed.shape[:-1], np.uint64)
-    for j in range(6):
-        w |= b[..., j] << np.uint64(8 * j)
-    f = np.stack([(w >> np.uint64(3 * i)) & np.uint64(7) for i in range(BLOCK)], axis=-1).astype(np.int8)
-    return np.where(f >= 4, f - 8, f).astype(np.int8)
+    """[..., D/32, 12] INT3 block pairs -> int8 codes [..., D/16, 16]."""
+    w = np.ascontiguousarray(packed).view("<u4")                     # [..., D/32, 3]
+    out = []
+    for o in range(2):
+        A, S = w[..., o].astype(np.int64), w[..., 2].astype(np.int64)
+        codes = []
+        for i in range(BLOCK):
+            sha = 4 * i if i < 8 else 4 * (i - 8) + 2
+            shs = (4 * i if i < 8 else 4 * (i - 8) + 1) + 2 * o
+            codes.append(((A >> sha) & 3) - 4 * ((S >> shs) & 1))
+        out.append(np.stack(codes, axis=-1))
+    res = np.stack(out, axis=-2)                                     # [..., D/32, 2, 16]
+    return res.reshape(res.shape[:-3] + (-1, BLOCK)).astype(np.int8)
 
 
 def dequant_int3v(c: dict) -> tuple[np.ndarray, np.ndarray]:

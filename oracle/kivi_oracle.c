@@ -314,30 +314,42 @@ void orc_dequant_int4(const uint8_t *k_packed, const uint16_t *k_scale,
 /* over 16-channel blocks on the kv_quant.py:215-217 `int3` grid (qmax 3,     */
 /* kv_quant.py:247-266 calibration), codes against the fp32 scale, scale      */
 /* stored as fp16.  The reference has no packed INT3 layout; this library's:  */
-/* 16 three-bit two's-complement codes, element i in bits [3i, 3i + 3) of a   */
-/* little-endian 48-bit word, 6 bytes per block.                              */
+/* c in [-3, 3] kept as L = c & 3 and sign s (c = L - 4s); blocks in pairs    */
+/* (2k, 2k+1) of three little-endian u32 words A_2k, A_2k+1, S_k (12 bytes):  */
+/* A_b has L of element i < 8 at bit 4i, of element 8+i at bit 4i+2; S_k has  */
+/* s of element i < 8 of block 2k+o at bit 4i+2o, of element 8+i at 4i+1+2o.  */
 /* ------------------------------------------------------------------------- */
-static void pack16_3(const int c[BLK], uint8_t out[6]) {
-    uint64_t w = 0;
-    for (int i = 0; i < BLK; ++i) w |= (uint64_t)(c[i] & 7) << (3 * i);
-    for (int j = 0; j < 6; ++j) out[j] = (uint8_t)(w >> (8 * j));
+static void put_u32(uint8_t *p, uint32_t w) {
+    for (int j = 0; j < 4; ++j) p[j] = (uint8_t)(w >> (8 * j));
+}
+static uint32_t get_u32(const uint8_t *p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
 }
 
-/* v: fp32 [H, S, D] -> v_packed [H, S, ND, 6], v_scale f16 [H, S, ND]. */
+/* v: fp32 [H, S, D] (D % 32 == 0) -> v_packed [H, S, D/32, 12], v_scale f16 [H, S, D/16]. */
 void orc_store_v3(const float *v, int H, int S, int D, int calib_v, const float *alphas,
                   int n_alphas, uint8_t *v_packed, uint16_t *v_scale) {
     int ND = D / BLK;
     #pragma omp parallel for collapse(2) schedule(static)
     for (int h = 0; h < H; ++h)
         for (int t = 0; t < S; ++t)
-            for (int db = 0; db < ND; ++db) {
-                float x[BLK]; int c[BLK];
-                gather_block(v, S, D, LAYOUT_HEADDIM, h, t, db, x);
-                float s = orc_calibrate_block(x, FMT_INT3, calib_v, alphas, n_alphas);
-                for (int j = 0; j < BLK; ++j) c[j] = (int)q_grid(x[j] / s, FMT_INT3);
-                size_t r = ((size_t)h * S + t) * ND + db;
-                pack16_3(c, v_packed + r * 6);
-                v_scale[r] = orc_f32_to_f16(s);
+            for (int pr = 0; pr < ND / 2; ++pr) {
+                uint32_t A[2] = {0, 0}, Sw = 0;
+                for (int o = 0; o < 2; ++o) {
+                    int db = 2 * pr + o;
+                    float x[BLK];
+                    gather_block(v, S, D, LAYOUT_HEADDIM, h, t, db, x);
+                    float s = orc_calibrate_block(x, FMT_INT3, calib_v, alphas, n_alphas);
+                    for (int i = 0; i < BLK; ++i) {
+                        int c = (int)q_grid(x[i] / s, FMT_INT3);
+                        int sha = i < 8 ? 4 * i : 4 * (i - 8) + 2, shs = (i < 8 ? 4 * i : 4 * (i - 8) + 1) + 2 * o;
+                        A[o] |= (uint32_t)(c & 3) << sha;
+                        Sw |= (uint32_t)(c < 0) << shs;
+                    }
+                    v_scale[((size_t)h * S + t) * ND + db] = orc_f32_to_f16(s);
+                }
+                uint8_t *out = v_packed + (((size_t)h * S + t) * (ND / 2) + pr) * 12;
+                put_u32(out, A[0]); put_u32(out + 4, A[1]); put_u32(out + 8, Sw);
             }
 }
 
@@ -348,13 +360,14 @@ void orc_dequant_v3(const uint8_t *v_packed, const uint16_t *v_scale, int H, int
     for (int h = 0; h < H; ++h)
         for (int t = 0; t < S; ++t)
             for (int db = 0; db < ND; ++db) {
-                size_t r = ((size_t)h * S + t) * ND + db;
-                uint64_t w = 0;
-                for (int j = 0; j < 6; ++j) w |= (uint64_t)v_packed[r * 6 + j] << (8 * j);
-                float s = orc_f16_to_f32(v_scale[r]);
-                for (int c = 0; c < BLK; ++c) {
-                    int f = (int)((w >> (3 * c)) & 7);
-                    vout[((size_t)h * S + t) * D + db * BLK + c] = (float)(f >= 4 ? f - 8 : f) * s;
+                const uint8_t *pp = v_packed + (((size_t)h * S + t) * (ND / 2) + db / 2) * 12;
+                int o = db & 1;
+                uint32_t A = get_u32(pp + 4 * o), Sw = get_u32(pp + 8);
+                float s = orc_f16_to_f32(v_scale[((size_t)h * S + t) * ND + db]);
+                for (int i = 0; i < BLK; ++i) {
+                    int sha = i < 8 ? 4 * i : 4 * (i - 8) + 2, shs = (i < 8 ? 4 * i : 4 * (i - 8) + 1) + 2 * o;
+                    int c = (int)((A >> sha) & 3) - 4 * (int)((Sw >> shs) & 1);
+                    vout[((size_t)h * S + t) * D + db * BLK + i] = (float)c * s;
                 }
             }
 }

@@ -19,10 +19,19 @@ constexpr int PACKB = 8;  // bytes per packed block
 
 // FMT_MIX43: the mixed-precision cache, K INT4 (the KIVI K layout) and V INT3
 // per token over 16-channel blocks (the kv_quant.py:215-217 `int3` grid,
-// qmax 3); a V block is 16 three-bit two's-complement codes, element i in
-// bits [3i, 3i + 3) of a little-endian 48-bit word (6 bytes).
+// qmax 3), 6 bytes per block.  A code c in [-3, 3] is stored as its low two
+// bits L = c & 3 and a sign bit s (c = L - 4s).  Blocks go in pairs (2k,
+// 2k + 1) of 12 bytes: two 32-bit words A_{2k}, A_{2k+1} and one word S_k.
+//   A_b:  L of element i < 8 at bits [4i, 4i + 2), of element 8 + i at bits
+//         [4i + 2, 4i + 4);
+//   S_k:  s of element i < 8 of block 2k + o at bit 4i + 2o, of element
+//         8 + i at bit 4i + 1 + 2o.
+// So (A & 0x33333333) and ((A >> 2) & 0x33333333) are the low two bits of
+// the nibble words of elements 0..7 and 8..15, and the sign bits land on bit
+// 2 of each nibble with one shift: a block becomes 3-bit nibbles c & 7 (the
+// INT4 nibble layout, bit 3 clear) in a few logic operations.
 enum Fmt { FMT_INT4 = 0, FMT_INT3 = 1, FMT_NVFP4 = 2, FMT_MIX43 = 3 };
-constexpr int PACKB3 = 6;  // bytes per packed INT3 block
+constexpr int PACKB3 = 6;  // bytes per packed INT3 block (12 per block pair)
 enum Calib { CAL_ABSMAX = 0, CAL_MSE = 1 };
 
 __device__ __forceinline__ float qmax_of(int fmt) {
@@ -162,13 +171,35 @@ template <> __device__ __forceinline__ float from_f32<float>(float v) { return v
 
 __device__ __forceinline__ int sx4(int n) { return n >= 8 ? n - 16 : n; }
 
-// Code i (0..15) of a 6-byte INT3 block (FMT_MIX43 V).
-__device__ __forceinline__ int int3_code(const uint8_t* blk, int i) {
-    const int b = 3 * i, byte = b >> 3, sh = b & 7;
-    uint32_t w = blk[byte];
-    if (sh > 5) w |= (uint32_t)blk[byte + 1] << 8;   // the field crosses into the next byte
-    const int f = (int)((w >> sh) & 7u);
-    return f >= 4 ? f - 8 : f;
+// FMT_MIX43 V: the 8-nibble words (elements 0..7, 8..15; nibble = c & 7) of
+// block 2k + o from its pair's words A (= A_{2k+o}) and S (= S_k).
+__device__ __forceinline__ void int3_pair_nibbles(uint32_t A, uint32_t S, int o, uint32_t& lo, uint32_t& hi) {
+    const uint32_t slo = (o ? S : S << 2) & 0x44444444u;
+    const uint32_t shi = (o ? S >> 1 : S << 1) & 0x44444444u;
+    lo = (A & 0x33333333u) | slo;
+    hi = ((A >> 2) & 0x33333333u) | shi;
+}
+// Code of channel d of a token row (6 * ND bytes) of FMT_MIX43 V.
+__device__ __forceinline__ int int3_code(const uint8_t* row, int d) {
+    const int db = d >> 4, i = d & 15, o = db & 1;
+    const uint32_t* pw = reinterpret_cast<const uint32_t*>(row + 12 * (db >> 1));
+    const uint32_t A = pw[o], S = pw[2];
+    const int L = (int)(A >> (i < 8 ? 4 * i : 4 * (i - 8) + 2)) & 3;
+    const int s = (int)(S >> ((i < 8 ? 4 * i : 4 * (i - 8) + 1) + 2 * o)) & 1;
+    return L - 4 * s;
+}
+// Pack two blocks' codes (c in [-3, 3]) into the 12-byte pair.
+__device__ __forceinline__ void int3_pack_pair(const int c0[16], const int c1[16], uint32_t& A0, uint32_t& A1,
+                                               uint32_t& S) {
+    A0 = A1 = S = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int sha = i < 8 ? 4 * i : 4 * (i - 8) + 2, shs = i < 8 ? 4 * i : 4 * (i - 8) + 1;
+        A0 |= (uint32_t)(c0[i] & 3) << sha;
+        A1 |= (uint32_t)(c1[i] & 3) << sha;
+        S |= (uint32_t)(c0[i] < 0) << shs;
+        S |= (uint32_t)(c1[i] < 0) << (shs + 2);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -205,6 +236,12 @@ __device__ __forceinline__ void sts32s(uint32_t a, uint32_t v) {
 }
 __device__ __forceinline__ void sts64s(uint32_t a, uint32_t x, uint32_t y) {
     asm volatile("st.shared.v2.u32 [%0], {%1, %2};" :: "r"(a), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ uint4 lds128s(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a)
+                 : "memory");
+    return v;
 }
 __device__ __forceinline__ void sts128s(uint32_t a, uint4 v) {
     asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" :: "r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
@@ -294,6 +331,15 @@ __device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_c
 __device__ __forceinline__ __half2 int4_lo_to_h2(uint32_t w) {
     uint32_t v = lop3_and_xor(w, 0x000F000Fu, 0x64086408u);      // 1024 + (n ^ 8)
     return __hsub2(u32_as_h2(v), u32_as_h2(0x64086408u));         // - 1032
+}
+// FMT_MIX43 V nibbles hold c & 7 (bit 3 clear): (n ^ 4) = c + 4.
+__device__ __forceinline__ __half2 int3n_lo_to_h2(uint32_t w) {
+    uint32_t v = lop3_and_xor(w, 0x000F000Fu, 0x64046404u);      // 1024 + (n ^ 4)
+    return __hsub2(u32_as_h2(v), u32_as_h2(0x64046404u));         // - 1028
+}
+__device__ __forceinline__ __half2 int3n_hi_to_h2(uint32_t w) {
+    uint32_t v = lop3_and_xor(w, 0x00F000F0u, 0x64406440u);      // 1024 + 16 (n ^ 4)
+    return __hfma2(u32_as_h2(v), u32_as_h2(0x2C002C00u), u32_as_h2(0xD440D440u));   // * 1/16 - 68
 }
 __device__ __forceinline__ __half2 int4_hi_to_h2(uint32_t w) {
     uint32_t v = lop3_and_xor(w, 0x00F000F0u, 0x64806480u);      // 1024 + 16 (n ^ 8)

@@ -181,7 +181,11 @@ struct StageLayout {
     static constexpr int VC = 8192 + 2048;              // 128 tok x 64 B, 64B-swizzled
     static constexpr int VS = VC + 8192;                // INT4: 128 x 16 B ; NVFP4: 128 x 8 B
     static constexpr int BYTES = VS + 2048;
-    static constexpr uint32_t TX = (FMT == FMT_NVFP4) ? (8192 + 2048 + 8192 + 1024) : 20480;
+    // FMT_MIX43: V codes arrive as four 32-token boxes of 48-byte INT3 rows,
+    // warp w's at VC + 2048 w + VC3_OFF (inside the 2 KB its nibble rows fill)
+    static constexpr int VC3_OFF = 512;
+    static constexpr uint32_t TX = (FMT == FMT_NVFP4) ? (8192 + 2048 + 8192 + 1024)
+                                 : (FMT == FMT_MIX43) ? (8192 + 2048 + 6144 + 2048) : 20480;
 };
 
 struct __align__(8) SmemCtl {
@@ -199,7 +203,13 @@ __device__ __forceinline__ void set_err(int* err, int code) {
 template <int FMT>
 __device__ __forceinline__ void codes4(uint32_t w, uint32_t& t0_lo, uint32_t& t0_hi,
                                        uint32_t& t1_lo, uint32_t& t1_hi) {
-    if (FMT == FMT_NVFP4) {
+    if (FMT == FMT_MIX43) {
+        t0_lo = h2_as_u32(int3n_lo_to_h2(w));
+        t0_hi = h2_as_u32(int3n_hi_to_h2(w));
+        const uint32_t w8 = w >> 8;
+        t1_lo = h2_as_u32(int3n_lo_to_h2(w8));
+        t1_hi = h2_as_u32(int3n_hi_to_h2(w8));
+    } else if (FMT == FMT_NVFP4) {
         uint32_t h0, h1, h2, h3;
         e2m1x8_to_h2x4(w, h0, h1, h2, h3);
         t0_lo = __byte_perm(h0, h2, 0x5410);
@@ -330,7 +340,13 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                 if (FMT == FMT_NVFP4) tma_load_2d(st + L::KS, &tm_ks, &ctl->full[s], (tl >> 1) * 16, bh * DH);
                 else tma_load_2d(st + L::KS, &tm_ks, &ctl->full[s], tl * 8, bh * DH);
                 const int vrow = bh * p.v_s_stride + tl * TILE;
-                tma_load_2d(st + L::VC, &tm_vc, &ctl->full[s], 0, vrow);
+                if (FMT == FMT_MIX43) {
+#pragma unroll
+                    for (int w = 0; w < NWARP_C; ++w)
+                        tma_load_2d(st + L::VC + 2048 * w + L::VC3_OFF, &tm_vc, &ctl->full[s], 0, vrow + 32 * w);
+                } else {
+                    tma_load_2d(st + L::VC, &tm_vc, &ctl->full[s], 0, vrow);
+                }
                 if (FMT == FMT_NVFP4) tma_load_2d(st + L::VS, &tm_vs, &ctl->full[s], 0, vrow >> 1);
                 else tma_load_2d(st + L::VS, &tm_vs, &ctl->full[s], 0, vrow);
             }
@@ -342,6 +358,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
     }
 
     // ------------------------------- consumers --------------------------------
+    constexpr int KF = FMT == FMT_MIX43 ? FMT_INT4 : FMT;   // K pages' format
     const int g = lane >> 2, tq = lane & 3;
     const int G = p.G;
     const int src_k = ((2 * warp + (g >> 2)) << 2) | tq;   // lane holding my page's K scales
@@ -434,6 +451,24 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
             __syncwarp();
             vs_base = reinterpret_cast<const uint8_t*>(vw) - 32 * warp * 16;
         }
+        if (FMT == FMT_MIX43) {
+            // my token's 48-byte INT3 row -> its 64-byte nibble row (c & 7 per
+            // nibble) in the INT4 tile layout, written over my warp's 2 KB
+            // (which also holds the staged INT3 rows: all lanes read first)
+            const uint32_t raw = smem_u32(st + L::VC + 2048 * warp + L::VC3_OFF + 48 * lane);
+            const uint4 r0 = lds128s(raw), r1 = lds128s(raw + 16), r2 = lds128s(raw + 32);
+            const uint32_t wd[12] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w, r2.x, r2.y, r2.z, r2.w};
+            __syncwarp();
+            const uint32_t row = 32 * warp + lane, vc0 = smem_u32(st + L::VC);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {                 // 16-byte chunk k = blocks 2k, 2k + 1
+                uint32_t l0, h0, l1, h1;
+                int3_pair_nibbles(wd[3 * k], wd[3 * k + 2], 0, l0, h0);
+                int3_pair_nibbles(wd[3 * k + 1], wd[3 * k + 2], 1, l1, h1);
+                sts128s(vc0 + swz64(row, k), make_uint4(l0, h0, l1, h1));
+            }
+            __syncwarp();
+        }
 
         const int t_span = tl * TILE + 32 * warp;      // first token of my span
         const int limit = n_full_h - t_span;           // valid tokens in my span
@@ -468,7 +503,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                     s2 = __shfl_sync(0xffffffffu, s2, src_k);
                     s3 = __shfl_sync(0xffffffffu, s3, src_k);
                 }
-                if constexpr (PAIRED && FMT == FMT_INT4) {
+                if constexpr (PAIRED && KF == FMT_INT4) {
                     uint32_t h0, l0_, h1, l1_, h2, l2_, h3, l3_;
                     split_prod(qB[2 * j][0], s0, h0, l0_);
                     split_prod(qB[2 * j][1], s1, h1, l1_);
@@ -477,8 +512,8 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                     mma_raw2(qa[j & 1], qb[j & 1], r0, r1, h0, h1, l0_, l1_);
                     mma_raw2(qa[j & 1], qb[j & 1], r2, r3, h2, h3, l2_, l3_);
                 } else {
-                    mma_pair<FMT, true>(qa[j & 1], qb[j & 1], r0, r1, s0, s1, qB[2 * j][0], qB[2 * j][1]);
-                    mma_pair<FMT, true>(qa[j & 1], qb[j & 1], r2, r3, s2, s3, qB[2 * j + 1][0], qB[2 * j + 1][1]);
+                    mma_pair<KF, true>(qa[j & 1], qb[j & 1], r0, r1, s0, s1, qB[2 * j][0], qB[2 * j][1]);
+                    mma_pair<KF, true>(qa[j & 1], qb[j & 1], r2, r3, s2, s3, qB[2 * j + 1][0], qB[2 * j + 1][1]);
                 }
             }
             float ca[4], cb[4];
@@ -487,7 +522,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
                 ca[e] = qa[0][e] + qa[1][e];
                 cb[e] = qb[0][e] + qb[1][e];
             }
-            if constexpr (PAIRED && FMT == FMT_INT4) {
+            if constexpr (PAIRED && KF == FMT_INT4) {
                 // keep the column half that matches my rows' page; after this
                 // every lane holds heads 2(tq&1), 2(tq&1)+1 of its rows
                 const bool mine = (g < 4) == (tq < 2);
@@ -587,6 +622,9 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_const
         };
         if (limit >= 32) span(std::false_type{});
         else if (limit > 0) span(std::true_type{});
+        // the nibble rows written above sit where the next TMA of this stage
+        // lands: order the generic-proxy writes before that async-proxy write
+        if (FMT == FMT_MIX43) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->empty[s]);
     }
@@ -616,7 +654,7 @@ __device__ __forceinline__ float gen_code(uint32_t nib) {
 template <int FMT>
 __device__ __forceinline__ float gen_v(const DecodeParams& p, int64_t vr, int d) {
     if (FMT == FMT_MIX43)
-        return (float)int3_code(p.v_packed + vr * PACKB3, d % BLK) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
+        return (float)int3_code(p.v_packed + (vr - d / BLK) * PACKB3, d) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
     const uint32_t vb = p.v_packed[vr * PACKB + (d % BLK) / 2];
     return gen_code<FMT>((vb >> (4 * (d & 1))) & 0xF) * gen_scale<FMT>(p.v_scale, vr, p.g_v);
 }
@@ -977,7 +1015,7 @@ bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-struct DevInfo { int sms = 0; int occ[2] = {0, 0}; };
+struct DevInfo { int sms = 0; int occ[3] = {0, 0, 0}; };
 DevInfo& dev_info(int dev) {
     static DevInfo info[64];
     return info[dev & 63];
@@ -1001,7 +1039,7 @@ int num_sms(int* dev_out) {
 template <int FMT>
 int fast_occupancy(int dev) {
     DevInfo& di = dev_info(dev);
-    const int k = (FMT == FMT_NVFP4) ? 1 : 0;
+    const int k = (FMT == FMT_NVFP4) ? 1 : (FMT == FMT_MIX43) ? 2 : 0;
     if (!di.occ[k]) {
         const size_t smem = fast_smem_bytes<FMT>();
         if (cudaFuncSetAttribute(decode_fast_kernel<FMT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1041,6 +1079,7 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
                 const SeqPar* sp = nullptr, int Tq = 1, int64_t q_st = 0, int q_pos = -1) {
     if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || S < 0 || D <= 0 || D % BLK) return KIVI_ERR_ARG;
     if (fmt != FMT_INT4 && fmt != FMT_NVFP4 && fmt != FMT_MIX43) return KIVI_ERR_ARG;
+    if (fmt == FMT_MIX43 && D % 32) return KIVI_ERR_ARG;
     const bool mq = q_pos >= 0;                       // multi-query decode
     if (Tq < 1 || (!mq && Tq != 1) || (mq && (mode != 0 || seq_lens || sp || q_pos + Tq > S)))
         return KIVI_ERR_ARG;
@@ -1066,14 +1105,14 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     const int sms = num_sms(&dev);
     if (!sms) return record_cuda_error(cudaGetLastError());
 
-    // the mixed INT4-K / INT3-V cache runs on the CUDA-core path only
-    const bool fast = fmt != FMT_MIX43 && D == DH && G <= 8 && sm_scale > 0.0f && k_np_stride % 16 == 0 && v_s_stride % 16 == 0 &&
+    const bool fast = D == DH && G <= 8 && sm_scale > 0.0f && k_np_stride % 16 == 0 && v_s_stride % 16 == 0 &&
                       (uintptr_t)k_packed % 16 == 0 && (uintptr_t)k_scale % 16 == 0 &&
                       (uintptr_t)v_packed % 16 == 0 && (uintptr_t)v_scale % 16 == 0 &&
                       q_sh % 2 == 0 && q_st % 2 == 0 && (uintptr_t)q % 4 == 0 && n_full > 0 &&
                       (int64_t)BH * v_s_stride < (1LL << 31) && (int64_t)BH * D < (1LL << 31);
     if (!fast && (G > GEN_MAXG || D > 32 * GEN_MAXC)) return KIVI_ERR_UNSUPPORTED;
-    const int occ = fast ? (fmt == FMT_NVFP4 ? fast_occupancy<FMT_NVFP4>(dev) : fast_occupancy<FMT_INT4>(dev)) : 4;
+    const int occ = !fast ? 4 : fmt == FMT_NVFP4 ? fast_occupancy<FMT_NVFP4>(dev)
+                             : fmt == FMT_MIX43 ? fast_occupancy<FMT_MIX43>(dev) : fast_occupancy<FMT_INT4>(dev);
     if (!occ) return record_cuda_error(cudaGetLastError());
     const Plan pl = make_plan(BH, n_full, sms, occ);   // varlen: bounds from the max length S
     const int64_t need = pl.slots * G * (2 + (int64_t)D) + (seq_lens ? BH + 2 : 0);
@@ -1111,8 +1150,11 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
             const uint64_t rows_k = (uint64_t)BH * DH, rows_v = (uint64_t)BH * v_s_stride;
             bool ok = make_map(&tkc, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_packed, (uint64_t)k_np_stride * 8, rows_k,
                                (uint64_t)k_np_stride * 8, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B) &&
-                      make_map(&tvc, CU_TENSOR_MAP_DATA_TYPE_UINT8, v_packed, 64, rows_v, 64, 64, 128,
-                               CU_TENSOR_MAP_SWIZZLE_64B);
+                      (fmt == FMT_MIX43
+                           ? make_map(&tvc, CU_TENSOR_MAP_DATA_TYPE_UINT8, v_packed, 48, rows_v, 48, 48, 32,
+                                      CU_TENSOR_MAP_SWIZZLE_NONE)
+                           : make_map(&tvc, CU_TENSOR_MAP_DATA_TYPE_UINT8, v_packed, 64, rows_v, 64, 64, 128,
+                                      CU_TENSOR_MAP_SWIZZLE_64B));
             if (fmt == FMT_NVFP4) {
                 ok = ok && make_map(&tks, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_scale, (uint64_t)k_np_stride, rows_k,
                                     (uint64_t)k_np_stride, 16, 128, CU_TENSOR_MAP_SWIZZLE_NONE) &&
@@ -1125,7 +1167,11 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
                               CU_TENSOR_MAP_SWIZZLE_NONE);
             }
             if (!ok) return KIVI_ERR_CUDA;
-            if (fmt == FMT_NVFP4 && G <= 4)
+            if (fmt == FMT_MIX43 && G <= 4)
+                decode_fast_kernel<FMT_MIX43, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_MIX43>(), st>>>(tkc, tks, tvc, tvs, p);
+            else if (fmt == FMT_MIX43)
+                decode_fast_kernel<FMT_MIX43, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_MIX43>(), st>>>(tkc, tks, tvc, tvs, p);
+            else if (fmt == FMT_NVFP4 && G <= 4)
                 decode_fast_kernel<FMT_NVFP4, true><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>(), st>>>(tkc, tks, tvc, tvs, p);
             else if (fmt == FMT_NVFP4)
                 decode_fast_kernel<FMT_NVFP4, false><<<pl.N, NTHREADS, fast_smem_bytes<FMT_NVFP4>(), st>>>(tkc, tks, tvc, tvs, p);

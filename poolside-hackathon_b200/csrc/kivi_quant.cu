@@ -99,19 +99,14 @@ __device__ __forceinline__ void quant_pack(const float x[BLK], int calib, const 
 }
 
 // One V block of the mixed cache: INT3 codes against the fp32 scale (scale
-// stored as fp16, like every KIVI scale), packed 3 bits per element; writes
-// the 6 bytes at v_packed + row * 6 as three 16-bit words.
-__device__ __forceinline__ void store_v3(const float x[BLK], int calib, const float* alphas, int n_alphas,
-                                         uint8_t* v_packed, void* v_scale, int64_t row) {
+// stored as fp16, like every KIVI scale).
+__device__ __forceinline__ void quant_v3(const float x[BLK], int calib, const float* alphas, int n_alphas,
+                                         int c[BLK], uint16_t& sbits) {
     const float s = calibrate16(x, FMT_INT3, calib, alphas, n_alphas);
     const float r = __frcp_rn(s);
-    uint64_t w = 0;
 #pragma unroll
-    for (int i = 0; i < BLK; ++i)
-        w |= (uint64_t)((uint32_t)(int)q_grid_div(x[i], s, r, FMT_INT3) & 7u) << (3 * i);
-    uint16_t* o = reinterpret_cast<uint16_t*>(v_packed + row * PACKB3);
-    o[0] = (uint16_t)w; o[1] = (uint16_t)(w >> 16); o[2] = (uint16_t)(w >> 32);
-    reinterpret_cast<uint16_t*>(v_scale)[row] = __half_as_ushort(__float2half_rn(s));
+    for (int i = 0; i < BLK; ++i) c[i] = (int)q_grid_div(x[i], s, r, FMT_INT3);
+    sbits = __half_as_ushort(__float2half_rn(s));
 }
 
 // K blocks (per channel, 16-token pages): a CTA owns PPC pages x D channels
@@ -189,6 +184,29 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
     const int64_t nv = (int64_t)a.H * a.S_v * ND;
     const int nv_ctas = gridDim.x - nk_ctas;
     const int calib_v = ANY_MSE ? a.calib_v : (int)CAL_ABSMAX;
+    if constexpr (FMT == FMT_MIX43) {
+        // INT3 V: a thread takes a block pair (they share a sign word)
+        for (int64_t j = (int64_t)(blockIdx.x - nk_ctas) * 256 + tid; j < nv / 2; j += (int64_t)nv_ctas * 256) {
+            const int db = (int)(2 * j % ND);
+            const int64_t r = 2 * j / ND;
+            const int t = (int)(r % a.S_v), h = (int)(r / a.S_v);
+            float x[BLK];
+            int c0[BLK], c1[BLK];
+            uint16_t s0, s1;
+            load_contig16<T>(v + h * a.sv_h + t * a.sv_s + (int64_t)db * BLK * a.sv_d, a.sv_d, x);
+            quant_v3(x, calib_v, a.alphas, a.n_alphas, c0, s0);
+            load_contig16<T>(v + h * a.sv_h + t * a.sv_s + (int64_t)(db + 1) * BLK * a.sv_d, a.sv_d, x);
+            quant_v3(x, calib_v, a.alphas, a.n_alphas, c1, s1);
+            const int64_t row = ((int64_t)h * a.v_s_stride + a.vtok0 + t) * ND + db;
+            uint32_t A0, A1, S;
+            int3_pack_pair(c0, c1, A0, A1, S);
+            uint32_t* o = reinterpret_cast<uint32_t*>(a.v_packed + row * PACKB3);
+            o[0] = A0; o[1] = A1; o[2] = S;
+            reinterpret_cast<uint16_t*>(a.v_scale)[row] = s0;
+            reinterpret_cast<uint16_t*>(a.v_scale)[row + 1] = s1;
+        }
+        return;
+    }
     if (FMT != FMT_MIX43 && !ANY_MSE && sizeof(T) == 2 && a.sv_d == 1 && ND % 2 == 0 && (a.sv_s * 2) % 16 == 0 &&
         (a.sv_h * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0) {
         // absmax: a thread takes two neighbouring blocks of one token, 64
@@ -228,10 +246,6 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a, int ppc, int n_
         uint16_t sb;
         load_contig16<T>(v + h * a.sv_h + t * a.sv_s + (int64_t)db * BLK * a.sv_d, a.sv_d, x);
         const int64_t row = ((int64_t)h * a.v_s_stride + a.vtok0 + t) * ND + db;
-        if constexpr (FMT == FMT_MIX43) {
-            store_v3(x, calib_v, a.alphas, a.n_alphas, a.v_packed, a.v_scale, row);
-            continue;
-        }
         quant_pack<FMT>(x, calib_v, a.alphas, a.n_alphas, a.g_v, pk, sb);
         reinterpret_cast<uint2*>(a.v_packed)[row] = pk;
         if (FMT == FMT_NVFP4) reinterpret_cast<uint8_t*>(a.v_scale)[row] = (uint8_t)sb;
@@ -390,9 +404,10 @@ __global__ void __launch_bounds__(256) dequant_kernel(DequantArgs a) {
             const float s = load_scale<FMT>(a.v_scale, row, a.g_v);
             __nv_bfloat16* o = vo + h * a.so_h + t * a.so_s + (int64_t)db * BLK * a.so_d;
             if constexpr (FMT == FMT_MIX43) {
-                const uint8_t* blk = a.v_packed + row * PACKB3;
+                const uint8_t* trow = a.v_packed + ((int64_t)h * a.v_s_stride + t) * ND * PACKB3;
 #pragma unroll
-                for (int c = 0; c < BLK; ++c) o[c * a.so_d] = __float2bfloat16_rn(__fmul_rn((float)int3_code(blk, c), s));
+                for (int c = 0; c < BLK; ++c)
+                    o[c * a.so_d] = __float2bfloat16_rn(__fmul_rn((float)int3_code(trow, db * BLK + c), s));
                 continue;
             }
             const uint2 pk = reinterpret_cast<const uint2*>(a.v_packed)[row];
@@ -553,6 +568,7 @@ extern "C" int kivi_store(const void* k, const void* v, int in_dtype, int64_t sk
                           int v_s_stride, kivi_stream_t stream) {
     if (H < 0 || S_k < 0 || S_v < 0 || D <= 0 || D % BLK) return KIVI_ERR_ARG;
     if (fmt != FMT_INT4 && fmt != FMT_NVFP4 && fmt != FMT_MIX43) return KIVI_ERR_ARG;
+    if (fmt == FMT_MIX43 && D % 32) return KIVI_ERR_ARG;     // V blocks go in pairs
     if ((unsigned)calib_k > 1 || (unsigned)calib_v > 1) return KIVI_ERR_ARG;
     if ((calib_k == CAL_MSE || calib_v == CAL_MSE) && (!alphas || n_alphas <= 0)) return KIVI_ERR_ARG;
     if (in_dtype != KIVI_DT_BF16 && in_dtype != KIVI_DT_F16 && in_dtype != KIVI_DT_F32) return KIVI_ERR_ARG;
@@ -588,6 +604,7 @@ extern "C" int kivi_dequant(const uint8_t* k_packed, const void* k_scale, int k_
                             int64_t so_h, int64_t so_s, int64_t so_d, kivi_stream_t stream) {
     if (H < 0 || S < 0 || D <= 0 || D % BLK) return KIVI_ERR_ARG;
     if (fmt != FMT_INT4 && fmt != FMT_NVFP4 && fmt != FMT_MIX43) return KIVI_ERR_ARG;
+    if (fmt == FMT_MIX43 && D % 32) return KIVI_ERR_ARG;
     if (k_np_stride < S / BLK || v_s_stride < S) return KIVI_ERR_ARG;
     if ((uintptr_t)k_packed % 8 || (uintptr_t)v_packed % 8) return KIVI_ERR_ALIGN;
     const int64_t n = (int64_t)H * (S / BLK) * D + (int64_t)H * S * (D / BLK);

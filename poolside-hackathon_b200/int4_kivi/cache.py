@@ -69,13 +69,14 @@ class KIVICache:
 def alloc_packed(H: int, S: int, D: int, device, scale_dtype, s_cap: Optional[int] = None, v_pack: int = PACK):
     """Zeroed capacity buffers (k_packed, k_scale, v_packed, v_scale) for up to
     s_cap tokens; page and token strides are multiples of 16.  v_pack is the
-    bytes per packed V block (8; 6 for the INT3 V of the mixed cache)."""
+    last dim of v_packed: 8 bytes per V block, or 12 per block pair (the INT3
+    V of the mixed cache, [H, S, D/32, 12])."""
     s_cap = _round_up(max(s_cap or S, S, 1), ALIGN * BLOCK)
     np_cap = s_cap // BLOCK
     ND = D // BLOCK
     kp = torch.zeros((H, D, np_cap, PACK), dtype=torch.uint8, device=device)
     ks = torch.zeros((H, D, np_cap), dtype=scale_dtype, device=device)
-    vp = torch.zeros((H, s_cap, ND, v_pack), dtype=torch.uint8, device=device)
+    vp = torch.zeros((H, s_cap, ND if v_pack == PACK else ND // 2, v_pack), dtype=torch.uint8, device=device)
     vs = torch.zeros((H, s_cap, ND), dtype=scale_dtype, device=device)
     return kp, ks, vp, vs
 
@@ -86,7 +87,7 @@ def cache_geometry(c) -> tuple[int, int]:
     `c` is a cache object or a (k_packed, k_scale, v_packed, v_scale) tuple."""
     kp, ks, vp, vs = c if isinstance(c, tuple) else (c.k_packed, c.k_scale, c.v_packed, c.v_scale)
     np_stride = kp.stride(1) // PACK if kp.dim() == 4 else 0
-    VP = vp.shape[3] if vp.dim() == 4 else PACK           # bytes per V block
+    VP = vp.shape[3] if vp.dim() == 4 else PACK           # bytes per V block (pair)
     s_stride = vp.stride(0) // (vp.shape[2] * VP) if vp.dim() == 4 and vp.shape[2] else 0
     ok = (kp.dim() == 4 and kp.stride(3) == 1 and kp.stride(2) == PACK and kp.stride(1) == np_stride * PACK
           and kp.stride(0) == kp.shape[1] * np_stride * PACK
@@ -168,7 +169,7 @@ def full_views(c):
     ND = D // BLOCK
     kp = c.k_packed.as_strided((H, D, np_stride, PACK), c.k_packed.stride())
     ks = c.k_scale.as_strided((H, D, np_stride), c.k_scale.stride())
-    vp = c.v_packed.as_strided((H, s_stride, ND, c.v_packed.shape[3]), c.v_packed.stride())
+    vp = c.v_packed.as_strided((H, s_stride) + tuple(c.v_packed.shape[2:]), c.v_packed.stride())
     vs = c.v_scale.as_strided((H, s_stride, ND), c.v_scale.stride())
     return kp, ks, vp, vs
 

@@ -269,7 +269,7 @@ def stack_caches(caches: list) -> dict:
     d = dict(k_packed=kp[:, :, :NP], k_scale=ks[:, :, :NP],
              k_hot=torch.cat([c.k_hot for c in caches], dim=0),
              v_packed=vp[:, :S], v_scale=vs[:, :S],
-             H=H, S=S, D=D, NP=NP, ND=c0.v_packed.shape[2], B=B)
+             H=H, S=S, D=D, NP=NP, ND=D // BLOCK, B=B)
     if getattr(c0, "fmt", "int4") != "int4":
         d.update(fmt=c0.fmt, g_k=c0.g_k, g_v=c0.g_v)
     return d
@@ -297,7 +297,7 @@ def _stack_varlen(caches: list) -> dict:
         if c.k_hot.shape[1]:
             khot[b * H:(b + 1) * H, :c.k_hot.shape[1]].copy_(c.k_hot)
     d = dict(k_packed=kp[:, :, :NP], k_scale=ks[:, :, :NP], k_hot=khot, v_packed=vp[:, :S], v_scale=vs[:, :S],
-             H=H, S=S, D=D, NP=NP, ND=c0.v_packed.shape[2], B=B,
+             H=H, S=S, D=D, NP=NP, ND=D // BLOCK, B=B,
              seq_lens=torch.tensor([c.S for c in caches], dtype=torch.int32, device=dev))
     if getattr(c0, "fmt", "int4") != "int4":
         d.update(fmt=c0.fmt, g_k=c0.g_k, g_v=c0.g_v)

@@ -10,13 +10,20 @@ layout below is this library's own:
     K exactly as KIVICache (INT4 codes, fp16 scale per channel and 16-token
       page, the S % 16 tail kept bf16 in k_hot);
     V codes against the fp32 block scale, the scale stored as fp16 (as every
-      KIVI scale); a 16-channel block is 16 three-bit two's-complement codes,
-      element i in bits [3i, 3i + 3) of a little-endian 48-bit word:
-        v_packed u8 [H, S, D/16, 6],  v_scale f16 [H, S, D/16].
+      KIVI scale); a code c in [-3, 3] is kept as its low two bits L = c & 3
+      and a sign bit s (c = L - 4s), blocks in pairs (2k, 2k + 1) of 12 bytes,
+      three little-endian 32-bit words A_2k, A_2k+1, S_k:
+        A_b: L of element i < 8 at bits 4i..4i+1, of element 8+i at 4i+2..4i+3;
+        S_k: s of element i < 8 of block 2k+o at bit 4i+2o, of 8+i at 4i+1+2o;
+        v_packed u8 [H, S, D/32, 12],  v_scale f16 [H, S, D/16]
+      (D a multiple of 32).  `(A & 0x33333333) | (S-bits on bit 2)` is the
+      block's INT4-style nibble word, so the decode kernel turns a staged tile
+      into nibbles with a few logic operations per block.
 
 Per token and kv-head the cache holds 64 + 16 + 48 + 16 = 144 bytes (160 for
-INT4 KIVI, 512 for bf16).  The fused decode runs on the CUDA-core path of
-libkivi_sm100 (the tensor-core path takes INT4 and NVFP4 pages only).
+INT4 KIVI, 512 for bf16).  The fused decode is libkivi_sm100's tensor-core
+decode kernel: each warp turns its TMA-staged INT3 rows into 3-bit nibbles in
+shared memory, then runs the INT4 PV path on them.
 """
 from __future__ import annotations
 
@@ -28,13 +35,13 @@ from torch import Tensor
 
 from .cache import BLOCK, KIVICache, alloc_packed, dequant_packed, store_into
 
-PACK3 = 6           # bytes per packed INT3 V block
+PACK3 = 12          # bytes per packed pair of INT3 V blocks
 QMAX3 = 3
 
 
 @dataclasses.dataclass
 class Int3VKIVICache(KIVICache):
-    """KIVICache with INT3 V blocks (v_packed [H, S, D/16, 6])."""
+    """KIVICache with INT3 V blocks (v_packed [H, S, D/32, 12])."""
     g_k: float = 1.0
     g_v: float = 1.0
 
@@ -49,7 +56,7 @@ def store_kivi_int3v(k: Tensor, v: Tensor, k_calib: str = "mse", v_calib: str = 
     assert k.shape == v.shape, "k and v must share shape [H, S, D]"
     assert k.is_cuda and v.is_cuda, "inputs must be on CUDA"
     H, S, D = k.shape
-    assert D % BLOCK == 0, "head_dim must be a multiple of 16"
+    assert D % (2 * BLOCK) == 0, "head_dim must be a multiple of 32 (INT3 V blocks go in pairs)"
     k = k.to(torch.bfloat16)
     v = v.to(torch.bfloat16)
     n_full = (S // BLOCK) * BLOCK

@@ -18,7 +18,7 @@ D = 128
 
 def _same_cache(c, o):
     H, S = c.H, c.S
-    assert c.v_packed.shape == (H, S, c.D // 16, 6)
+    assert c.v_packed.shape == (H, S, c.D // 32, 12)
     assert np.array_equal(c.k_packed.cpu().numpy(), o["k_packed"])
     assert np.array_equal(c.k_scale.cpu().numpy().view(np.uint16), o["k_scale"].view(np.uint16))
     assert np.array_equal(c.v_packed.cpu().numpy(), o["v_packed"])

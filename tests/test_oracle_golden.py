@@ -275,7 +275,7 @@ def test_int3v_store_pinned_to_roundtrip(calib):
     k, v = bf16_from_bits(g["k"]), bf16_from_bits(g["v"])
     H, S, D = v.shape
     c = oracle.store_int3v(k, v, calib, calib)
-    assert c["v_packed"].shape == (H, S, D // 16, 6)
+    assert c["v_packed"].shape == (H, S, D // 32, 12)
     codes = oracle.unpack_int3(c["v_packed"]).astype(np.float32)
     assert codes.min() >= -3 and codes.max() <= 3
     s32 = oracle.calibrate(v.float().numpy().reshape(-1, 16), "int3", calib).reshape(H, S, D // 16, 1)
