@@ -39,7 +39,18 @@ enum kivi_status {
     KIVI_ERR_SCRATCH = 6       /* problem exceeds the fixed no-alloc scratch */
 };
 
-enum kivi_fmt { KIVI_FMT_INT4 = 0, KIVI_FMT_INT3 = 1, KIVI_FMT_NVFP4 = 2 };
+/* KIVI_FMT_INT3 is a kivi_roundtrip / kivi_calibrate grid only.  A cache of
+ * KIVI_FMT_MIX43 keeps K as INT4 (the INT4 K layout) and V as INT3 on the
+ * kv_quant.py:215-217 `int3` grid (qmax 3, fp16 scales), the 3-bit-V / 4-bit-K
+ * cache WRITEUP.md:336-339 names (the reference ships no packed INT3 format;
+ * this layout is the library's own).  V blocks go in pairs: v_packed rows are
+ * [D/32][12] bytes, little-endian u32 words A_2k, A_2k+1, S_k; a code c in
+ * [-3, 3] is L = c & 3 plus sign s (c = L - 4s); A_b holds L of element
+ * i < 8 at bits 4i..4i+1 and of element 8+i at 4i+2..4i+3; S_k holds s of
+ * element i < 8 of block 2k+o at bit 4i+2o and of element 8+i at 4i+1+2o.
+ * D must be a multiple of 32.  Every store, dequant and decode entry point
+ * takes it (the paged entry points do not). */
+enum kivi_fmt { KIVI_FMT_INT4 = 0, KIVI_FMT_INT3 = 1, KIVI_FMT_NVFP4 = 2, KIVI_FMT_MIX43 = 3 };
 enum kivi_calib { KIVI_CALIB_ABSMAX = 0, KIVI_CALIB_MSE = 1 };
 enum kivi_layout { KIVI_LAYOUT_HEADDIM = 0, KIVI_LAYOUT_CHANNEL = 1 };
 enum kivi_dtype { KIVI_DT_BF16 = 0, KIVI_DT_F16 = 1, KIVI_DT_F32 = 2 };
@@ -63,6 +74,7 @@ int kivi_last_cuda_error(void);         /* cudaError_t of the last KIVI_ERR_CUDA
 /*    (head stride v_s_stride tokens) and v_scale[h, vtok0 + t, db].          */
 /* fmt INT4: scale = fp16 (2 bytes), codes two's-complement nibbles.         */
 /* fmt NVFP4: scale = e4m3 byte of (s / g), codes e2m1 nibbles (g_k, g_v).   */
+/* fmt MIX43: K as INT4; V INT3, 12 bytes per block pair per token (above). */
 /* alphas: device fp32 [n_alphas], the MSE clip grid linspace(0.5, 1, n).    */
 /* D must be a multiple of 16.                                               */
 /* ------------------------------------------------------------------------ */
@@ -127,7 +139,8 @@ int kivi_page_dequant(const uint8_t *packed, const void *scale, int rows, int to
 /*           k_packed [BH, D, k_np_stride, 8], k_scale [BH, D, k_np_stride]  */
 /*           k_hot bf16 [BH, hot_stride, D] (tokens n_full..S-1)             */
 /*           v_packed [BH, v_s_stride, D/16, 8], v_scale [BH, v_s_stride, D/16]*/
-/*           fmt INT4: fp16 scales; NVFP4: e4m3 scales with g_k, g_v.        */
+/*           fmt INT4: fp16 scales; NVFP4: e4m3 scales with g_k, g_v;        */
+/*           MIX43: v_packed [BH, v_s_stride, D/32, 12] (INT3 V, above).     */
 /* S       : tokens attended (n_full = (S/16)*16 from pages, rest from k_hot)*/
 /* out     : bf16 [B, Hq, D] contiguous.                                     */
 /* work    : fp32 scratch of kivi_decode_workspace_floats(...) floats      */

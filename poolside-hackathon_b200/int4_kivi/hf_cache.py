@@ -37,6 +37,7 @@ from torch import Tensor
 from transformers.cache_utils import Cache, CacheLayerMixin
 
 from .cache import BLOCK, KIVICache, alloc_packed, append_kivi, dequant_kivi, store_kivi
+from .mixed import store_kivi_int3v
 
 ATTN_IMPL = "int4_kivi"
 # Steps of up to this many new tokens (a decode step, or a speculative verify
@@ -46,9 +47,11 @@ FUSED_MAX_Q = 8
 
 class _Int4KiviLayer(CacheLayerMixin):
     def __init__(self, k_calib: str = "mse", v_calib: str = "mse", is_sliding: bool = False,
-                 sliding_window: int | None = None, fused_decode: bool = False):
+                 sliding_window: int | None = None, fused_decode: bool = False, v_bits: int = 4):
         super().__init__()
-        self.k_calib, self.v_calib = k_calib, v_calib
+        if v_bits not in (3, 4):
+            raise ValueError(f"v_bits must be 4 (INT4 KIVI) or 3 (INT4 K / INT3 V), not {v_bits}")
+        self.k_calib, self.v_calib, self.v_bits = k_calib, v_calib, v_bits
         self.is_sliding, self.sliding_window = is_sliding, sliding_window
         self.fused = fused_decode and not is_sliding
         self.store: KIVICache | None = None     # frozen pages (S multiple of 16)
@@ -95,8 +98,9 @@ class _Int4KiviLayer(CacheLayerMixin):
             return
         kp, vp = self.hot_k[:, :n_full], self.hot_v[:, :n_full]
         if self.store is None:
-            self.store = store_kivi(kp.contiguous(), vp.contiguous(), self.k_calib, self.v_calib,
-                                    capacity=max(4 * n_full, 1024))
+            store = store_kivi if self.v_bits == 4 else store_kivi_int3v
+            self.store = store(kp.contiguous(), vp.contiguous(), self.k_calib, self.v_calib,
+                               capacity=max(4 * n_full, 1024))
         else:
             append_kivi(self.store, kp, vp, self.k_calib, self.v_calib)
         self.hot_k = self.hot_k[:, n_full:].contiguous()
@@ -119,14 +123,15 @@ class _Int4KiviLayer(CacheLayerMixin):
         pages do not accumulate over a long sliding-window generation."""
         c, off = self.store, self._offset
         S1 = c.S - off
-        kp, ks, vp, vs = alloc_packed(c.H, S1, c.D, c.k_packed.device, c.k_scale.dtype, s_cap=max(4 * S1, 1024))
+        kp, ks, vp, vs = alloc_packed(c.H, S1, c.D, c.k_packed.device, c.k_scale.dtype, s_cap=max(4 * S1, 1024),
+                                      v_pack=c.v_packed.shape[3])
         NP1 = S1 // BLOCK
         kp[:, :, :NP1].copy_(c.k_packed[:, :, off // BLOCK:])
         ks[:, :, :NP1].copy_(c.k_scale[:, :, off // BLOCK:])
         vp[:, :S1].copy_(c.v_packed[:, off:])
         vs[:, :S1].copy_(c.v_scale[:, off:])
-        self.store = KIVICache(k_packed=kp[:, :, :NP1], k_scale=ks[:, :, :NP1], k_hot=c.k_hot,
-                               v_packed=vp[:, :S1], v_scale=vs[:, :S1], H=c.H, S=S1, D=c.D)
+        self.store = type(c)(k_packed=kp[:, :, :NP1], k_scale=ks[:, :, :NP1], k_hot=c.k_hot,
+                             v_packed=vp[:, :S1], v_scale=vs[:, :S1], H=c.H, S=S1, D=c.D)
         self._offset = 0
         self._deq_k = self._deq_v = None
         self._deq_len = 0
@@ -208,7 +213,7 @@ class _Int4KiviLayer(CacheLayerMixin):
                   v_packed=c.v_packed if frozen else None, v_scale=c.v_scale if frozen else None,
                   k_hot=self.hot_k if t else torch.empty((self._B * self._H, 0, D), dtype=torch.bfloat16,
                                                          device=query.device),
-                  H=self._H, S=frozen + t, D=D, B=self._B)
+                  H=self._H, S=frozen + t, D=D, B=self._B, fmt="int4" if self.v_bits == 4 else "int4k_int3v")
         if query.shape[2] > 1:
             return kivi_decode_attention_multiquery(query.transpose(1, 2).to(torch.bfloat16), st, Hq,
                                                     sm_scale=scaling, v_hot=self.hot_v if t else None)
@@ -230,7 +235,7 @@ class _Int4KiviLayer(CacheLayerMixin):
         return 2 * (self._stored_len() * heads * getattr(self, "_D", 0)) * 2
 
     def reset(self) -> None:
-        self.__init__(self.k_calib, self.v_calib, self.is_sliding, self.sliding_window, self.fused)
+        self.__init__(self.k_calib, self.v_calib, self.is_sliding, self.sliding_window, self.fused, self.v_bits)
 
     def reorder_cache(self, beam_idx) -> None:
         if getattr(self, "_B", 1) > 1:
@@ -251,9 +256,13 @@ class Int4KiviCache(Cache):
 
         cache = Int4KiviCache(config=model.config)
         model.generate(..., past_key_values=cache)
+
+    v_bits=3 keeps V in INT3 (the mixed cache of int4_kivi.mixed: 144 bytes
+    per token and kv-head instead of 160).
     """
 
-    def __init__(self, config, k_calib: str = "mse", v_calib: str = "mse", fused_decode: bool = False):
+    def __init__(self, config, k_calib: str = "mse", v_calib: str = "mse", fused_decode: bool = False,
+                 v_bits: int = 4):
         decoder = config.get_text_config(decoder=True)
         sliding_window = getattr(decoder, "sliding_window", None) or getattr(decoder, "attention_chunk_size", None)
         layer_types = getattr(decoder, "layer_types", None)
@@ -262,7 +271,7 @@ class Int4KiviCache(Cache):
             layer_types = [kind] * decoder.num_hidden_layers
         layers = [_Int4KiviLayer(k_calib=k_calib, v_calib=v_calib, is_sliding=(lt == "sliding_attention"),
                                  sliding_window=sliding_window if lt == "sliding_attention" else None,
-                                 fused_decode=fused_decode)
+                                 fused_decode=fused_decode, v_bits=v_bits)
                   for lt in layer_types]
         super().__init__(layers=layers)
 

@@ -97,7 +97,7 @@ def _exact_kv(layer):
         d = dict(k_packed=c.k_packed.cpu().numpy(), k_scale=c.k_scale.cpu().numpy(),
                  v_packed=c.v_packed.cpu().numpy(), v_scale=c.v_scale.cpu().numpy(),
                  k_hot=c.k_hot.float().cpu().numpy(), H=c.H, S=c.S, D=c.D)
-        k, v = oracle.dequant_int4(d)
+        k, v = oracle.dequant_int4(d) if c.fmt == "int4" else oracle.dequant_int3v(d)
         ks.append(torch.from_numpy(k)); vs.append(torch.from_numpy(v))
     if layer._hot_len():
         ks.append(layer.hot_k.float().cpu()); vs.append(layer.hot_v.float().cpu())
@@ -276,3 +276,70 @@ def test_batched_generate_tiny_random_model(cuda_dev):
     out_d = model.generate(x, attention_mask=pad, max_new_tokens=12, do_sample=False,
                            past_key_values=Int4KiviCache(config=cfg))
     assert out_f.shape == (2, 52) and torch.equal(out_f, out_d)
+
+
+def test_int3v_layer_update_and_fused_decode(cuda_dev):
+    """v_bits=3 (K INT4, V INT3): `update` returns store_kivi_int3v +
+    dequant of the completed pages and the bf16 partial page; the fused read
+    path (single and multi-token steps) meets the decode bar against fp32
+    attention over the exactly dequantised tokens."""
+    from conftest import check_decode_bf16
+    from int4_kivi.hf_cache import _Int4KiviLayer
+    from int4_kivi.mixed import dequant_kivi_int3v, store_kivi_int3v
+    H, Hq, D = 2, 8, 128
+    k, v, _ = gen_kv(H, 200, D, seed=41)
+    kd, vd = k.to(cuda_dev), v.to(cuda_dev)
+    g = torch.Generator().manual_seed(42)
+    plain, fused = _Int4KiviLayer(v_bits=3), _Int4KiviLayer(fused_decode=True, v_bits=3)
+    pos = 0
+    for n in (37, 1, 1, 3, 14, 8, 1, 60, 5, 1):
+        kk, vv = plain.update(kd[None, :, pos:pos + n], vd[None, :, pos:pos + n])
+        stub, _ = fused.update(kd[None, :, pos:pos + n], vd[None, :, pos:pos + n])
+        pos += n
+        nf = (pos // 16) * 16
+        rk, rv = dequant_kivi_int3v(store_kivi_int3v(kd[:, :nf], vd[:, :nf])) if nf else (kd[:, :0], vd[:, :0])
+        assert torch.equal(kk[0], torch.cat([rk, kd[:, nf:pos]], 1))
+        assert torch.equal(vv[0], torch.cat([rv, vd[:, nf:pos]], 1))
+        if n > 8:
+            continue
+        q = torch.randn(1, Hq, n, D, generator=g).bfloat16().to(cuda_dev)
+        out = fused.fused_decode(q, D ** -0.5)
+        out = (out[0] if n > 1 else out).float().cpu().reshape(n, Hq, D)
+        ek, ev = _exact_kv(fused)
+        ref = torch.stack([_ref_attention(q[0, :, j].cpu(), ek[:, :pos - n + j + 1], ev[:, :pos - n + j + 1],
+                                          D ** -0.5) for j in range(n)])
+        check_decode_bf16(out, ref, f"int3v pos={pos} n={n}")
+    assert fused.store.fmt == "int4k_int3v" and fused.store.v_packed.shape[2:] == (D // 32, 12)
+
+
+def test_int3v_generate_tiny_random_model(cuda_dev):
+    """Int4KiviCache(v_bits=3): fused decode logits track the same cache's
+    dequantise + SDPA path, greedy generate runs, and the cache is smaller
+    than the INT4 one for the same tokens."""
+    transformers = pytest.importorskip("transformers")
+    from int4_kivi.hf_cache import Int4KiviCache, enable_fused_decode
+    cfg = transformers.LlamaConfig(vocab_size=128, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                                   num_attention_heads=8, num_key_value_heads=2, head_dim=128,
+                                   max_position_embeddings=512)
+    torch.manual_seed(0)
+    model = transformers.LlamaForCausalLM(cfg).to(cuda_dev, torch.bfloat16).eval()
+    ids = torch.randint(0, 128, (1, 80), device=cuda_dev)
+    with torch.no_grad():
+        c_ref, c4 = Int4KiviCache(config=cfg, v_bits=3), Int4KiviCache(config=cfg)
+        model(ids[:, :40], past_key_values=c4)
+        ref = [model(ids[:, :40], past_key_values=c_ref).logits[:, -1]]
+        for t in range(40, 80):
+            ref.append(model(ids[:, t:t + 1], past_key_values=c_ref).logits[:, -1])
+            model(ids[:, t:t + 1], past_key_values=c4)
+        enable_fused_decode(model)
+        c_f = Int4KiviCache(config=cfg, fused_decode=True, v_bits=3)
+        got = [model(ids[:, :40], past_key_values=c_f).logits[:, -1]]
+        for t in range(40, 80):
+            got.append(model(ids[:, t:t + 1], past_key_values=c_f).logits[:, -1])
+        out = model.generate(ids[:, :40], max_new_tokens=16, do_sample=False,
+                             past_key_values=Int4KiviCache(config=cfg, fused_decode=True, v_bits=3))
+        model.set_attn_implementation("sdpa")
+    r, g_ = torch.stack(ref).float(), torch.stack(got).float()
+    assert (r - g_).abs().max().item() <= 0.02 * r.abs().max().item()
+    assert out.shape == (1, 56)
+    assert c_ref.nbytes() < c4.nbytes()
