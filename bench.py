@@ -418,6 +418,36 @@ for S in (8192, 65536):
     res[f"S{S}"] = {"ms_per_step": round(ms, 4), "GB/s": round(by / ms / 1e6, 1), "decode_tok_s": round(8e3 / ms, 1)}
     del st
     torch.cuda.empty_cache()
+# the reference's bf16 GQA split-K decode (scripts/speedup_int4_kivi.py:47-108,
+# its int4-vs-bf16 comparator) at the headline shapes: its module constants set
+# to this config's 32 q heads / 8 kv heads (group 4) before the call
+sp = os.path.join(ref, 'ref_scripts', 'speedup_int4_kivi.py')
+if os.path.exists(sp):
+    import importlib.util
+    spec = importlib.util.spec_from_file_location('ref_speedup', sp)
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    m.N_QH, m.GROUP = 32, 4
+    S = 65536
+    g = torch.Generator(device=dev).manual_seed(8)
+    k = torch.randn(64, S, 128, device=dev, generator=g).bfloat16()
+    v = torch.randn(64, S, 128, device=dev, generator=g).bfloat16()
+    q = torch.randn(8, 32, 128, device=dev, generator=g).bfloat16()
+    sm = 1.0 / math.sqrt(128)
+    for _ in range(5):
+        m.bf16_decode_gqa(q, k, v, sm)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        m.bf16_decode_gqa(q, k, v, sm)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 20
+    by = 64 * S * 128 * 2 * 2
+    res["bf16_gqa_S65536"] = {"ms_per_step": round(ms, 4), "GB/s": round(by / ms / 1e6, 1),
+                              "decode_tok_s": round(8e3 / ms, 1),
+                              "kernel": "reference Triton bf16 GQA split-K (scripts/speedup_int4_kivi.py)"}
 print(json.dumps(res))
 """
 
@@ -436,7 +466,8 @@ def reference_gpu_comparator(local: int) -> dict:
         if r.returncode != 0:
             return {"unavailable": (r.stderr.strip().splitlines() or ["failed"])[-1][:300]}
         out = json.loads(r.stdout.strip().splitlines()[-1])
-        out["kernel"] = "reference Triton kivi_decode_attention_gqa (split=16, block_n=64), eager"
+        out["kernel"] = "reference Triton kivi_decode_attention_gqa (split=16, block_n=64), eager; "\
+                        "bf16_gqa: the reference's bf16 comparator kernel"
         return out
     except Exception as e:  # noqa: BLE001 -- reported, never fatal to the bench line
         return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
@@ -1046,7 +1077,9 @@ def main():
             extra = extra_configs(dev, peak, ms if S == 65536 else None)
             extra.update(store_configs(dev, peak))
             extra.update(multiquery_configs(dev, peak))
-            extra["reference_triton_gpu"] = reference_gpu_comparator(local)
+            extra["reference_triton_gpu"] = rg = reference_gpu_comparator(local)
+            if S == 65536 and "bf16_gqa_S65536" in rg:
+                rg["bf16_gqa_S65536"]["int4_speedup"] = round(rg["bf16_gqa_S65536"]["ms_per_step"] / ms, 3)
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
