@@ -922,39 +922,55 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         __threadfence_system();
         st_release_sys_u32(reinterpret_cast<unsigned int*>(p.peers[threadIdx.x]) + (int64_t)p.xrank * rows + row, e);
     }
+    // One thread per rank (W <= 16): wait, bounded, for rank j's epoch of this
+    // row (its flag sits in this rank's own buffer), then load that rank's
+    // (m, l) over NVLink -- all ranks' loads in flight at once.
     __shared__ int x_ok;
-    __shared__ float x_w[16];
-    __shared__ float x_l;
-    if (threadIdx.x == 0) {
-        const unsigned int* flags = reinterpret_cast<const unsigned int*>(p.xbuf);
-        int ok = 1;
+    __shared__ float x_m[16], x_lr[16];
+    if (threadIdx.x == 0) x_ok = 1;
+    __syncthreads();
+    const int W = p.xW;
+    if (threadIdx.x < W) {
+        const int j = threadIdx.x;
+        const unsigned int* flag = reinterpret_cast<const unsigned int*>(p.xbuf) + (int64_t)j * rows + row;
         const uint64_t t0 = globaltimer_ns();
-        for (int j = 0; j < p.xW && ok; ++j)
-            while ((int)(ld_acquire_sys_u32(flags + (int64_t)j * rows + row) - e) < 0)
-                if ((long long)(globaltimer_ns() - t0) > p.timeout_ns) { ok = 0; set_err(p.err, KIVI_ERR_TIMEOUT); break; }
-        x_ok = ok;
+        bool ok = true;
+        while ((int)(ld_acquire_sys_u32(flag) - e) < 0)
+            if ((long long)(globaltimer_ns() - t0) > p.timeout_ns) { ok = false; break; }
         if (ok) {
-            float Mx = -INFINITY;
-            for (int j = 0; j < p.xW; ++j)
-                Mx = fmaxf(Mx, __ldcg(xslot(reinterpret_cast<uint8_t*>(p.peers[j]), p.xW, rows, D, e) + row));
-            const float Mxr = (Mx == -INFINITY) ? 0.f : Mx;
-            float Lx = 0.f;
-            for (int j = 0; j < p.xW; ++j) {
-                const float* sj = xslot(reinterpret_cast<uint8_t*>(p.peers[j]), p.xW, rows, D, e);
-                x_w[j] = exp2f(__ldcg(sj + row) - Mxr);
-                Lx += __ldcg(sj + rows + row) * x_w[j];
-            }
-            x_l = Lx;
-            p.row_epoch[row] = e;
+            const float* sj = xslot(reinterpret_cast<uint8_t*>(p.peers[j]), W, rows, D, e);
+            x_m[j] = __ldcg(sj + row);
+            x_lr[j] = __ldcg(sj + rows + row);
+        } else {
+            atomicAnd(&x_ok, 0);
+            set_err(p.err, KIVI_ERR_TIMEOUT);
         }
     }
-    __syncthreads();                                     // peers' rows acquired by thread 0
+    __syncthreads();                                     // every rank's row acquired (or a timeout)
     if (!x_ok) return;
+    float Mx = -INFINITY;
+    for (int j = 0; j < W; ++j) Mx = fmaxf(Mx, x_m[j]);
+    const float Mxr = (Mx == -INFINITY) ? 0.f : Mx;
+    float xw[16];
+    float Lx = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        xw[j] = j < W ? exp2f(x_m[j] - Mxr) : 0.f;
+        if (j < W) Lx += x_lr[j] * xw[j];
+    }
+    if (threadIdx.x == 0) p.row_epoch[row] = e;
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)                     // all ranks' loads issued before any is used
+            v[j] = j < W ? __ldcg(xslot(reinterpret_cast<uint8_t*>(p.peers[j]), W, rows, D, e) + 2 * rows +
+                                  row * D + d)
+                         : 0.f;
         float a = 0.f;
-        for (int j = 0; j < p.xW; ++j)
-            a += __ldcg(xslot(reinterpret_cast<uint8_t*>(p.peers[j]), p.xW, rows, D, e) + 2 * rows + row * D + d) * x_w[j];
-        out[row * D + d] = __float2bfloat16_rn(x_l > 0.f ? a / x_l : 0.f);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (j < W) a += v[j] * xw[j];
+        out[row * D + d] = __float2bfloat16_rn(Lx > 0.f ? a / Lx : 0.f);
     }
 }
 
