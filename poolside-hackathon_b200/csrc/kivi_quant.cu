@@ -104,8 +104,23 @@ __device__ __forceinline__ void quant_v3(const float x[BLK], int calib, const fl
                                          int c[BLK], uint16_t& sbits) {
     const float s = calibrate16(x, FMT_INT3, calib, alphas, n_alphas);
     const float r = __frcp_rn(s);
+    if (calib == CAL_ABSMAX) {
+        // s = absmax / 3: |x / s| <= 3 (1 + 2^-23), so rint stays in [-3, 3]
+        // without a clamp; rounding by the 1.5 * 2^23 magic number (ties to
+        // even, like rint) leaves the code two's complement in the low
+        // mantissa bits (the same near-half fallback as the INT4 store)
+        constexpr float MAGIC = 12582912.0f;
 #pragma unroll
-    for (int i = 0; i < BLK; ++i) c[i] = (int)q_grid_div(x[i], s, r, FMT_INT3);
+        for (int i = 0; i < BLK; ++i) {
+            const float y = __fmul_rn(x[i], r);
+            float t = __fadd_rn(y, MAGIC);
+            if (fabsf(__fsub_rn(y, __fsub_rn(t, MAGIC))) > 0.5f - 1e-5f) t = __fadd_rn(__fdiv_rn(x[i], s), MAGIC);
+            c[i] = (int)(__float_as_uint(t) << 29) >> 29;        // sign-extend the low 3 bits
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < BLK; ++i) c[i] = (int)q_grid_div(x[i], s, r, FMT_INT3);
+    }
     sbits = __half_as_ushort(__float2half_rn(s));
 }
 
