@@ -759,9 +759,11 @@ __device__ __forceinline__ float tail_v(const DecodeParams& p, int bh, int n_ful
     return gen_v<FMT>(p, ((int64_t)bh * p.v_s_stride + t) * ND + d / BLK, d);
 }
 
-template <int FMT>
-__global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int mode, __nv_bfloat16* out,
-                                                      float* m_out, float* l_out, float* acc_out) {
+// NWC warps per row: 4, or 16 when heads spread over many CTAs (long rows of
+// partial slots, e.g. batch 1), so more slot loads are in flight per row.
+template <int FMT, int NWC>
+__global__ void __launch_bounds__(NWC * 32, 1) combine_kernel(const DecodeParams p, int mode, __nv_bfloat16* out,
+                                                              float* m_out, float* l_out, float* acc_out) {
     extern __shared__ float csm[];
     const int bh = blockIdx.x, h = blockIdx.y, b = bh / p.Hkv, kvh = bh % p.Hkv;
     const int G = p.G, D = p.D, ND = D / BLK;
@@ -779,7 +781,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     const int ns = (c_hi - c_lo + 1) * NWARP_C;          // partial slots of this head
     const int wcap = ns + ((16 + p.Tq - 1 + 3) & ~3);   // slots, then up to 15 + Tq - 1 tail tokens
     float* w = csm;                                      // [wcap] weights (slots, then tail tokens)
-    float* red = csm + wcap;                             // [8] block reduction scratch
+    float* red = csm + wcap;                             // [2 NWC] block reduction scratch
     const float sc2 = p.sm_scale * 1.4426950408889634f;
     const __nv_bfloat16* qp = q_row(p, b, kvh, h);
     // K of tail token n_full + j at channel d: from the packed pages when it is
@@ -794,7 +796,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         return __bfloat162float(p.k_hot[((int64_t)bh * p.hot_stride + (p.mq ? t - p.nf_real : j)) * D + d]);
     };
     // tail scores (log2 units), one warp per token
-    for (int j = warp; j < hot; j += 4) {
+    for (int j = warp; j < hot; j += NWC) {
         float sdot = 0.f;
         for (int d = lane; d < D; d += 32) sdot += __bfloat162float(qp[d]) * k_tail(j, d);
 #pragma unroll
@@ -818,7 +820,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     // and (the long-sequence path) the first acc vectors of this warp's slots,
     // all issued before any of them is used.  Partials of another kernel are
     // read at L2.
-    float* wl = w + wcap + 8 + 4 * DH;                   // [ns] l of each slot
+    float* wl = w + wcap + 2 * NWC + NWC * DH;           // [ns] l of each slot
     for (int i = threadIdx.x; i < ns; i += blockDim.x) {
         const bool lv = live(i);
         w[i] = lv ? __ldcg(p.part_m + slot(i)) : -INFINITY;
@@ -830,7 +832,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     if (wide) {
 #pragma unroll
         for (int u = 0; u < PRE; ++u) {
-            const int i = warp + 4 * u;
+            const int i = warp + NWC * u;
             pre[u] = (i < ns && live(i)) ? __ldcg(reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane))
                                          : make_float4(0.f, 0.f, 0.f, 0.f);
         }
@@ -844,6 +846,8 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     if (lane == 0) red[warp] = M;
     __syncthreads();
     M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+#pragma unroll
+    for (int k = 4; k < NWC; ++k) M = fmaxf(M, red[k]);
     const float Mr = (M == -INFINITY) ? 0.f : M;
     __syncthreads();
     // weights and L
@@ -855,9 +859,11 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, o);
-    if (lane == 0) red[4 + warp] = Ls;
+    if (lane == 0) red[NWC + warp] = Ls;
     __syncthreads();
-    Ls = (red[4] + red[5]) + (red[6] + red[7]);
+    Ls = (red[NWC] + red[NWC + 1]) + (red[NWC + 2] + red[NWC + 3]);
+#pragma unroll
+    for (int k = 4; k < NWC; ++k) Ls += red[NWC + k];
     const int64_t row = out_row(p, b, kvh, h);           // == b * Hq + kvh * G + h unless multi-query
     const int rows = p.B * p.Hq;
     unsigned int e = 0;
@@ -867,23 +873,23 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
         xacc = xslot(p.xbuf, p.xW, rows, D, e) + 2 * rows + row * D;
     }
     if (wide) {
-        // many slots (long sequences): warp w takes slots w, w + 4, ...; each
-        // lane owns 4 channels (float4), then a shared-memory reduction
+        // many slots (long sequences): warp w takes slots w, w + NWC, ...;
+        // each lane owns 4 channels (float4), then a shared-memory reduction
         float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int u = 0; u < PRE; ++u) {
-            const int i = warp + 4 * u;
+            const int i = warp + NWC * u;
             const float wi = i < ns ? w[i] : 0.f;
             if (wi != 0.f) {
                 a4.x += pre[u].x * wi; a4.y += pre[u].y * wi; a4.z += pre[u].z * wi; a4.w += pre[u].w * wi;
             }
         }
-        for (int i0 = warp + 4 * PRE; i0 < ns; i0 += 16) {   // four loads in flight per iteration
+        for (int i0 = warp + NWC * PRE; i0 < ns; i0 += 4 * NWC) {   // four loads in flight per iteration
             float4 v4[4];
             float wi[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                const int i = i0 + 4 * u;
+                const int i = i0 + NWC * u;
                 wi[u] = i < ns ? w[i] : 0.f;
                 v4[u] = wi[u] != 0.f ? __ldcg(reinterpret_cast<const float4*>(p.part_acc + slot(i) * DH + 4 * lane))
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -893,15 +899,19 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p, int 
                 a4.x += v4[u].x * wi[u]; a4.y += v4[u].y * wi[u]; a4.z += v4[u].z * wi[u]; a4.w += v4[u].w * wi[u];
             }
         }
-        float* sacc = red + 8;                           // [4][128]
+        float* sacc = red + 2 * NWC;                     // [NWC][128]
         *reinterpret_cast<float4*>(sacc + warp * DH + 4 * lane) = a4;
         __syncthreads();
         const int d = threadIdx.x;
-        float a = (sacc[d] + sacc[DH + d]) + (sacc[2 * DH + d] + sacc[3 * DH + d]);
-        for (int j = 0; j < hot; ++j) a += w[ns + j] * tail_v<FMT>(p, bh, n_full, j, d, ND);
-        if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
-        else if (mode == 1) acc_out[row * D + d] = a;
-        else xacc[d] = a;
+        if (d < DH) {
+            float a = (sacc[d] + sacc[DH + d]) + (sacc[2 * DH + d] + sacc[3 * DH + d]);
+#pragma unroll
+            for (int k = 4; k < NWC; ++k) a += sacc[k * DH + d];
+            for (int j = 0; j < hot; ++j) a += w[ns + j] * tail_v<FMT>(p, bh, n_full, j, d, ND);
+            if (mode == 0) out[row * D + d] = __float2bfloat16_rn(a / Ls);
+            else if (mode == 1) acc_out[row * D + d] = a;
+            else xacc[d] = a;
+        }
     } else {
         for (int d = threadIdx.x; d < D; d += blockDim.x) {
             float a = 0.f;
@@ -1209,12 +1219,15 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
         const int64_t per = std::max<int64_t>(pl.W / pl.N, 1);
         max_ctas = seq_lens ? pl.N + 1 : (int)((pl.T + per - 1) / per) + 1;
     }
-    const size_t csm = ((size_t)2 * max_ctas * NWARP_C + ((16 + Tq - 1 + 3) & ~3) + 8 + 4 * DH) * sizeof(float);
+    // 16 warps per merge row when a head spans many CTAs (long slot rows)
+    const int nwc = pl.N >= 16LL * BH ? 16 : 4;
+    const size_t csm = ((size_t)2 * max_ctas * NWARP_C + ((16 + Tq - 1 + 3) & ~3) + 2 * nwc + nwc * DH) *
+                       sizeof(float);
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
     const dim3 cgrid(BH, G);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = cgrid;
-    cfg.blockDim = dim3(128);
+    cfg.blockDim = dim3(32 * nwc);
     cfg.dynamicSmemBytes = csm;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1222,11 +1235,11 @@ int decode_impl(int mode, const void* q, int64_t q_sb, int64_t q_sh, const uint8
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t le = (fmt == FMT_NVFP4)
-        ? cudaLaunchKernelEx(&cfg, combine_kernel<FMT_NVFP4>, p, mode, o, m_out, l_out, acc_out)
-        : (fmt == FMT_MIX43)
-        ? cudaLaunchKernelEx(&cfg, combine_kernel<FMT_MIX43>, p, mode, o, m_out, l_out, acc_out)
-        : cudaLaunchKernelEx(&cfg, combine_kernel<FMT_INT4>, p, mode, o, m_out, l_out, acc_out);
+    auto launch_c = [&](auto kern) { return cudaLaunchKernelEx(&cfg, kern, p, mode, o, m_out, l_out, acc_out); };
+    cudaError_t le;
+    if (fmt == FMT_NVFP4) le = nwc == 16 ? launch_c(combine_kernel<FMT_NVFP4, 16>) : launch_c(combine_kernel<FMT_NVFP4, 4>);
+    else if (fmt == FMT_MIX43) le = nwc == 16 ? launch_c(combine_kernel<FMT_MIX43, 16>) : launch_c(combine_kernel<FMT_MIX43, 4>);
+    else le = nwc == 16 ? launch_c(combine_kernel<FMT_INT4, 16>) : launch_c(combine_kernel<FMT_INT4, 4>);
     if (le != cudaSuccess) return record_cuda_error(le);
     return check_launch();
 }
