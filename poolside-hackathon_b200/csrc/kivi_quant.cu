@@ -539,9 +539,13 @@ static int grid_for(int64_t n) {
 using namespace kivi;
 
 namespace {
-// Up to this many blocks an MSE store runs one warp per block (the search
-// spread over lanes); above it one thread per block fills the GPU anyway.
-constexpr int64_t SMALL_MSE_BLOCKS = 148LL * 64;
+// Up to this many blocks an MSE store runs one warp per block, the 32 clip
+// ratios spread over the lanes and the 16 elements quantised in parallel: one
+// thread per block would keep fewer than 256 threads per SM busy, each running
+// the whole search alone (the 16-token step store of 64 heads, 16384 blocks:
+// NVFP4 154 -> 31 us, INT4 43 -> 16 us).  Absmax stores have one candidate,
+// which one lane would evaluate alone, so they stay one thread per block.
+constexpr int64_t SMALL_STORE_BLOCKS = 148LL * 256;
 
 template <typename T, int FMT>
 int launch_store(const StoreArgs& a, cudaStream_t st) {
@@ -558,7 +562,7 @@ int launch_store(const StoreArgs& a, cudaStream_t st) {
     if (nk_ctas64 + nv_ctas > 0x7fffffffLL) return KIVI_ERR_UNSUPPORTED;
     const int64_t nblocks = (int64_t)a.H * NP * a.D + nv;
     if constexpr (FMT != FMT_MIX43) {        // (the mixed cache's INT3 V blocks use the thread-per-block kernel)
-        if ((a.calib_k == CAL_MSE || a.calib_v == CAL_MSE) && nblocks <= SMALL_MSE_BLOCKS) {
+        if ((a.calib_k == CAL_MSE || a.calib_v == CAL_MSE) && nblocks <= SMALL_STORE_BLOCKS) {
             const int64_t ctas = (nblocks + 7) / 8;          // 8 warps, one block each
             store_warp_kernel<T, FMT><<<(int)ctas, 256, 0, st>>>(a);
             return check_launch();
