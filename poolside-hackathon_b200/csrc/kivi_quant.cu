@@ -314,7 +314,27 @@ __global__ void __launch_bounds__(256) store_warp_kernel(StoreArgs a) {
         // INT4 absmax takes amax / 7 as is; every other case searches (NVFP4
         // absmax too: its one candidate passes the same finite-error test)
         const int nA = calib == CAL_ABSMAX ? 1 : a.n_alphas;
-        for (int al = lane; al < nA && !(FMT != FMT_NVFP4 && calib == CAL_ABSMAX); al += 32) {
+        float xl = x[0];                                 // my element (lanes 0..15)
+#pragma unroll
+        for (int e = 1; e < BLK; ++e) xl = lane == e ? x[e] : xl;
+        if (FMT == FMT_NVFP4 && calib == CAL_ABSMAX) {
+            // one candidate: lanes 0..15 take one element's squared error each,
+            // then every lane sums the 16 in kv_quant's mean order
+            const uint32_t sc = f32_to_e4m3(__fdiv_rn(__fdiv_rn(amax, qmax), g));
+            const float s = __fmul_rn(e4m3_to_f32((uint8_t)sc), g);
+            float ei = 0.f;
+            if (lane < BLK) {
+                const float q = (s == 0.0f) ? 0.0f : q_grid_div(xl, s, __frcp_rn(s), FMT_NVFP4);
+                const float d = __fsub_rn(xl, __fmul_rn(q, s));
+                ei = __fmul_rn(d, d);
+            }
+            float ev[BLK];
+#pragma unroll
+            for (int e = 0; e < BLK; ++e) ev[e] = __shfl_sync(0xffffffffu, ei, e);
+            const float err = mean16(ev);
+            if (err < best) { best = err; bs = s; bi = 0; bsc = sc; }
+        }
+        for (int al = lane; al < nA && calib != CAL_ABSMAX; al += 32) {
             float s = calib == CAL_ABSMAX ? __fdiv_rn(amax, qmax) : __fdiv_rn(__fmul_rn(a.alphas[al], amax), qmax);
             uint32_t sc = 0;
             if (FMT == FMT_NVFP4) {
@@ -336,9 +356,6 @@ __global__ void __launch_bounds__(256) store_warp_kernel(StoreArgs a) {
         if (FMT != FMT_NVFP4 && calib == CAL_ABSMAX) bs = __fdiv_rn(amax, qmax);
         // lanes 0..15 quantise one element each; the nibbles are OR-reduced
         uint32_t nib = 0;
-        float xl = x[0];
-#pragma unroll
-        for (int e = 1; e < BLK; ++e) xl = lane == e ? x[e] : xl;
         if (lane < BLK) {
             if (FMT == FMT_NVFP4) {
                 if (bs != 0.0f) {
@@ -543,8 +560,9 @@ namespace {
 // ratios spread over the lanes and the 16 elements quantised in parallel: one
 // thread per block would keep fewer than 256 threads per SM busy, each running
 // the whole search alone (the 16-token step store of 64 heads, 16384 blocks:
-// NVFP4 154 -> 31 us, INT4 43 -> 16 us).  Absmax stores have one candidate,
-// which one lane would evaluate alone, so they stay one thread per block.
+// NVFP4 154 -> 31 us, INT4 43 -> 16 us).  NVFP4 absmax stores too: their one
+// candidate's error check (e4m3-rounded scale, non-finite error -> scale 0) is
+// spread over 16 lanes.  INT4 absmax has no check and stays thread-per-block.
 constexpr int64_t SMALL_STORE_BLOCKS = 148LL * 256;
 
 template <typename T, int FMT>
@@ -562,7 +580,7 @@ int launch_store(const StoreArgs& a, cudaStream_t st) {
     if (nk_ctas64 + nv_ctas > 0x7fffffffLL) return KIVI_ERR_UNSUPPORTED;
     const int64_t nblocks = (int64_t)a.H * NP * a.D + nv;
     if constexpr (FMT != FMT_MIX43) {        // (the mixed cache's INT3 V blocks use the thread-per-block kernel)
-        if ((a.calib_k == CAL_MSE || a.calib_v == CAL_MSE) && nblocks <= SMALL_STORE_BLOCKS) {
+        if ((a.calib_k == CAL_MSE || a.calib_v == CAL_MSE || FMT == FMT_NVFP4) && nblocks <= SMALL_STORE_BLOCKS) {
             const int64_t ctas = (nblocks + 7) / 8;          // 8 warps, one block each
             store_warp_kernel<T, FMT><<<(int)ctas, 256, 0, st>>>(a);
             return check_launch();
