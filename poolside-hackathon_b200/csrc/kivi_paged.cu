@@ -174,6 +174,10 @@ __global__ void __launch_bounds__(256) store_token_kernel(const StoreP p) {
     bool live = in && s >= 0;
     if (live && !slot_ok(p, s)) { if (a == 0) set_err_flag(p.err, KIVI_ERR_ARG); live = false; }
     if (live && !isv && k_deferred(p, i, s)) live = false;
+    // A warp's two half-warps are neighbouring blocks of one token and head
+    // (both V or both K, ND even): when neither stores anything (K that goes
+    // per channel, or padding slots) the warp leaves before the search.
+    if (!__any_sync(0xffffffffu, live)) return;
     // both half-warps of a warp reach the shuffles; a dead one computes on a valid block
     float x[BLK];
     const void* src = isv ? p.v : p.k;
@@ -193,11 +197,17 @@ __global__ void __launch_bounds__(256) store_token_kernel(const StoreP p) {
 }
 
 // Per-channel K of blocks completed by this call: one 512-thread CTA per 16
-// input tokens and head.  For each completing token the block's 16 x D values
-// are staged in shared memory first (rows this call brings from the input,
-// the others dequantised from their per-token form in the cache), then every
-// warp takes channel pairs: half-warp u owns channel 2cp+u, lane a evaluates
-// clip alpha_a, then lane e quantises token e.
+// input tokens, head and group of 32 channels (blockIdx.z).  For each
+// completing token the block's 16 x D values are staged in shared memory
+// first (rows this call brings from the input, the others dequantised from
+// their per-token form in the cache), then warps take channel pairs:
+// half-warp u owns channel 2cp+u, lane a evaluates clip alpha_a, then lane e
+// quantises token e.  A block whose 16 rows all come from this call's input
+// is split over the channel groups (CTA z stages and quantises its 32
+// channels).  A block that also needs rows from the cache is done whole by
+// the z = 0 CTA: the per-token scale bytes those rows are dequantised with
+// are the bytes the per-channel scales overwrite, and only one CTA can order
+// its reads before those writes.
 __global__ void __launch_bounds__(512) store_channel_kernel(const StoreP p) {
     extern __shared__ float xs[];                        // [16][D]
     const int h = blockIdx.y;
@@ -209,8 +219,17 @@ __global__ void __launch_bounds__(512) store_channel_kernel(const StoreP p) {
         const int64_t s = p.slots[i];                    // uniform over the CTA
         if (!slot_ok(p, s) || s % PG != PG - 1) continue;
         const int64_t s0 = s - (PG - 1);
-        for (int e = threadIdx.x; e < PG * D; e += blockDim.x) {
-            const int j = e / D, c = e % D;
+        bool all_in = true;                              // every row of the block from this call's input
+        for (int j = 0; j < PG; ++j) {
+            const int idx = i - (PG - 1) + j;
+            all_in = all_in && idx >= 0 && p.slots[idx] == s0 + j;
+        }
+        if (!all_in && blockIdx.z != 0) continue;
+        const int cp_lo = all_in ? blockIdx.z * nwarp : 0;
+        const int cp_hi = all_in ? min(cp_lo + nwarp, D / 2) : D / 2;   // this CTA's channel pairs
+        const int c_lo = 2 * cp_lo, nc = 2 * (cp_hi - cp_lo);
+        for (int e = threadIdx.x; e < PG * nc; e += blockDim.x) {
+            const int j = e / nc, c = c_lo + e % nc;
             const int idx = i - (PG - 1) + j;
             float val;
             if (idx >= 0 && p.slots[idx] == s0 + j) {
@@ -223,7 +242,7 @@ __global__ void __launch_bounds__(512) store_channel_kernel(const StoreP p) {
             xs[j * D + c] = val;
         }
         __syncthreads();                                  // all rows read before any is rewritten
-        for (int cp = warp; cp < D / 2; cp += nwarp) {
+        for (int cp = cp_lo + warp; cp < cp_hi; cp += nwarp) {
             const int c = 2 * cp + u;
             float x[BLK];
 #pragma unroll
@@ -1035,8 +1054,8 @@ extern "C" int kivi_paged_store(const void* k, const void* v, int in_dtype, int6
     store_token_kernel<<<(unsigned)((halves * 16 + 255) / 256), 256, 0, st>>>(p);
     int e = check_launch();
     if (e) return e;
-    store_channel_kernel<<<dim3((unsigned)((N + PG - 1) / PG), (unsigned)H), 512, (size_t)PG * D * sizeof(float),
-                           st>>>(p);
+    store_channel_kernel<<<dim3((unsigned)((N + PG - 1) / PG), (unsigned)H, (unsigned)((D / 2 + 15) / 16)), 512,
+                           (size_t)PG * D * sizeof(float), st>>>(p);
     return check_launch();
 }
 
