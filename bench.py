@@ -42,7 +42,7 @@ METRIC = "packed-KV HBM GB/s (INT4-KIVI fused decode, 64K ctx)"
 GPU_LAUNCHES_PER_STEP = 2           # split-K decode kernel + combine kernel
 REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode_fast_kernel launch
-# at the headline shape (65536 tokens, B=8): 701.72 MB + 3.94 MB from a
+# at the headline shape (65536 tokens, B=8): 701.71 MB + 4.44 MB from a
 # one-pass ncu capture of that launch (1.052 x the 671.1 MB algorithmic).
 TRAFFIC_PER_LAUNCH = 706.15e6
 # same for the paged decode kernel, a 16384-token capture scaled by tokens
