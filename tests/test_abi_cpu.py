@@ -152,3 +152,25 @@ def test_fused_attention_mask_check():
     c3 = c.clone()
     c3[1, 0, 0, 7] = True                               # a future key visible
     assert not _causal_over_all(c3, 3)
+
+
+def test_hf_cache_v_bits_and_mixed_layout_host_side():
+    """Host-side checks of the mixed INT4-K / INT3-V cache (no GPU): the HF
+    cache takes v_bits 4 or 3 only, the format id is the ABI's
+    KIVI_FMT_MIX43, and a capacity buffer for it holds 12 bytes per pair of
+    16-channel V blocks (144 bytes per token and kv head with its scales)."""
+    import pytest
+    import torch
+    from int4_kivi import _native as N
+    from int4_kivi.cache import alloc_packed, cache_geometry
+    from int4_kivi.hf_cache import _Int4KiviLayer
+    from int4_kivi.mixed import PACK3
+    assert _Int4KiviLayer(v_bits=3).v_bits == 3 and _Int4KiviLayer().v_bits == 4
+    with pytest.raises(ValueError):
+        _Int4KiviLayer(v_bits=2)
+    assert N.FMT["int4k_int3v"] == 3
+    kp, ks, vp, vs = alloc_packed(2, 40, 128, "cpu", torch.float16, v_pack=PACK3)
+    assert vp.shape[2:] == (4, 12) and vs.shape[2] == 8
+    per_token = (vp[0, 0].numel() + vs[0, 0].numel() * 2 + kp[0, :, 0].numel() / 16 + ks[0, :, 0].numel() * 2 / 16)
+    assert per_token == 48 + 16 + 64 + 16
+    assert cache_geometry((kp[:, :, :2], ks[:, :, :2], vp[:, :40], vs[:, :40])) == (kp.shape[2], vp.shape[1])
