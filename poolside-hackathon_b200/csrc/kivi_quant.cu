@@ -311,8 +311,9 @@ __global__ void __launch_bounds__(256) store_warp_kernel(StoreArgs a) {
         float best = __int_as_float(0x7f800000), bs = 0.0f;
         int bi = 0x7fffffff;
         uint32_t bsc = 0;
-        // INT4 absmax takes amax / 7 as is; every other case searches (NVFP4
-        // absmax too: its one candidate passes the same finite-error test)
+        // INT4 absmax takes amax / 7 as is; NVFP4 absmax checks its one
+        // candidate's error (finite, else scale 0) with 16 lanes; MSE searches
+        // the clip ratios, one per lane
         const int nA = calib == CAL_ABSMAX ? 1 : a.n_alphas;
         float xl = x[0];                                 // my element (lanes 0..15)
 #pragma unroll
